@@ -1,0 +1,124 @@
+"""CPU oracle for the Block-RVQ runtime linear: TEST INFRASTRUCTURE ONLY.
+
+This module restates, in numpy, the reference's dequantise-then-matmul path
+(``matmul_strategy="per_group"``) so that tests can check the CUDA kernels
+against it.  Nothing in the product imports it: only ``tests/``,
+``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py`` may.
+
+Algorithm followed, with the reference lines it restates:
+
+* ``PackedBlockRVQGroup.reconstruct_weight`` (reference
+  ``src/runtime.py:379-414``): an fp32 accumulator starts at +0.0; for each
+  stage in order, ``recon += float32(codebook[ids])`` (``:383-388``); the
+  plain encodings used here skip the optional corrections (``:389-412``); the
+  result is sliced to ``in_features`` columns, rounded to bf16 and multiplied
+  by the bf16-rounded fp16 row scale, the product being rounded to bf16 again
+  (``:413-414``).
+* ``PackedGroupedBlockRVQLinear.forward`` default branch (reference
+  ``src/runtime.py:1501-1507``): per row group ``F.linear(x, weight, bias)``
+  with bf16 operands and the groups concatenated along the output dimension.
+  The oracle accumulates that product exactly (float64 over exact bf16*bf16
+  products), which is the fp32-accumulate result up to accumulation order.
+
+Rounding helpers follow PyTorch's float -> bfloat16 conversion
+(round-to-nearest-even on the fp32 bit pattern, NaN -> 0x7FC0), which the
+reference uses through ``Tensor.to(torch.bfloat16)``.
+
+Parity of this restatement is pinned by ``tests/golden/`` fixtures produced by
+running the reference itself (``tests/golden/make_golden.py``).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+def f32_to_bf16_bits(a: np.ndarray) -> np.ndarray:
+    """Round float32 values to bf16 (RNE), returned as uint16 bit patterns."""
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    u = a.view(np.uint32).astype(np.uint64)
+    lsb = (u >> np.uint64(16)) & np.uint64(1)
+    r = ((u + np.uint64(0x7FFF) + lsb) >> np.uint64(16)).astype(np.uint16)
+    nan = np.isnan(a)
+    if nan.any():
+        r[nan] = np.uint16(0x7FC0)
+    return r
+
+
+def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    b = np.ascontiguousarray(b, dtype=np.uint16)
+    return (b.astype(np.uint32) << np.uint32(16)).view(np.float32)
+
+
+def stage_sum_f32(stage_ids: list[np.ndarray], codebooks: list[np.ndarray]) -> np.ndarray:
+    """fp32 sum of the gathered stage entries, ``[rows, blocks, d]`` (``src/runtime.py:381-388``)."""
+    rows, blocks = stage_ids[0].shape
+    d = codebooks[0].shape[1]
+    acc = np.zeros((rows, blocks, d), dtype=np.float32)
+    for ids, book in zip(stage_ids, codebooks):
+        entries = np.asarray(book, dtype=np.float16).astype(np.float32)
+        acc += entries[np.asarray(ids).astype(np.int64)]
+    return acc
+
+
+def reconstruct_group_bits(
+    stage_ids: list[np.ndarray],
+    codebooks: list[np.ndarray],
+    row_scale: np.ndarray,
+    in_features: int,
+) -> np.ndarray:
+    """bf16 weight bits ``[rows, in_features]`` of one plain group (``src/runtime.py:379-414``)."""
+    acc = stage_sum_f32(stage_ids, codebooks)
+    rows = acc.shape[0]
+    w = acc.reshape(rows, -1)[:, :in_features]
+    w_bf = bf16_bits_to_f32(f32_to_bf16_bits(w))
+    rho = np.asarray(row_scale, dtype=np.float16).astype(np.float32).reshape(rows, 1)
+    rho_bf = bf16_bits_to_f32(f32_to_bf16_bits(rho))
+    return f32_to_bf16_bits(w_bf * rho_bf)
+
+
+def reconstruct_bits(groups: list[dict], in_features: int) -> np.ndarray:
+    """Concatenate per-group weights (``PackedGroupedBlockRVQLinear.reconstruct_weight``, ``src/runtime.py:1234-1236``).
+
+    Each group is a dict with ``stage_ids`` (list of ``[rows, blocks]`` int arrays),
+    ``codebooks`` (list of ``[entries, d]`` fp16 arrays) and ``row_scale``.
+    """
+    parts = [reconstruct_group_bits(g["stage_ids"], g["codebooks"], g["row_scale"], in_features) for g in groups]
+    return np.concatenate(parts, axis=0)
+
+
+def linear_exact(x_bits: np.ndarray, w_bits: np.ndarray, bias_bits: np.ndarray | None = None) -> np.ndarray:
+    """``y = x @ w.T (+ bias)`` over bf16 operands, accumulated in float64 (``src/runtime.py:1505``)."""
+    x = bf16_bits_to_f32(x_bits).astype(np.float64)
+    w = bf16_bits_to_f32(w_bits).astype(np.float64)
+    y = x @ w.T
+    if bias_bits is not None:
+        y = y + bf16_bits_to_f32(bias_bits).astype(np.float64)[None, :]
+    return y
+
+
+def forward_f32(x_bits: np.ndarray, groups: list[dict], in_features: int,
+                bias_bits: np.ndarray | None = None) -> np.ndarray:
+    """fp32 (pre-output-rounding) result of the per_group forward."""
+    w = reconstruct_bits(groups, in_features)
+    return linear_exact(x_bits, w, bias_bits).astype(np.float32)
+
+
+def unpack_route_code(ids: np.ndarray, entries_per_route: int = 256) -> tuple[np.ndarray, np.ndarray]:
+    """Split single-stage routed ids ``route * entries + code`` back into (route, code)."""
+    ids = np.asarray(ids).astype(np.int64)
+    return (ids // entries_per_route).astype(np.uint8), (ids % entries_per_route).astype(np.uint8)
+
+
+def groups_from_encoding(enc) -> list[dict]:
+    """Convert a (grouped) encoding object with torch tensors into oracle group dicts."""
+    groups = enc.groups if hasattr(enc, "groups") else (enc,)
+    out = []
+    for g in groups:
+        out.append(
+            {
+                "stage_ids": [t.cpu().numpy() for t in g.stage_ids],
+                "codebooks": [t.cpu().numpy().astype(np.float16) for t in g.codebooks],
+                "row_scale": g.row_scale.cpu().numpy(),
+            }
+        )
+    return out

@@ -1,0 +1,131 @@
+"""Generate golden fixtures by running the reference implementation itself.
+
+Run in a container that has the reference source tree (it is not needed, and
+not present, where the tests run):
+
+    python tests/golden/make_golden.py --reference <path-to-reference-checkout>
+
+For every case the script builds the synthetic encoding with
+``wal2026_b200.synthetic`` (seeded, fixed draw order), converts it into the
+reference's own ``BlockRVQEncoding``/``GroupedBlockRVQEncoding`` dataclasses,
+wraps it in the reference's ``PackedGroupedBlockRVQLinear`` with
+``matmul_strategy="per_group"`` (the dequantise-then-matmul path) and records:
+
+* ``w_bits``/``w_sha256`` - the bf16 weight from ``reconstruct_weight(torch.bfloat16)``;
+* ``y_ref_bf16``          - the reference forward output (bf16 bits);
+* ``y_ref32``             - ``x.float() @ W.float().T (+ bias)`` accumulated in float64;
+* SHA-256 digests of every input array, so the tests can prove that the
+  synthetic generator still produces the same bytes.
+
+Small cases store all arrays; the two full-size configurations store input
+digests, the weight digest and a bounded slice of the outputs.
+"""
+from __future__ import annotations
+
+import argparse
+import dataclasses
+import hashlib
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE.parents[1]))
+
+from wal2026_b200 import synthetic  # noqa: E402
+from wal2026_b200.block_vq import GroupedBlockRVQEncoding, single_group  # noqa: E402
+
+
+def sha(t: torch.Tensor | np.ndarray) -> str:
+    if isinstance(t, torch.Tensor):
+        t = t.detach().cpu().contiguous()
+        if t.dtype == torch.bfloat16:
+            t = t.view(torch.int16)
+        t = t.numpy()
+    return hashlib.sha256(np.ascontiguousarray(t).tobytes()).hexdigest()
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def to_reference(enc: GroupedBlockRVQEncoding, ref_block_vq):
+    groups = []
+    for g in enc.groups:
+        kwargs = {f.name: getattr(g, f.name) for f in dataclasses.fields(ref_block_vq.BlockRVQEncoding)}
+        groups.append(ref_block_vq.BlockRVQEncoding(**kwargs))
+    return ref_block_vq.GroupedBlockRVQEncoding(groups=tuple(groups), row_slices=enc.row_slices,
+                                                original_shape=enc.original_shape)
+
+
+def run_case(name, enc, Ms, x_seed, bias, ref_runtime, ref_block_vq, *, full: bool, y_rows: int | None = None):
+    ref_enc = to_reference(enc, ref_block_vq)
+    mod = ref_runtime.PackedGroupedBlockRVQLinear(ref_enc, bias, matmul_strategy="per_group")
+    with torch.no_grad():
+        w = mod.reconstruct_weight(torch.bfloat16)
+    out = {"name": np.array(name), "w_sha256": np.array(sha(w)),
+           "N": np.array(enc.original_shape[0]), "K": np.array(enc.original_shape[1])}
+    if full:
+        out["w_bits"] = bits(w)
+    for gi, g in enumerate(enc.groups):
+        for s, (ids, book) in enumerate(zip(g.stage_ids, g.codebooks)):
+            out[f"g{gi}_ids{s}_sha256"] = np.array(sha(ids))
+            out[f"g{gi}_book{s}_sha256"] = np.array(sha(book))
+            if full:
+                out[f"g{gi}_ids{s}"] = ids.numpy()
+                out[f"g{gi}_book{s}"] = book.numpy()
+        out[f"g{gi}_rho_sha256"] = np.array(sha(g.row_scale))
+        if full:
+            out[f"g{gi}_rho"] = g.row_scale.numpy()
+    if bias is not None:
+        out["bias_bits"] = bits(bias)
+    for M in Ms:
+        x = synthetic.activations(M, enc.original_shape[1], seed=x_seed)
+        with torch.no_grad():
+            y = mod(x)
+        y32 = x.double() @ w.double().T
+        if bias is not None:
+            y32 = y32 + bias.double()[None, :]
+        rows = slice(None) if y_rows is None else slice(0, y_rows)
+        out[f"x{M}_sha256"] = np.array(sha(x))
+        if full:
+            out[f"x{M}_bits"] = bits(x)
+        out[f"y{M}_ref32"] = y32[:, rows].float().numpy()
+        out[f"y{M}_ref_bf16"] = bits(y[:, rows])
+    np.savez_compressed(HERE / f"{name}.npz", **out)
+    print(f"wrote {name}.npz  w_sha256={out['w_sha256']}")
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", required=True, help="path of the reference checkout")
+    ap.add_argument("--skip-full", action="store_true")
+    args = ap.parse_args()
+    sys.path.insert(0, args.reference)
+    from src import block_vq as ref_block_vq  # type: ignore
+    from src import runtime as ref_runtime  # type: ignore
+
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    small = [
+        ("small_r2_d8", single_group(synthetic.rvq_encoding(37, 64, d=8, R=2, seed=11)), [1, 3], 11, True),
+        ("small_r1_ragged", single_group(synthetic.rvq_encoding(48, 100, d=8, R=1, C=200, seed=12)), [5], 12, False),
+        ("small_r3_d16", single_group(synthetic.rvq_encoding(64, 96, d=16, R=3, seed=13)), [2, 16], 13, False),
+        ("small_grouped", synthetic.grouped_encoding([16, 24, 9], 128, d=8, R=2, seed=14), [4], 14, True),
+        ("small_route", single_group(synthetic.route_inputs(40, 64, d=16, G=4, seed=15).encoding()), [3], 15, False),
+        ("small_d32", single_group(synthetic.rvq_encoding(33, 128, d=32, R=2, seed=16)), [16], 16, True),
+        ("small_r4_wide", single_group(synthetic.rvq_encoding(20, 272, d=8, R=4, seed=17)), [9], 17, False),
+    ]
+    for name, enc, Ms, seed, with_bias in small:
+        bias = synthetic.bias_vector(enc.original_shape[0], seed=seed) if with_bias else None
+        run_case(name, enc, Ms, seed, bias, ref_runtime, ref_block_vq, full=True)
+    if args.skip_full:
+        return
+    run_case("cfg0", synthetic.cfg0_encoding(0), [1, 4, 16], 0, None, ref_runtime, ref_block_vq, full=False)
+    run_case("cfg1", single_group(synthetic.cfg1_inputs(1).encoding()), [1, 8], 1, None, ref_runtime,
+             ref_block_vq, full=False, y_rows=2048)
+
+
+if __name__ == "__main__":
+    main()
