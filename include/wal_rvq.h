@@ -1,0 +1,163 @@
+/*
+ * wal_rvq.h - C ABI of the B200 Block-RVQ / route-codebook runtime linear.
+ *
+ * A Block-RVQ linear stores an N x K weight as, for every (row, block of d
+ * columns) unit and every stage s < R, an id into a per-stage fp16 codebook
+ * of `num_entries` rows of d values, plus one fp16 scale per output row.
+ * Rows may be split into groups that carry their own codebooks.  The weight
+ * this library decodes is, bit for bit, the one the reference's
+ * dequantise-then-matmul path builds for a bf16 forward:
+ *
+ *   w[n, k] = bf16( bf16( sum_s fp32(C_s[id_s(n, k / d)][k % d]) ) * bf16(rho[n]) )
+ *
+ * (reference src/runtime.py:379-414, PackedBlockRVQGroup.reconstruct_weight),
+ * and the GEMV computes y = x @ w^T (+ bias) with fp32 accumulation
+ * (reference src/runtime.py:1501-1507, PackedGroupedBlockRVQLinear.forward,
+ * default "per_group" strategy).  The dense weight is never materialised by
+ * the GEMV.
+ *
+ * Conventions: every entry point returns a wal_status (0 = success) and never
+ * throws.  Device pointers are CUDA device memory of the current device;
+ * `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ * Host pointers are ordinary CPU memory.  bf16/fp16 values are passed as
+ * uint16_t bit patterns.  No entry point synchronises the stream.
+ */
+#ifndef WAL_RVQ_H
+#define WAL_RVQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define WAL_API __attribute__((visibility("default")))
+#else
+#define WAL_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum wal_status {
+  WAL_OK = 0,
+  WAL_ERR_INVALID_ARGUMENT = 1, /* null pointer, non-positive size            */
+  WAL_ERR_SHAPE = 2,            /* inconsistent or unsupported dimensions     */
+  WAL_ERR_ALIGNMENT = 3,        /* pointer or leading dimension misaligned    */
+  WAL_ERR_ID_RANGE = 4,         /* an id or route is >= its codebook size     */
+  WAL_ERR_UNSUPPORTED = 5,      /* valid input this build does not implement  */
+  WAL_ERR_CUDA = 6,             /* a CUDA runtime call failed                  */
+  WAL_ERR_BUFFER_TOO_SMALL = 7  /* caller buffer smaller than required        */
+} wal_status;
+
+typedef enum wal_dtype { WAL_BF16 = 0, WAL_F32 = 1, WAL_F16 = 2 } wal_dtype;
+
+/* Rows per packed tile and blocks per packed chunk (layout constants). */
+#define WAL_TILE_ROWS 16
+#define WAL_CHUNK_BLOCKS 16
+
+/* Shape of one packed linear. */
+typedef struct wal_rvq_geometry {
+  int64_t out_features; /* N (sum of group rows)                                  */
+  int64_t in_features;  /* K, a multiple of 4                                      */
+  int32_t block_size;   /* d in {8, 16, 32}                                         */
+  int32_t num_stages;   /* R in 1..4                                                */
+  int32_t num_entries;  /* codebook rows per stage: <= 256 (1-byte ids) or, for     */
+                        /* R == 1, <= 32767 (2-byte ids, e.g. route*256 + code)     */
+  int32_t num_groups;   /* row groups, each with its own R codebooks               */
+} wal_rvq_geometry;
+
+/* Device-resident packed linear.  All pointers are device pointers. */
+typedef struct wal_rvq_layer {
+  wal_rvq_geometry geom;
+  int64_t num_tiles;          /* from wal_rvq_packed_size                            */
+  const void* packed_ids;     /* packed id stream (layout in wal_rvq_pack)           */
+  const int32_t* tile_table;  /* 4 x int32 per tile: group, first row, rows, 0       */
+  const uint16_t* codebooks;  /* fp16 [num_groups][R][num_entries][d]                */
+  const uint16_t* row_scale;  /* fp16 [N]                                            */
+  const uint16_t* bias;       /* bf16 [N] or NULL                                    */
+} wal_rvq_layer;
+
+/* Human-readable text for a status code (static storage). */
+WAL_API const char* wal_status_string(int status);
+
+/* Library version as an integer (major * 10000 + minor * 100 + patch). */
+WAL_API int wal_version(void);
+
+/*
+ * Size of the packed id stream and tile count for a geometry whose groups
+ * have the given row counts (host array of num_groups values summing to N).
+ * Replaces the buffer registration of reference src/runtime.py:262-265
+ * (stage_ids_{i} buffers) with one tile-major stream.
+ */
+WAL_API int wal_rvq_packed_size(const wal_rvq_geometry* geom, const int64_t* group_rows,
+                        size_t* packed_bytes, int64_t* num_tiles);
+
+/*
+ * Host re-layout of per-group, per-stage id matrices into the packed stream.
+ * stage_ids[g * R + s] points to a host [rows_g, blocks] row-major matrix of
+ * uint8 (num_entries <= 256) or uint16/int16 ids, blocks = ceil(K / d).
+ * Every id is checked against num_entries (WAL_ERR_ID_RANGE).
+ *
+ * Layout: tiles of 16 rows (groups padded to whole tiles with id 0), each tile
+ * split into chunks of 16 blocks; chunk = 16 rows x R stages x 16 ids, id
+ * width 1 or 2 bytes little-endian, i.e. 16*R*idw bytes per row-chunk, so a
+ * row-chunk is whole 16-byte vectors and each 8-row half of a chunk is one
+ * contiguous, 128-byte-aligned run.  tile_table receives (group, first output
+ * row, valid rows, 0) per tile.
+ * Replaces reference src/runtime.py:249-344 (PackedBlockRVQGroup.__init__
+ * buffer registration) and src/runtime.py:855-876 (_triton_state id stacking).
+ */
+WAL_API int wal_rvq_pack(const wal_rvq_geometry* geom, const int64_t* group_rows,
+                 const void* const* stage_ids, void* packed, size_t packed_bytes,
+                 int32_t* tile_table);
+
+/*
+ * Route-codebook packing: a uint8 route (< num_routes) and a uint8 code per
+ * unit, host [N, blocks] each, become single-stage 2-byte ids
+ * route * 256 + code into a flattened [num_routes * 256, d] codebook.
+ * geom must have num_stages == 1, num_groups == 1 and
+ * num_entries == num_routes * 256.  No reference module exists for this
+ * format; it is the one-stage special case of reference src/runtime.py:379-414.
+ */
+WAL_API int wal_route_pack(const wal_rvq_geometry* geom, const uint8_t* route, const uint8_t* code,
+                   void* packed, size_t packed_bytes, int32_t* tile_table);
+
+/*
+ * Decode GEMV (M <= 16 tokens): y[M, N] = x[M, K] @ w^T (+ bias).
+ * x: device bf16, row stride ldx elements (ldx >= K, ldx % 4 == 0, 8-byte
+ * aligned base).  y: device, row stride ldy elements, dtype y_dtype
+ * (WAL_BF16: one rounding of the fp32 result; WAL_F32: the fp32 result).
+ * Replaces reference src/runtime.py:1362-1507 (PackedGroupedBlockRVQLinear.forward)
+ * and src/triton_id_matmul.py:220-306 (rvq_group_linear_matmul).
+ */
+WAL_API int wal_rvq_gemv(const wal_rvq_layer* layer, const uint16_t* x, int64_t M, int64_t ldx,
+                 void* y, int64_t ldy, int y_dtype, void* stream);
+
+/*
+ * Same as wal_rvq_gemv with an explicit split of each 16-row tile's blocks
+ * over `warps_per_tile` warps (1, 2, 4 or 8; 0 = library default) and an
+ * explicit CTA count (0 = one persistent wave).  For tuning and tests.
+ */
+WAL_API int wal_rvq_gemv_ex(const wal_rvq_layer* layer, const uint16_t* x, int64_t M, int64_t ldx,
+                    void* y, int64_t ldy, int y_dtype, int warps_per_tile, int num_ctas,
+                    void* stream);
+
+/*
+ * Materialise the bf16 weight [N, K] (row stride ldw) from the packed form,
+ * bit-identical to reference src/runtime.py:1234-1236
+ * (PackedGroupedBlockRVQLinear.reconstruct_weight(torch.bfloat16)).
+ */
+WAL_API int wal_rvq_dequant(const wal_rvq_layer* layer, uint16_t* w, int64_t ldw, void* stream);
+
+/*
+ * Read the packed stream back into per-stage id matrices on the device:
+ * ids [R][N][blocks] with 1-byte (num_entries <= 256) or 2-byte elements.
+ * Used to prove the re-layout is lossless (ids must round-trip bit-exactly).
+ */
+WAL_API int wal_rvq_unpack_ids(const wal_rvq_layer* layer, void* ids, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WAL_RVQ_H */

@@ -43,3 +43,30 @@ def groups_from_fixture(fx: dict) -> list[dict]:
 
 def bf16_tensor(bits: np.ndarray) -> torch.Tensor:
     return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16)
+
+
+def encoding_from_fixture(fx: dict):
+    """Rebuild the grouped encoding (torch tensors) a fixture was generated from."""
+    from wal2026_b200.block_vq import GroupedBlockRVQEncoding, make_plain_encoding
+
+    K = int(fx["K"])
+    groups, slices, row0 = [], [], 0
+    for g in groups_from_fixture(fx):
+        d = int(g["codebooks"][0].shape[1])
+        ids = [torch.from_numpy(np.ascontiguousarray(a)) for a in g["stage_ids"]]
+        books = [torch.from_numpy(np.ascontiguousarray(b)) for b in g["codebooks"]]
+        rho = torch.from_numpy(np.ascontiguousarray(g["row_scale"]))
+        enc = make_plain_encoding(ids, books, rho, in_features=K, block_size=d)
+        n = int(ids[0].shape[0])
+        groups.append(enc)
+        slices.append((row0, row0 + n))
+        row0 += n
+    return GroupedBlockRVQEncoding(groups=tuple(groups), row_slices=tuple(slices), original_shape=(row0, K))
+
+
+def x_inputs(fx: dict) -> dict[int, torch.Tensor]:
+    out = {}
+    for key in fx:
+        if key.startswith("x") and key.endswith("_bits"):
+            out[int(key[1:-5])] = bf16_tensor(fx[key])
+    return out

@@ -1,0 +1,167 @@
+"""Parity of the CUDA path with the reference (golden fixtures) and the CPU oracle.
+
+Gate (from the build's north star): max|y - y_ref| <= 2e-3 * ||y_ref||_inf on the
+fp32 (pre-output-rounding) result, bf16 output within one bf16 ulp of the
+reference's bf16 output, materialised weights and unpacked ids bit-exact.
+All calls go through the C ABI (``libwal_rvq.so``).
+"""
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import rvq_oracle as orc
+from tests import goldens
+from wal2026_b200 import synthetic
+from wal2026_b200.block_vq import single_group
+from wal2026_b200.runtime import PackedGroupedBlockRVQLinear, RouteCodebookLinear
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-3  # relative to ||y_ref||_inf
+
+
+def bits_of(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def gemv_f32(mod: PackedGroupedBlockRVQLinear, x: torch.Tensor, **kw) -> torch.Tensor:
+    x = x.cuda()
+    y = torch.empty((x.shape[0], mod.out_features), device="cuda", dtype=torch.float32)
+    mod.gemv_into(x, y, **kw)
+    return y
+
+
+def assert_close(y: np.ndarray, ref: np.ndarray, tol: float = TOL) -> float:
+    scale = float(np.abs(ref).max())
+    err = float(np.abs(y.astype(np.float64) - ref.astype(np.float64)).max())
+    assert err <= tol * scale, f"max err {err} > {tol} * {scale}"
+    return err / max(scale, 1e-30)
+
+
+def assert_bf16_within_ulp(y_bits: np.ndarray, ref_bits: np.ndarray) -> None:
+    a = orc.bf16_bits_to_f32(y_bits).astype(np.float64)
+    b = orc.bf16_bits_to_f32(ref_bits).astype(np.float64)
+    ulp = np.maximum(np.abs(b), 1e-30) * 2.0 ** -7
+    assert np.all(np.abs(a - b) <= ulp)
+
+
+@pytest.mark.parametrize("name", goldens.SMALL_CASES)
+def test_small_cases_match_reference(name):
+    fx = goldens.load(name)
+    enc = goldens.encoding_from_fixture(fx)
+    bias = goldens.bf16_tensor(fx["bias_bits"]) if "bias_bits" in fx else None
+    mod = PackedGroupedBlockRVQLinear(enc, bias).cuda()
+    w = mod.reconstruct_weight(torch.bfloat16)
+    assert np.array_equal(bits_of(w), fx["w_bits"])
+    ids = mod.unpack_ids().cpu().numpy()
+    for s in range(mod.num_stages):
+        want = np.concatenate([g.stage_ids[s].numpy() for g in enc.groups])
+        assert np.array_equal(ids[s].view(want.dtype), want)
+    for M, x in goldens.x_inputs(fx).items():
+        y32 = gemv_f32(mod, x).cpu().numpy()
+        assert_close(y32, fx[f"y{M}_ref32"])
+        yb = mod(x.cuda())
+        assert yb.dtype == torch.bfloat16 and yb.shape == (M, mod.out_features)
+        assert_bf16_within_ulp(bits_of(yb), fx[f"y{M}_ref_bf16"])
+
+
+def test_cfg0_full_size_matches_reference():
+    fx = goldens.load("cfg0")
+    mod = PackedGroupedBlockRVQLinear(synthetic.cfg0_encoding(0)).cuda()
+    w = mod.reconstruct_weight()
+    assert hashlib.sha256(bits_of(w).tobytes()).hexdigest() == str(fx["w_sha256"])
+    for M in (1, 4, 16):
+        x = synthetic.activations(M, 2048, seed=0)
+        assert goldens.sha(x) == str(fx[f"x{M}_sha256"])
+        rel = assert_close(gemv_f32(mod, x).cpu().numpy(), fx[f"y{M}_ref32"])
+        assert rel < 1e-4  # fp32 accumulation-order noise only
+        assert_bf16_within_ulp(bits_of(mod(x.cuda())), fx[f"y{M}_ref_bf16"])
+
+
+def test_cfg1_route_codebook_full_size_matches_reference():
+    fx = goldens.load("cfg1")
+    inp = synthetic.cfg1_inputs(1)
+    mod = RouteCodebookLinear.from_routes(inp.route, inp.code, inp.codebooks, inp.row_scale,
+                                          in_features=4096).cuda()
+    w = mod.reconstruct_weight()
+    assert hashlib.sha256(bits_of(w).tobytes()).hexdigest() == str(fx["w_sha256"])
+    ids = mod.unpack_ids()[0].cpu().numpy().view(np.uint16)
+    route, code = orc.unpack_route_code(ids)
+    assert np.array_equal(route, inp.route.numpy()) and np.array_equal(code, inp.code.numpy())
+    w_bits = bits_of(w)
+    for M in (1, 8, 16):
+        x = synthetic.activations(M, 4096, seed=1)
+        y = gemv_f32(mod, x).cpu().numpy()
+        ref = orc.linear_exact(bits_of(x), w_bits).astype(np.float32)
+        assert_close(y, ref)
+        if f"y{M}_ref32" in fx:
+            assert_close(y[:, :2048], fx[f"y{M}_ref32"])
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 5, 8, 9, 13, 16, 17, 37])
+def test_every_token_count(M):
+    enc = single_group(synthetic.rvq_encoding(200, 512, d=8, R=2, seed=21))
+    bias = synthetic.bias_vector(200, seed=21)
+    mod = PackedGroupedBlockRVQLinear(enc, bias).cuda()
+    x = synthetic.activations(M, 512, seed=21)
+    ref = orc.forward_f32(bits_of(x), orc.groups_from_encoding(enc), 512, bits_of(bias))
+    assert_close(gemv_f32(mod, x).cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("wpt", [1, 2, 4, 8])
+@pytest.mark.parametrize("ctas", [0, 1, 3])
+def test_work_split_variants_agree(wpt, ctas):
+    enc = synthetic.grouped_encoding([48, 40, 64], 1024, d=16, R=2, seed=5)
+    mod = PackedGroupedBlockRVQLinear(enc).cuda()
+    x = synthetic.activations(6, 1024, seed=5)
+    ref = orc.forward_f32(bits_of(x), orc.groups_from_encoding(enc), 1024)
+    assert_close(gemv_f32(mod, x, warps_per_tile=wpt, num_ctas=ctas).cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("d,R,C,K", [(8, 1, 256, 264), (8, 3, 256, 520), (16, 4, 128, 1008), (32, 1, 256, 96),
+                                     (32, 3, 256, 200), (8, 1, 3000, 256), (32, 1, 1024, 320)])
+def test_shape_and_stage_variants(d, R, C, K):
+    enc = single_group(synthetic.rvq_encoding(70, K, d=d, R=R, C=C, seed=d + R))
+    mod = PackedGroupedBlockRVQLinear(enc).cuda()
+    w = mod.reconstruct_weight()
+    want = orc.reconstruct_bits(orc.groups_from_encoding(enc), K)
+    assert np.array_equal(bits_of(w), want)
+    for M in (1, 11):
+        x = synthetic.activations(M, K, seed=M)
+        assert_close(gemv_f32(mod, x).cpu().numpy(), orc.linear_exact(bits_of(x), want))
+
+
+def test_signed_zero_and_extreme_entries_decode_like_reference():
+    enc = synthetic.rvq_encoding(32, 64, d=8, R=2, seed=9)
+    b0 = enc.codebooks[0].clone()
+    b1 = enc.codebooks[1].clone()
+    b0[0] = -0.0
+    b1[0] = -0.0
+    b0[1] = 65504.0
+    b1[1] = -65504.0
+    b0[2] = 6e-8  # fp16 subnormal
+    enc.stage_ids[0][:4] = torch.tensor([0, 1, 2, 3], dtype=torch.uint8).repeat(8)[:8]
+    enc.stage_ids[1][:4] = torch.tensor([0, 1, 0, 1], dtype=torch.uint8).repeat(8)[:8]
+    import dataclasses
+
+    enc = dataclasses.replace(enc, codebooks=(b0, b1))
+    mod = PackedGroupedBlockRVQLinear(single_group(enc)).cuda()
+    want = orc.reconstruct_bits(orc.groups_from_encoding(single_group(enc)), 64)
+    assert np.array_equal(bits_of(mod.reconstruct_weight()), want)
+
+
+def test_cuda_forward_keeps_leading_dims_and_stream():
+    enc = single_group(synthetic.rvq_encoding(64, 128, seed=4))
+    mod = PackedGroupedBlockRVQLinear(enc).cuda()
+    x = synthetic.activations(6, 128, seed=4).view(2, 3, 128).cuda()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        y = mod(x)
+    s.synchronize()
+    assert y.shape == (2, 3, 64)
+    ref = orc.forward_f32(bits_of(x.reshape(6, 128)), orc.groups_from_encoding(enc), 128)
+    assert_close(y.float().reshape(6, 64).cpu().numpy(), ref, tol=8e-3)

@@ -91,3 +91,27 @@ def test_oracle_full_cfg1_pinned():
     assert np.abs(y - ref32).max() <= 1e-5 * np.abs(ref32).max()
     route, code = orc.unpack_route_code(g.stage_ids[0].numpy())
     assert np.array_equal(route, inp.route.numpy()) and np.array_equal(code, inp.code.numpy())
+
+
+@pytest.mark.parametrize("name", goldens.SMALL_CASES)
+def test_c_oracle_matches_reference(name):
+    from oracle import c_oracle
+
+    fx = goldens.load(name)
+    groups = goldens.groups_from_fixture(fx)
+    K = int(fx["K"])
+    assert np.array_equal(c_oracle.reconstruct(groups, K), fx["w_bits"])
+    bias = fx.get("bias_bits")
+    for M, x in goldens.x_inputs(fx).items():
+        xb = x.view(torch.int16).numpy().view(np.uint16)
+        y = c_oracle.forward(xb, groups, K, bias)
+        ref = fx[f"y{M}_ref32"]
+        assert np.abs(y - ref).max() <= 1e-5 * np.abs(ref).max()
+
+
+def test_c_oracle_full_cfg0_weight_digest():
+    from oracle import c_oracle
+
+    fx = goldens.load("cfg0")
+    w = c_oracle.reconstruct(orc.groups_from_encoding(synthetic.cfg0_encoding(0)), 2048)
+    assert hashlib.sha256(w.tobytes()).hexdigest() == str(fx["w_sha256"])

@@ -1,0 +1,159 @@
+"""Host-side re-layout of Block-RVQ encodings into the packed, tile-major form.
+
+The packed form (layout documented in ``include/wal_rvq.h``) is built once at
+load time by the C ABI's ``wal_rvq_pack``/``wal_route_pack`` and then lives in
+device memory as module buffers.  It replaces the per-stage id buffers of the
+reference's ``PackedBlockRVQGroup`` (reference ``src/runtime.py:249-344``).
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _abi
+from .block_vq import BlockRVQEncoding, GroupedBlockRVQEncoding
+
+
+@dataclass
+class PackedArrays:
+    """Host (CPU) tensors of one packed linear, ready to be registered as buffers."""
+
+    geometry: _abi.Geometry
+    num_tiles: int
+    packed_ids: torch.Tensor  # uint8 [bytes]
+    tile_table: torch.Tensor  # int32 [num_tiles, 4]
+    codebooks: torch.Tensor   # fp16 [groups, R, entries, d]
+    row_scale: torch.Tensor   # fp16 [N]
+
+
+def _geometry(N: int, K: int, d: int, R: int, entries: int, groups: int) -> _abi.Geometry:
+    return _abi.Geometry(out_features=N, in_features=K, block_size=d, num_stages=R, num_entries=entries,
+                         num_groups=groups)
+
+
+def validate_grouped(enc: GroupedBlockRVQEncoding) -> tuple[int, int, int, int]:
+    """Check an encoding is supported by the fused path; return (d, R, entries, K).
+
+    Unsupported encodings raise ``ValueError`` like the reference's fused path
+    does (``src/runtime.py:848-853``).
+    """
+    if not enc.groups:
+        raise ValueError("encoding has no groups")
+    K = int(enc.original_shape[1])
+    first = enc.groups[0]
+    d = int(first.block_size)
+    R = int(first.num_stages)
+    entries = int(first.codebooks[0].shape[0])
+    row = 0
+    for g, (r0, r1) in zip(enc.groups, enc.row_slices):
+        if not g.is_plain():
+            raise ValueError("packed CUDA path supports plain Block-RVQ encodings only "
+                             "(no stage_scales, block_scale, residual correction or transform)")
+        if int(g.block_size) != d or int(g.num_stages) != R:
+            raise ValueError("all row groups must share block_size and num_stages")
+        if any(int(c.shape[0]) != entries or int(c.shape[1]) != d for c in g.codebooks):
+            raise ValueError("all codebooks must be [entries, block_size] with the same entries")
+        if int(g.original_shape[1]) != K:
+            raise ValueError("group in_features differs from the layer's")
+        if r0 != row or r1 - r0 != int(g.original_shape[0]):
+            raise ValueError("row_slices must be contiguous and match the group row counts")
+        if int(g.padded_cols) != -(-K // d) * d:
+            raise ValueError("padded_cols must equal ceil(in_features / block_size) * block_size")
+        row = r1
+    if row != int(enc.original_shape[0]):
+        raise ValueError("row_slices do not cover out_features")
+    if d not in (8, 16, 32):
+        raise ValueError(f"block_size {d} is not supported (8, 16 or 32)")
+    if not 1 <= R <= 4:
+        raise ValueError(f"num_stages {R} is not supported (1..4)")
+    if R > 1 and entries > 256:
+        raise ValueError("multi-stage codebooks must have <= 256 entries")
+    if entries > 32767:
+        raise ValueError("codebooks larger than 32767 entries are not supported")
+    if K % 4 != 0:
+        raise ValueError("in_features must be a multiple of 4")
+    return d, R, entries, K
+
+
+def _ids_array(t: torch.Tensor, entries: int) -> np.ndarray:
+    t = t.detach().cpu().contiguous()
+    if entries <= 256:
+        if t.dtype != torch.uint8:
+            t = t.to(torch.int64)
+            if int(t.min()) < 0 or int(t.max()) >= 256:
+                raise ValueError("id out of range of its codebook")
+            t = t.to(torch.uint8)
+        return t.numpy()
+    # two-byte ids (int16 in the reference for <= 32767 entries)
+    if t.dtype == torch.int16:
+        return t.numpy().view(np.uint16)
+    t = t.to(torch.int64)
+    if int(t.min()) < 0 or int(t.max()) >= 65536:
+        raise ValueError("id out of range of its codebook")
+    return t.to(torch.int32).numpy().astype(np.uint16)
+
+
+def pack_grouped(enc: GroupedBlockRVQEncoding) -> PackedArrays:
+    d, R, entries, K = validate_grouped(enc)
+    lib = _abi.load()
+    N = int(enc.original_shape[0])
+    G = len(enc.groups)
+    geom = _geometry(N, K, d, R, entries, G)
+    rows = (ctypes.c_int64 * G)(*[int(g.original_shape[0]) for g in enc.groups])
+    nbytes = ctypes.c_size_t(0)
+    ntiles = ctypes.c_int64(0)
+    _abi.check(lib.wal_rvq_packed_size(ctypes.byref(geom), rows, ctypes.byref(nbytes), ctypes.byref(ntiles)),
+               "wal_rvq_packed_size")
+    arrays = []
+    for g in enc.groups:
+        for ids in g.stage_ids:
+            a = _ids_array(ids, entries)
+            if a.shape != (int(g.original_shape[0]), -(-K // d)):
+                raise ValueError(f"stage ids shape {a.shape} does not match [rows, blocks]")
+            arrays.append(np.ascontiguousarray(a))
+    ptrs = (ctypes.c_void_p * len(arrays))(*[a.ctypes.data for a in arrays])
+    packed = torch.empty(int(nbytes.value), dtype=torch.uint8)
+    table = torch.empty(int(ntiles.value), 4, dtype=torch.int32)
+    _abi.check(
+        lib.wal_rvq_pack(ctypes.byref(geom), rows, ptrs, packed.data_ptr(), nbytes.value,
+                         ctypes.cast(table.data_ptr(), ctypes.POINTER(ctypes.c_int32))),
+        "wal_rvq_pack",
+    )
+    books = torch.stack(
+        [torch.stack([c.detach().cpu().to(torch.float16) for c in g.codebooks]) for g in enc.groups]
+    ).contiguous()
+    rho = torch.cat([g.row_scale.detach().cpu().to(torch.float16).reshape(-1) for g in enc.groups]).contiguous()
+    return PackedArrays(geom, int(ntiles.value), packed, table, books, rho)
+
+
+def pack_routes(route: torch.Tensor, code: torch.Tensor, codebooks: torch.Tensor, row_scale: torch.Tensor,
+                in_features: int) -> PackedArrays:
+    """Pack a route-codebook weight (uint8 route and code per unit) through ``wal_route_pack``."""
+    lib = _abi.load()
+    G, C, d = (int(v) for v in codebooks.shape)
+    if C != 256:
+        raise ValueError("route-codebook packing expects 256 entries per routed codebook")
+    N, B = (int(v) for v in route.shape)
+    if tuple(code.shape) != (N, B) or B != -(-in_features // d):
+        raise ValueError("route/code must be [out_features, ceil(in_features / d)]")
+    geom = _geometry(N, in_features, d, 1, G * C, 1)
+    rows = (ctypes.c_int64 * 1)(N)
+    nbytes = ctypes.c_size_t(0)
+    ntiles = ctypes.c_int64(0)
+    _abi.check(lib.wal_rvq_packed_size(ctypes.byref(geom), rows, ctypes.byref(nbytes), ctypes.byref(ntiles)),
+               "wal_rvq_packed_size")
+    r = np.ascontiguousarray(route.detach().cpu().to(torch.uint8).numpy())
+    c = np.ascontiguousarray(code.detach().cpu().to(torch.uint8).numpy())
+    packed = torch.empty(int(nbytes.value), dtype=torch.uint8)
+    table = torch.empty(int(ntiles.value), 4, dtype=torch.int32)
+    _abi.check(
+        lib.wal_route_pack(ctypes.byref(geom), r.ctypes.data, c.ctypes.data, packed.data_ptr(), nbytes.value,
+                           ctypes.cast(table.data_ptr(), ctypes.POINTER(ctypes.c_int32))),
+        "wal_route_pack",
+    )
+    books = codebooks.detach().cpu().to(torch.float16).reshape(1, 1, G * C, d).contiguous()
+    rho = row_scale.detach().cpu().to(torch.float16).reshape(-1).contiguous()
+    return PackedArrays(geom, int(ntiles.value), packed, table, books, rho)

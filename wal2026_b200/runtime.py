@@ -1,0 +1,306 @@
+"""Drop-in runtime linear modules backed by the sm_100a CUDA library.
+
+``PackedGroupedBlockRVQLinear`` keeps the constructor, attributes and forward
+contract of the reference module of the same name (reference
+``src/runtime.py:1175-1236`` and ``:1362-1507``): it takes a
+``GroupedBlockRVQEncoding`` and an optional bias, exposes ``in_features``,
+``out_features``, ``groups``, ``row_slices`` and ``reconstruct_weight``, and maps
+``x[..., in_features]`` to ``y[..., out_features]`` in ``x.dtype``.  Every
+``matmul_strategy`` the reference accepts is accepted here; they are
+numerically interchangeable strategies in the reference, and this module always
+runs its one fused kernel, which reproduces the default ``per_group`` path's
+weight bit for bit.
+
+There is no CPU path: the forward raises on CPU input, and the CUDA library
+must be built (``python -m wal2026_b200.build``).
+"""
+from __future__ import annotations
+
+import ctypes
+import weakref
+from typing import Optional
+
+import torch
+from torch import Tensor, nn
+
+from . import _abi
+from .block_vq import GroupedBlockRVQEncoding, single_group
+from .packing import PackedArrays, pack_grouped, pack_routes
+
+# the reference's accepted strategy names (src/runtime.py:1192)
+MATMUL_STRATEGIES = frozenset({
+    "per_group", "per_group_fast", "full_weight", "full_weight_fast", "full_weight_hot", "full_weight_hot_v2",
+    "chunked_weight", "local_palette", "triton_hot_cold_persistent", "stage_local_hot_cold",
+    "stage_local_hot_cold_b1", "stage_local_hot_cold_b2", "stage_local_hot_cold_b3", "stagewise_einsum",
+    "triton_block_rvq", "stacked_matmul",
+})
+
+TARGET_LINEAR_SUFFIXES = (
+    "self_attn.q_proj",
+    "self_attn.k_proj",
+    "self_attn.v_proj",
+    "self_attn.o_proj",
+    "mlp.gate_proj",
+    "mlp.up_proj",
+    "mlp.down_proj",
+)
+
+
+def _check_strategy_args(matmul_strategy, matmul_chunk_rows, local_palette_group_cols, hot_topk):
+    """Same argument validation as reference ``src/runtime.py:1190-1211``."""
+    if matmul_strategy == "triton_hot_cold_persistent" and local_palette_group_cols is None:
+        local_palette_group_cols = 256
+    if matmul_strategy not in MATMUL_STRATEGIES:
+        raise ValueError(f"unsupported matmul_strategy: {matmul_strategy}")
+    if matmul_strategy == "chunked_weight" and (matmul_chunk_rows is None or int(matmul_chunk_rows) <= 0):
+        raise ValueError("chunked_weight requires a positive matmul_chunk_rows")
+    if matmul_strategy in {"local_palette", "triton_hot_cold_persistent"} and (
+        local_palette_group_cols is None or int(local_palette_group_cols) <= 0
+    ):
+        raise ValueError(f"{matmul_strategy} requires a positive local_palette_group_cols")
+    needs_topk = {"full_weight_hot", "full_weight_hot_v2", "triton_hot_cold_persistent", "stage_local_hot_cold",
+                  "stage_local_hot_cold_b1", "stage_local_hot_cold_b2", "stage_local_hot_cold_b3"}
+    if matmul_strategy in needs_topk and (hot_topk is None or int(hot_topk) <= 0):
+        raise ValueError(f"{matmul_strategy} requires a positive hot_topk")
+    return local_palette_group_cols
+
+
+class PackedBlockRVQGroup(nn.Module):
+    """One row group of a packed linear (reference ``src/runtime.py:248``).
+
+    The ids of every group live in the parent's single packed stream; a group
+    keeps its shape attributes, its codebooks and row scales (small) and
+    reaches the parent through a weak reference for ``reconstruct_weight``.
+    """
+
+    def __init__(self, enc, parent: "PackedGroupedBlockRVQLinear", row0: int, row1: int) -> None:
+        super().__init__()
+        self.block_size = int(enc.block_size)
+        self.in_features = int(enc.original_shape[1])
+        self.out_features = int(enc.original_shape[0])
+        self.padded_cols = int(enc.padded_cols)
+        self.num_stages = len(enc.stage_ids)
+        self.product_splits = int(enc.product_splits)
+        self.stages_per_split = tuple(int(x) for x in enc.stages_per_split)
+        self.transform_kind = enc.transform_kind
+        self.residual_correction = enc.residual_correction
+        self.row0, self.row1 = int(row0), int(row1)
+        self._parent = weakref.ref(parent)
+
+    def reconstruct_weight(self, out_dtype: torch.dtype = torch.bfloat16) -> Tensor:
+        parent = self._parent()
+        if parent is None:
+            raise RuntimeError("group outlived its packed linear")
+        return parent.reconstruct_weight(out_dtype)[self.row0:self.row1]
+
+
+class PackedGroupedBlockRVQLinear(nn.Module):
+    """Block-RVQ linear with packed ids and the fused CUDA decode GEMV."""
+
+    def __init__(
+        self,
+        enc: GroupedBlockRVQEncoding,
+        bias: Optional[Tensor] = None,
+        *,
+        matmul_strategy: str = "per_group",
+        matmul_chunk_rows: Optional[int] = None,
+        local_palette_group_cols: Optional[int] = None,
+        hot_topk: Optional[int] = None,
+        hot_score_mode: str = "row_scale_norm",
+        hot_min_stage_share: float = 0.0,
+        hot_score_threshold_ratio: float = 0.0,
+        _packed: Optional[PackedArrays] = None,
+    ) -> None:
+        super().__init__()
+        local_palette_group_cols = _check_strategy_args(matmul_strategy, matmul_chunk_rows,
+                                                        local_palette_group_cols, hot_topk)
+        if not isinstance(enc, GroupedBlockRVQEncoding):
+            enc = single_group(enc)
+        self.in_features = int(enc.original_shape[1])
+        self.out_features = int(enc.original_shape[0])
+        self.row_slices = tuple(tuple(int(v) for v in s) for s in enc.row_slices)
+        self.matmul_strategy = matmul_strategy
+        self.matmul_chunk_rows = None if matmul_chunk_rows is None else int(matmul_chunk_rows)
+        self.local_palette_group_cols = None if local_palette_group_cols is None else int(local_palette_group_cols)
+        self.hot_topk = None if hot_topk is None else int(hot_topk)
+        self.hot_score_mode = hot_score_mode
+        self.hot_min_stage_share = float(hot_min_stage_share)
+        self.hot_score_threshold_ratio = float(hot_score_threshold_ratio)
+        packed = _packed if _packed is not None else pack_grouped(enc)
+        self._set_packed(packed)
+        self.groups = nn.ModuleList(
+            PackedBlockRVQGroup(g, self, r0, r1) for g, (r0, r1) in zip(enc.groups, self.row_slices)
+        )
+        if bias is not None:
+            self.register_buffer("bias", bias.detach().to(torch.bfloat16).reshape(-1).contiguous())
+        else:
+            self.bias = None
+        self._layer_cache: tuple | None = None
+
+    def _set_packed(self, packed: PackedArrays) -> None:
+        g = packed.geometry
+        self.block_size = int(g.block_size)
+        self.num_stages = int(g.num_stages)
+        self.num_entries = int(g.num_entries)
+        self.num_groups = int(g.num_groups)
+        self.num_tiles = int(packed.num_tiles)
+        self.register_buffer("packed_ids", packed.packed_ids)
+        self.register_buffer("tile_table", packed.tile_table)
+        self.register_buffer("codebooks", packed.codebooks)
+        self.register_buffer("row_scale", packed.row_scale)
+
+    # -- C ABI plumbing -----------------------------------------------------
+    def layer_struct(self) -> _abi.Layer:
+        """The ``wal_rvq_layer`` descriptor of this module's current device buffers."""
+        key = (self.packed_ids.data_ptr(), self.tile_table.data_ptr(), self.codebooks.data_ptr(),
+               self.row_scale.data_ptr(), None if self.bias is None else self.bias.data_ptr())
+        if self._layer_cache is not None and self._layer_cache[0] == key:
+            return self._layer_cache[1]
+        geom = _abi.Geometry(out_features=self.out_features, in_features=self.in_features,
+                             block_size=self.block_size, num_stages=self.num_stages,
+                             num_entries=self.num_entries, num_groups=self.num_groups)
+        layer = _abi.Layer(geom=geom, num_tiles=self.num_tiles, packed_ids=key[0], tile_table=key[1],
+                           codebooks=key[2], row_scale=key[3], bias=key[4])
+        self._layer_cache = (key, layer)
+        return layer
+
+    def _require_cuda(self, x: Tensor) -> None:
+        if not x.is_cuda:
+            raise ValueError("PackedGroupedBlockRVQLinear runs on CUDA only (no CPU path); move the input "
+                             "and the module to a CUDA device")
+        if self.packed_ids.device != x.device:
+            raise ValueError(f"input on {x.device} but module buffers on {self.packed_ids.device}")
+
+    # -- public API ---------------------------------------------------------
+    def forward(self, x: Tensor) -> Tensor:
+        self._require_cuda(x)
+        if x.dtype != torch.bfloat16:
+            raise ValueError(f"PackedGroupedBlockRVQLinear expects bfloat16 activations, got {x.dtype}")
+        orig = x.shape
+        if orig[-1] != self.in_features:
+            raise ValueError(f"Feature mismatch: {orig[-1]} != {self.in_features}")
+        x2 = x.reshape(-1, self.in_features)
+        if x2.stride(-1) != 1 or x2.stride(0) % 4 != 0 or x2.data_ptr() % 8 != 0:
+            x2 = x2.contiguous()
+        M = x2.shape[0]
+        y = torch.empty((M, self.out_features), device=x.device, dtype=torch.bfloat16)
+        if M > 0:
+            self.gemv_into(x2, y)
+        return y.reshape(*orig[:-1], self.out_features)
+
+    def gemv_into(self, x2: Tensor, y: Tensor, *, warps_per_tile: int = 0, num_ctas: int = 0) -> None:
+        """y[M, N] <- x2[M, K] @ w^T (+ bias) through ``wal_rvq_gemv_ex`` on the current stream."""
+        lib = _abi.load()
+        layer = self.layer_struct()
+        with torch.cuda.device(x2.device):
+            st = lib.wal_rvq_gemv_ex(ctypes.byref(layer), x2.data_ptr(), x2.shape[0], x2.stride(0), y.data_ptr(),
+                                     y.stride(0), _abi.DTYPE_CODE[y.dtype], warps_per_tile, num_ctas,
+                                     _abi.stream_handle(x2.device))
+        _abi.check(st, "wal_rvq_gemv")
+
+    def reconstruct_weight(self, out_dtype: torch.dtype = torch.bfloat16) -> Tensor:
+        """Materialise the weight, bit-identical to the reference's bf16 reconstruction."""
+        if out_dtype != torch.bfloat16:
+            raise ValueError("reconstruct_weight supports torch.bfloat16 (the forward's weight dtype)")
+        dev = self.packed_ids.device
+        if dev.type != "cuda":
+            raise ValueError("reconstruct_weight runs on CUDA only; move the module to a CUDA device")
+        w = torch.empty((self.out_features, self.in_features), device=dev, dtype=torch.bfloat16)
+        lib = _abi.load()
+        with torch.cuda.device(dev):
+            st = lib.wal_rvq_dequant(ctypes.byref(self.layer_struct()), w.data_ptr(), w.stride(0),
+                                     _abi.stream_handle(dev))
+        _abi.check(st, "wal_rvq_dequant")
+        return w
+
+    def unpack_ids(self) -> Tensor:
+        """Packed stream read back on the device: ids [R, N, blocks] (uint8 or int16)."""
+        dev = self.packed_ids.device
+        if dev.type != "cuda":
+            raise ValueError("unpack_ids runs on CUDA only")
+        blocks = -(-self.in_features // self.block_size)
+        dtype = torch.uint8 if self.num_entries <= 256 else torch.int16
+        out = torch.empty((self.num_stages, self.out_features, blocks), device=dev, dtype=dtype)
+        lib = _abi.load()
+        with torch.cuda.device(dev):
+            st = lib.wal_rvq_unpack_ids(ctypes.byref(self.layer_struct()), out.data_ptr(), _abi.stream_handle(dev))
+        _abi.check(st, "wal_rvq_unpack_ids")
+        return out
+
+    def compressed_bytes(self) -> int:
+        """Bytes a decode GEMV must read for the weight: ids + codebooks + row scales (+ bias)."""
+        blocks = -(-self.in_features // self.block_size)
+        idw = 1 if self.num_entries <= 256 else 2
+        total = self.out_features * blocks * self.num_stages * idw
+        total += self.codebooks.numel() * 2 + self.out_features * 2
+        if self.bias is not None:
+            total += self.out_features * 2
+        return total
+
+    def extra_repr(self) -> str:
+        return (f"in_features={self.in_features}, out_features={self.out_features}, block_size={self.block_size}, "
+                f"num_stages={self.num_stages}, entries={self.num_entries}, groups={self.num_groups}, "
+                f"matmul_strategy={self.matmul_strategy}")
+
+
+class RouteCodebookLinear(PackedGroupedBlockRVQLinear):
+    """Route-codebook linear: per unit a route over G codebooks plus a code.
+
+    No module of this name exists in the reference; the format is the
+    one-stage special case of its Block-RVQ path (id = route * 256 + code into
+    the flattened ``[G * 256, d]`` codebook), so this class is a
+    ``PackedGroupedBlockRVQLinear`` whose ids are packed from route/code arrays.
+    """
+
+    @classmethod
+    def from_routes(cls, route: Tensor, code: Tensor, codebooks: Tensor, row_scale: Tensor,
+                    bias: Optional[Tensor] = None, *, in_features: int, **kwargs) -> "RouteCodebookLinear":
+        """Build from uint8 ``route``/``code`` ``[N, blocks]``, fp16 ``codebooks`` ``[G, 256, d]``, fp16 ``row_scale``."""
+        from .block_vq import route_code_encoding
+
+        packed = pack_routes(route, code, codebooks, row_scale, in_features)
+        enc = single_group(route_code_encoding(route, code, codebooks, row_scale, in_features=in_features))
+        return cls(enc, bias, _packed=packed, **kwargs)
+
+
+def _set_submodule(root: nn.Module, path: str, module: nn.Module) -> None:
+    parent = root
+    parts = path.split(".")
+    for part in parts[:-1]:
+        parent = getattr(parent, part)
+    setattr(parent, parts[-1], module)
+
+
+@torch.no_grad()
+def replace_with_preencoded_packed_block_rvq(
+    model: nn.Module,
+    encodings_by_name: dict[str, GroupedBlockRVQEncoding],
+    *,
+    matmul_strategy: str = "per_group",
+    device: Optional[torch.device] = None,
+    **strategy_kwargs,
+) -> list[dict[str, object]]:
+    """Swap named ``nn.Linear`` modules for packed modules built from encodings.
+
+    Mirrors reference ``src/runtime.py:2145-2200``: every ``nn.Linear`` whose
+    name is a key of ``encodings_by_name`` is replaced in place; the original
+    weight is released.  Returns one stats dict per replaced layer.
+    """
+    stats = []
+    for name, module in list(model.named_modules()):
+        if name not in encodings_by_name or not isinstance(module, nn.Linear):
+            continue
+        enc = encodings_by_name[name]
+        target = device if device is not None else module.weight.device
+        packed = PackedGroupedBlockRVQLinear(enc, module.bias, matmul_strategy=matmul_strategy,
+                                             **strategy_kwargs).to(target)
+        _set_submodule(model, name, packed)
+        stats.append({
+            "name": name,
+            "tensor_name": f"{name}.weight",
+            "runtime_decision": "preencoded_packed_block_rvq",
+            "matmul_strategy": matmul_strategy,
+            "storage_bytes": int(enc.storage_bytes()),
+            "bits_per_weight": float(enc.bits_per_weight()),
+        })
+    return stats
