@@ -65,7 +65,7 @@ __device__ __forceinline__ uint32_t rho_pair(uint16_t rho_bits) {
 }
 
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -74,7 +74,7 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
 
 __device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
   uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
                : "l"(p));
   return v;
@@ -82,7 +82,7 @@ __device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
 
 __device__ __forceinline__ uint2 lds_v2(uint32_t saddr) {
   uint2 v;
-  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(saddr));
+  asm("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(saddr) : "memory");
   return v;
 }
 
@@ -122,26 +122,50 @@ struct CbLayout {
   }
 };
 
+__device__ __forceinline__ void cp_async_16(uint32_t saddr, const void* gptr) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(saddr), "l"(gptr));
+}
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::); }
+
 // Stage R codebooks of one group (fp16 [R][entries][D] in global memory) into
-// shared memory.  One-stage tables are pre-rounded to bf16 (first rounding).
+// shared memory.  Every 16-byte run of an entry is fetched with cp.async into
+// its copy-0 position (all fetches in flight at once), then copy 0 is expanded
+// into the other copies; one-stage tables are pre-rounded to bf16 in place
+// (first rounding).  Caller brackets the call with __syncthreads().
 template <int D, int R, bool REPL>
 __device__ void stage_codebooks(uint8_t* cb, const uint16_t* __restrict__ books, int entries) {
   using L = CbLayout<D, REPL>;
   const int sb = L::stage_bytes(entries);
-  const int total = R * entries * L::kPieces;
-  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+  constexpr int kRuns = D / 8;  // 16-byte runs per entry (two pieces each)
+  const int total_runs = R * entries * kRuns;
+  const uint32_t base = smem_u32(cb);
+  for (int i = threadIdx.x; i < total_runs; i += blockDim.x) {
+    const int s = i / (entries * kRuns);
+    const int rem = i - s * entries * kRuns;
+    const int e = rem / kRuns;
+    const int run = rem - e * kRuns;
+    const uint16_t* src = books + ((size_t)s * entries + e) * D + 8 * run;
+    cp_async_16(base + s * sb + L::piece_offset(e, 2 * run, 0), src);
+  }
+  cp_async_wait_all();
+  if (R > 1 && !REPL) return;  // raw fp16 table, single copy: done
+  __syncthreads();
+  const int total_pieces = R * entries * L::kPieces;
+  for (int i = threadIdx.x; i < total_pieces; i += blockDim.x) {
     const int s = i / (entries * L::kPieces);
     const int rem = i - s * entries * L::kPieces;
     const int e = rem / L::kPieces;
     const int j = rem - e * L::kPieces;
-    uint2 v = *reinterpret_cast<const uint2*>(books + ((size_t)s * entries + e) * D + 4 * j);
+    uint8_t* sbase = cb + s * sb;
+    uint2 v = *reinterpret_cast<const uint2*>(sbase + L::piece_offset(e, j, 0));
     if (R == 1) {
       v.x = preround_pair(v.x);
       v.y = preround_pair(v.y);
+      *reinterpret_cast<uint2*>(sbase + L::piece_offset(e, j, 0)) = v;
     }
-    uint8_t* base = cb + s * sb;
 #pragma unroll
-    for (int c = 0; c < L::kCopies; ++c) *reinterpret_cast<uint2*>(base + L::piece_offset(e, j, c)) = v;
+    for (int c = 1; c < L::kCopies; ++c) *reinterpret_cast<uint2*>(sbase + L::piece_offset(e, j, c)) = v;
   }
 }
 

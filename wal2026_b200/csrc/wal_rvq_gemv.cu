@@ -64,7 +64,7 @@ __device__ __forceinline__ void store_out(void* y, long long idx, float v, int d
 
 // Process one chunk of one tile for one warp: D k-tiles of 16 columns.
 template <int D, int R, int IDW, bool REPL, int MT, bool MASK>
-__device__ __forceinline__ void gemv_chunk(float (&acc)[MT][4], const uint32_t (&c0)[R * IDW * 4],
+__device__ __forceinline__ void gemv_chunk(float (&acc)[2][MT][4], const uint32_t (&c0)[R * IDW * 4],
                                            const uint32_t (&c1)[R * IDW * 4], uint32_t cb_base, int stage_bytes,
                                            uint32_t rho_a, uint32_t rho_b, int qh_shift, const uint16_t* xrow0,
                                            const uint16_t* xrow1, bool xv0, bool xv1, int col_base, int K) {
@@ -83,8 +83,9 @@ __device__ __forceinline__ void gemv_chunk(float (&acc)[MT][4], const uint32_t (
     if (MASK && !in_k) {
       a[0] = a[1] = a[2] = a[3] = 0u;
     }
-    mma_bf16_16816(acc[0], a, xa.x, xa.y);
-    if (MT == 2) mma_bf16_16816(acc[MT - 1], a, xb.x, xb.y);
+    // even and odd k-tiles feed separate accumulators: two independent MMA chains
+    mma_bf16_16816(acc[kt & 1][0], a, xa.x, xa.y);
+    if (MT == 2) mma_bf16_16816(acc[kt & 1][MT - 1], a, xb.x, xb.y);
   });
 }
 
@@ -132,9 +133,11 @@ __global__ void __launch_bounds__(kThreads) rvq_gemv_kernel(GemvParams p) {
     while (n_here < slots && t + n_here < t_end && p.tiles[t + n_here].x == g) ++n_here;
     const long long my_t = t + slot;
     const bool active = slot < n_here;
-    float acc[MT][4];
+    float acc[2][MT][4];
 #pragma unroll
-    for (int i = 0; i < MT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int i = 0; i < MT; ++i) acc[h][i][0] = acc[h][i][1] = acc[h][i][2] = acc[h][i][3] = 0.f;
     int4 ti = make_int4(0, 0, 0, 0);
     if (active) {
       ti = p.tiles[my_t];
@@ -186,10 +189,10 @@ __global__ void __launch_bounds__(kThreads) rvq_gemv_kernel(GemvParams p) {
     float* wred = red + warp * 16 * MC;
 #pragma unroll
     for (int i = 0; i < MT; ++i) {
-      wred[r * MC + i * 8 + 2 * q] = acc[i][0];
-      wred[r * MC + i * 8 + 2 * q + 1] = acc[i][1];
-      wred[(r + 8) * MC + i * 8 + 2 * q] = acc[i][2];
-      wred[(r + 8) * MC + i * 8 + 2 * q + 1] = acc[i][3];
+      wred[r * MC + i * 8 + 2 * q] = acc[0][i][0] + acc[1][i][0];
+      wred[r * MC + i * 8 + 2 * q + 1] = acc[0][i][1] + acc[1][i][1];
+      wred[(r + 8) * MC + i * 8 + 2 * q] = acc[0][i][2] + acc[1][i][2];
+      wred[(r + 8) * MC + i * 8 + 2 * q + 1] = acc[0][i][3] + acc[1][i][3];
     }
     __syncthreads();
     const int per_slot = 16 * MC;
@@ -321,7 +324,7 @@ int check_layer(const wal_rvq_layer* L) {
     return WAL_ERR_UNSUPPORTED;
   if (g.in_features % 4 != 0) return WAL_ERR_UNSUPPORTED;
   if (!L->packed_ids || !L->tile_table || !L->codebooks || !L->row_scale) return WAL_ERR_INVALID_ARGUMENT;
-  if (((uintptr_t)L->packed_ids & 15) || ((uintptr_t)L->tile_table & 15) || ((uintptr_t)L->codebooks & 7))
+  if (((uintptr_t)L->packed_ids & 15) || ((uintptr_t)L->tile_table & 15) || ((uintptr_t)L->codebooks & 15))
     return WAL_ERR_ALIGNMENT;
   const bool repl = replicated(g.block_size, g.num_stages, g.num_entries);
   if (smem_bytes(g.block_size, g.num_stages, g.num_entries, repl, 2) > 227 * 1024) return WAL_ERR_UNSUPPORTED;
@@ -474,7 +477,9 @@ extern "C" int wal_rvq_gemv_ex(const wal_rvq_layer* layer, const uint16_t* x, in
     p.y = static_cast<uint8_t*>(y) + (size_t)(m0 * ldy) * ysz;
     p.M = mm;
     const int mt = mm <= 8 ? 1 : 2;
-    WAL_FOR_ALL_CONFIGS(dispatch_gemv, p, num_ctas, s, g.num_entries, repl, mt)
+    auto run = [&]() -> int { WAL_FOR_ALL_CONFIGS(dispatch_gemv, p, num_ctas, s, g.num_entries, repl, mt) };
+    const int rs = run();
+    if (rs != WAL_OK) return rs;
   }
   return WAL_OK;
 }
