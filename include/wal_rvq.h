@@ -66,7 +66,8 @@ typedef struct wal_rvq_geometry {
   int32_t num_groups;   /* row groups, each with its own R codebooks               */
 } wal_rvq_geometry;
 
-/* Device-resident packed linear.  All pointers are device pointers. */
+/* Device-resident packed linear.  All pointers are device pointers except
+ * group_rows, a host array (read during the call only). */
 typedef struct wal_rvq_layer {
   wal_rvq_geometry geom;
   int64_t num_tiles;          /* from wal_rvq_packed_size                            */
@@ -75,6 +76,7 @@ typedef struct wal_rvq_layer {
   const uint16_t* codebooks;  /* fp16 [num_groups][R][num_entries][d]                */
   const uint16_t* row_scale;  /* fp16 [N]                                            */
   const uint16_t* bias;       /* bf16 [N] or NULL                                    */
+  const int64_t* group_rows;  /* HOST [num_groups] rows per group; NULL if 1 group   */
 } wal_rvq_layer;
 
 /* Human-readable text for a status code (static storage). */
@@ -125,7 +127,7 @@ WAL_API int wal_route_pack(const wal_rvq_geometry* geom, const uint8_t* route, c
 /*
  * Decode GEMV (M <= 16 tokens): y[M, N] = x[M, K] @ w^T (+ bias).
  * x: device bf16, row stride ldx elements (ldx >= K, ldx % 4 == 0, 8-byte
- * aligned base).  y: device, row stride ldy elements, dtype y_dtype
+ * aligned base; ldx % 8 == 0 with a 16-byte aligned base is fastest).  y: device, row stride ldy elements, dtype y_dtype
  * (WAL_BF16: one rounding of the fp32 result; WAL_F32: the fp32 result).
  * Replaces reference src/runtime.py:1362-1507 (PackedGroupedBlockRVQLinear.forward)
  * and src/triton_id_matmul.py:220-306 (rvq_group_linear_matmul).

@@ -114,7 +114,7 @@ def test_every_token_count(M):
     assert_close(gemv_f32(mod, x).cpu().numpy(), ref)
 
 
-@pytest.mark.parametrize("wpt", [1, 2, 4, 8])
+@pytest.mark.parametrize("wpt", [1, 2, 4, 8, 16])
 @pytest.mark.parametrize("ctas", [0, 1, 3])
 def test_work_split_variants_agree(wpt, ctas):
     enc = synthetic.grouped_encoding([48, 40, 64], 1024, d=16, R=2, seed=5)

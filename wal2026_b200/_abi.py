@@ -55,6 +55,7 @@ class Layer(ctypes.Structure):
         ("codebooks", ctypes.c_void_p),
         ("row_scale", ctypes.c_void_p),
         ("bias", ctypes.c_void_p),
+        ("group_rows", ctypes.POINTER(ctypes.c_int64)),
     ]
 
 

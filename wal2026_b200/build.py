@@ -39,21 +39,45 @@ def _stale() -> bool:
     return any(p.stat().st_mtime > mtime for p in deps)
 
 
-def build(verbose: bool = False, extra: list[str] | None = None) -> Path:
-    cmd = [
-        _nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
-        "-Xcompiler", "-fvisibility=hidden", f"-I{INCLUDE}", "-o", str(LIB) + ".tmp",
-        *[str(s) for s in sources()], "-lcuda",
-    ]
-    if extra:
-        cmd[1:1] = extra
+# translation units: (source, extra defines).  The GEMV source is compiled once
+# per block size so the template instantiations build in parallel.
+def units() -> list[tuple[Path, list[str]]]:
+    out = []
+    for src in sources():
+        if src.name == "wal_rvq_gemv.cu":
+            out.append((src, ["-DWAL_UNIT_API"]))
+            out += [(src, [f"-DWAL_UNIT_D={d}"]) for d in (8, 16, 32)]
+        else:
+            out.append((src, []))
+    return out
+
+
+def _run(cmd: list[str], verbose: bool) -> str:
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
-        raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
-    if verbose and (res.stdout or res.stderr):
-        print(res.stdout + res.stderr, file=sys.stderr)
+        raise RuntimeError(f"nvcc failed ({res.returncode}): {' '.join(cmd)}\n{res.stdout}\n{res.stderr}")
+    return res.stdout + res.stderr
+
+
+def build(verbose: bool = False, extra: list[str] | None = None) -> Path:
+    from concurrent.futures import ThreadPoolExecutor
+
+    objdir = PKG / "_build"
+    objdir.mkdir(exist_ok=True)
+    common = [_nvcc(), *(extra or []), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
+              "-Xcompiler", "-fvisibility=hidden", f"-I{INCLUDE}"]
+    jobs = []
+    for i, (src, defs) in enumerate(units()):
+        obj = objdir / f"{src.stem}_{i}.o"
+        jobs.append((common + defs + ["-c", str(src), "-o", str(obj)], obj))
+    with ThreadPoolExecutor(max_workers=max(1, min(len(jobs), os.cpu_count() or 1))) as ex:
+        logs = list(ex.map(lambda j: _run(j[0], verbose), jobs))
+    if verbose:
+        print("".join(logs), file=sys.stderr)
+    link = [_nvcc(), *ARCH, "-shared", "-o", str(LIB) + ".tmp", *[str(o) for _, o in jobs], "-lcuda"]
+    _run(link, verbose)
     os.replace(str(LIB) + ".tmp", LIB)
     return LIB
 

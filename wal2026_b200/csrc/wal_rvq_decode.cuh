@@ -50,10 +50,18 @@ __device__ __forceinline__ uint32_t mul_bf16x2_rn(uint32_t a, uint32_t b) {
   return d;
 }
 
+// (a0, a1) += fp32 of the two fp16 halves of h2 (lo half -> a0), round-to-nearest.
+// The halves are split inside the asm so no 16-bit extraction is materialised.
+__device__ __forceinline__ void add2_f32_f16x2(float& a0, float& a1, uint32_t h2) {
+  asm("{\n .reg .f16 lo, hi;\n mov.b32 {lo, hi}, %2;\n add.rn.f32.f16 %0, lo, %0;\n add.rn.f32.f16 %1, hi, %1;\n}"
+      : "+f"(a0), "+f"(a1)
+      : "r"(h2));
+}
+
 // fp16 bits -> bf16 bits of bf16_rn(+0.0f + fp32(h)) (first rounding, one stage)
 __device__ __forceinline__ uint32_t preround_pair(uint32_t h2) {
-  const float lo = add_f32_f16((uint16_t)(h2 & 0xFFFFu), 0.0f);
-  const float hi = add_f32_f16((uint16_t)(h2 >> 16), 0.0f);
+  float lo = 0.0f, hi = 0.0f;
+  add2_f32_f16x2(lo, hi, h2);
   return pack_bf16x2_rn(lo, hi);
 }
 
@@ -126,95 +134,137 @@ __device__ __forceinline__ void cp_async_16(uint32_t saddr, const void* gptr) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(saddr), "l"(gptr));
 }
 
+__device__ __forceinline__ void cp_async_8(uint32_t saddr, const void* gptr) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(saddr), "l"(gptr));
+}
+
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::); }
 
 // Stage R codebooks of one group (fp16 [R][entries][D] in global memory) into
-// shared memory.  Every 16-byte run of an entry is fetched with cp.async into
-// its copy-0 position (all fetches in flight at once), then copy 0 is expanded
-// into the other copies; one-stage tables are pre-rounded to bf16 in place
-// (first rounding).  Caller brackets the call with __syncthreads().
+// shared memory, in two steps so the copies overlap other prologue work:
+//   stage_codebooks_issue  - every 16-byte run of an entry is fetched with
+//                            cp.async into its copy-0 position (not committed);
+//   stage_codebooks_finish - after the caller's cp.async wait + __syncthreads,
+//                            copy 0 is expanded into the other copies and
+//                            one-stage tables are pre-rounded to bf16 in place
+//                            (first rounding).  Follow it with __syncthreads().
+// `sb` is the byte stride between stages in shared memory.
 template <int D, int R, bool REPL>
-__device__ void stage_codebooks(uint8_t* cb, const uint16_t* __restrict__ books, int entries) {
+__device__ void stage_codebooks_issue(uint8_t* cb, const uint16_t* __restrict__ books, int entries, int sb) {
   using L = CbLayout<D, REPL>;
-  const int sb = L::stage_bytes(entries);
   constexpr int kRuns = D / 8;  // 16-byte runs per entry (two pieces each)
-  const int total_runs = R * entries * kRuns;
   const uint32_t base = smem_u32(cb);
-  for (int i = threadIdx.x; i < total_runs; i += blockDim.x) {
-    const int s = i / (entries * kRuns);
-    const int rem = i - s * entries * kRuns;
-    const int e = rem / kRuns;
-    const int run = rem - e * kRuns;
-    const uint16_t* src = books + ((size_t)s * entries + e) * D + 8 * run;
-    cp_async_16(base + s * sb + L::piece_offset(e, 2 * run, 0), src);
-  }
-  cp_async_wait_all();
-  if (R > 1 && !REPL) return;  // raw fp16 table, single copy: done
-  __syncthreads();
-  const int total_pieces = R * entries * L::kPieces;
-  for (int i = threadIdx.x; i < total_pieces; i += blockDim.x) {
-    const int s = i / (entries * L::kPieces);
-    const int rem = i - s * entries * L::kPieces;
-    const int e = rem / L::kPieces;
-    const int j = rem - e * L::kPieces;
-    uint8_t* sbase = cb + s * sb;
-    uint2 v = *reinterpret_cast<const uint2*>(sbase + L::piece_offset(e, j, 0));
-    if (R == 1) {
-      v.x = preround_pair(v.x);
-      v.y = preround_pair(v.y);
-      *reinterpret_cast<uint2*>(sbase + L::piece_offset(e, j, 0)) = v;
-    }
 #pragma unroll
-    for (int c = 1; c < L::kCopies; ++c) *reinterpret_cast<uint2*>(sbase + L::piece_offset(e, j, c)) = v;
+  for (int s = 0; s < R; ++s) {
+    const uint16_t* sbooks = books + (size_t)s * entries * D;
+    const uint32_t sbase = base + s * sb;
+    for (int e = threadIdx.x; e < entries; e += blockDim.x) {
+#pragma unroll
+      for (int run = 0; run < kRuns; ++run)
+        cp_async_16(sbase + L::piece_offset(e, 2 * run, 0), sbooks + (size_t)e * D + 8 * run);
+    }
   }
+}
+
+template <int D, int R, bool REPL>
+__device__ void stage_codebooks_finish(uint8_t* cb, int entries, int sb) {
+  using L = CbLayout<D, REPL>;
+  if (R > 1 && !REPL) return;  // raw fp16 table, single copy: nothing to do
+#pragma unroll
+  for (int s = 0; s < R; ++s) {
+    uint8_t* sbase = cb + s * sb;
+    for (int e = threadIdx.x; e < entries; e += blockDim.x) {
+#pragma unroll
+      for (int j = 0; j < L::kPieces; ++j) {
+        uint2 v = *reinterpret_cast<const uint2*>(sbase + L::piece_offset(e, j, 0));
+        if (R == 1) {
+          v.x = preround_pair(v.x);
+          v.y = preround_pair(v.y);
+          *reinterpret_cast<uint2*>(sbase + L::piece_offset(e, j, 0)) = v;
+        }
+#pragma unroll
+        for (int c = 1; c < L::kCopies; ++c) *reinterpret_cast<uint2*>(sbase + L::piece_offset(e, j, c)) = v;
+      }
+    }
+  }
+}
+
+// One-call staging for kernels without other prologue work.
+template <int D, int R, bool REPL>
+__device__ void stage_codebooks(uint8_t* cb, const uint16_t* __restrict__ books, int entries, int sb) {
+  stage_codebooks_issue<D, R, REPL>(cb, books, entries, sb);
+  cp_async_wait_all();
+  __syncthreads();
+  stage_codebooks_finish<D, R, REPL>(cb, entries, sb);
 }
 
 // ---------------------------------------------------------------------------
 // Id extraction from one row's chunk registers.
-// codes[v*4 + w] holds 32-bit word w of 16-byte vector v of this row's chunk.
-// Block-in-chunk for k-tile KT of a lane with q:
+// codes[v*4 + w] holds 32-bit word w of 16-byte vector v of this row's chunk
+// (vector v = stage * idw + half).  Block-in-chunk for k-tile KT of lane q:
 //   D = 8 : 2*KT + (q >> 1)      D = 16: KT      D = 32: KT >> 1
+// Lane-dependent byte selection (D = 8) goes through a precomputed
+// __byte_perm selector: sel8[KT & 1] = 0x4440 + (2*(KT&1) + (q>>1)) for 1-byte
+// ids, sel16 = (q>>1) ? 0x4432 : 0x4410 for 2-byte ids.
 // ---------------------------------------------------------------------------
-template <int D, int IDW, int KT, int S, int V>
-__device__ __forceinline__ uint32_t extract_id(const uint32_t (&codes)[V * 4], int qh_shift) {
+struct LaneSel {
+  uint32_t sel8[2];
+  uint32_t sel16;
+  __device__ explicit LaneSel(int q) {
+    const uint32_t qh = (uint32_t)(q >> 1);
+    sel8[0] = 0x4440u + qh;
+    sel8[1] = 0x4442u + qh;
+    sel16 = qh ? 0x4432u : 0x4410u;
+  }
+};
+
+template <int D, int IDW, int KT, int S, int NW>
+__device__ __forceinline__ uint32_t extract_id(const uint32_t (&codes)[NW], const LaneSel& ls) {
   if (IDW == 1) {
     if (D == 8) {
-      constexpr int b0 = 2 * KT;  // even; lane adds q>>1
-      constexpr int word = S * 4 + (b0 >> 2);
-      constexpr int sh = 8 * (b0 & 3);
-      return (codes[word] >> (sh + qh_shift)) & 0xFFu;  // qh_shift = 8*(q>>1)
+      return __byte_perm(codes[S * 4 + (KT >> 1)], 0u, ls.sel8[KT & 1]);
     } else {
       constexpr int b = (D == 16) ? KT : (KT >> 1);
-      constexpr int word = S * 4 + (b >> 2);
-      constexpr int sh = 8 * (b & 3);
-      return (codes[word] >> sh) & 0xFFu;
+      return __byte_perm(codes[S * 4 + (b >> 2)], 0u, 0x4440u + (b & 3));
     }
   } else {
     if (D == 8) {
       constexpr int b0 = 2 * KT;
-      constexpr int v = S * 2 + (b0 >> 3);
-      constexpr int word = v * 4 + ((b0 & 7) >> 1);
-      return (codes[word] >> (qh_shift << 1)) & 0xFFFFu;  // 16*(q>>1)
+      return __byte_perm(codes[(S * 2 + (b0 >> 3)) * 4 + ((b0 & 7) >> 1)], 0u, ls.sel16);
     } else {
       constexpr int b = (D == 16) ? KT : (KT >> 1);
-      constexpr int v = S * 2 + (b >> 3);
-      constexpr int word = v * 4 + ((b & 7) >> 1);
-      constexpr int sh = 16 * (b & 1);
-      return (codes[word] >> sh) & 0xFFFFu;
+      return __byte_perm(codes[(S * 2 + (b >> 3)) * 4 + ((b & 7) >> 1)], 0u, (b & 1) ? 0x4432u : 0x4410u);
     }
   }
 }
 
 // Decode the lane's two bf16x2 words of one row for k-tile KT:
-// out[0] = columns 4q, 4q+1; out[1] = columns 4q+2, 4q+3.
-template <int D, int R, int IDW, bool REPL, int KT, int V>
-__device__ __forceinline__ void decode_row(uint32_t (&out)[2], const uint32_t (&codes)[V * 4], uint32_t cb_base,
-                                           int stage_bytes, uint32_t rho2, int qh_shift) {
+// out[0] = columns 4q, 4q+1; out[1] = columns 4q+2, 4q+3 (both already
+// multiplied by the row scale with the second rounding).
+// cbl = shared codebook base + this lane's offset; SB = bytes per stage.
+template <int OFF>
+__device__ __forceinline__ uint2 lds64(uint32_t saddr) {
+  uint2 v;
+  asm("ld.shared.v2.u32 {%0,%1}, [%2+%3];" : "=r"(v.x), "=r"(v.y) : "r"(saddr), "n"(OFF));
+  return v;
+}
+
+// Ordered variant for buffers written earlier in the kernel (activations).
+template <int OFF>
+__device__ __forceinline__ uint2 lds64_ordered(uint32_t saddr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.u32 {%0,%1}, [%2+%3];" : "=r"(v.x), "=r"(v.y) : "r"(saddr), "n"(OFF));
+  return v;
+}
+
+template <int D, int R, int IDW, bool REPL, int KT, int NW, int SB>
+__device__ __forceinline__ void decode_row(uint32_t (&out)[2], const uint32_t (&codes)[NW], uint32_t cbl,
+                                           uint32_t rho2, const LaneSel& ls) {
   using L = CbLayout<D, REPL>;
   constexpr int half_off = (D == 32) ? (KT & 1) * L::kHalfStride : 0;
   if (R == 1) {
-    const uint32_t id = extract_id<D, IDW, KT, 0, V>(codes, qh_shift);
-    const uint2 p = lds_v2(cb_base + id * L::kEntryStride + half_off);
+    const uint32_t id = extract_id<D, IDW, KT, 0, NW>(codes, ls);
+    const uint2 p = lds64<half_off>(cbl + id * L::kEntryStride);
     out[0] = mul_bf16x2_rn(p.x, rho2);
     out[1] = mul_bf16x2_rn(p.y, rho2);
   } else {
@@ -222,15 +272,17 @@ __device__ __forceinline__ void decode_row(uint32_t (&out)[2], const uint32_t (&
 #pragma unroll
     for (int s = 0; s < R; ++s) {
       uint32_t id;
-      if (s == 0) id = extract_id<D, IDW, KT, 0, V>(codes, qh_shift);
-      if (s == 1) id = extract_id<D, IDW, KT, 1, V>(codes, qh_shift);
-      if (s == 2) id = extract_id<D, IDW, KT, 2, V>(codes, qh_shift);
-      if (s == 3) id = extract_id<D, IDW, KT, 3, V>(codes, qh_shift);
-      const uint2 p = lds_v2(cb_base + s * stage_bytes + id * L::kEntryStride + half_off);
-      s0 = add_f32_f16((uint16_t)(p.x & 0xFFFFu), s0);
-      s1 = add_f32_f16((uint16_t)(p.x >> 16), s1);
-      s2 = add_f32_f16((uint16_t)(p.y & 0xFFFFu), s2);
-      s3 = add_f32_f16((uint16_t)(p.y >> 16), s3);
+      if (s == 0) id = extract_id<D, IDW, KT, 0, NW>(codes, ls);
+      if (s == 1) id = extract_id<D, IDW, KT, 1, NW>(codes, ls);
+      if (s == 2) id = extract_id<D, IDW, KT, 2, NW>(codes, ls);
+      if (s == 3) id = extract_id<D, IDW, KT, 3, NW>(codes, ls);
+      uint2 p;
+      if (s == 0) p = lds64<0 * SB + half_off>(cbl + id * L::kEntryStride);
+      if (s == 1) p = lds64<1 * SB + half_off>(cbl + id * L::kEntryStride);
+      if (s == 2) p = lds64<2 * SB + half_off>(cbl + id * L::kEntryStride);
+      if (s == 3) p = lds64<3 * SB + half_off>(cbl + id * L::kEntryStride);
+      add2_f32_f16x2(s0, s1, p.x);
+      add2_f32_f16x2(s2, s3, p.y);
     }
     out[0] = mul_bf16x2_rn(pack_bf16x2_rn(s0, s1), rho2);
     out[1] = mul_bf16x2_rn(pack_bf16x2_rn(s2, s3), rho2);

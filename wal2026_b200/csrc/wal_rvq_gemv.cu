@@ -2,16 +2,20 @@
 // packed-id unpacking for the Block-RVQ runtime linear.
 //
 // GEMV structure (one persistent wave of CTAs, 8 warps each):
-//   * a CTA owns a contiguous range of 16-row tiles and stages the codebooks
-//     of the tile's row group in shared memory (restaged only when the group
-//     changes);
-//   * each tile's 16-block chunks are split over `wpt` warps (K split); a warp
-//     streams its chunks' ids from HBM with 16-byte no-allocate loads
-//     (prefetching the next chunk), decodes every weight exactly in registers
-//     and feeds mma.sync m16n8k16 (bf16, fp32 accumulate) with the activation
-//     fragment, so the dense weight never exists;
-//   * the partial sums of the wpt warps are reduced in shared memory in a
-//     fixed order, the bias is added in fp32 and y is written once.
+//   * every CTA works inside one row group: it stages that group's codebooks
+//     in shared memory once (cp.async) and, when they fit, the activations;
+//   * the CTA's tiles are processed in rounds of `slots` tiles; the 16-block
+//     chunks of a tile are split over `wpt` warps (slots * wpt = 8);
+//   * each warp walks its own flat list of (tile, chunk) items with a
+//     kRing-deep cp.async ring in shared memory, so id loads for later items
+//     are in flight while the current one is decoded (no spin-waits: the copy
+//     engine's group counters are the only synchronisation);
+//   * every weight is decoded exactly in registers (wal_rvq_decode.cuh) and
+//     fed to mma.sync m16n8k16 (bf16, fp32 accumulate) with the activation
+//     fragment: the dense weight never exists;
+//   * the wpt warps of a slot reduce their partial sums through shared memory
+//     behind a named barrier of their own, in a fixed order, add the bias in
+//     fp32 and write y once.
 // Replaces reference src/runtime.py:1501-1507 (reconstruct + F.linear) and the
 // fused Triton kernel src/triton_id_matmul.py:143-217.
 #include "../../include/wal_rvq.h"
@@ -21,18 +25,8 @@
 #include <type_traits>
 
 namespace wal {
-namespace {
 
-template <int I, int N, typename F>
-__device__ __forceinline__ void static_for(F&& f) {
-  if constexpr (I < N) {
-    f(std::integral_constant<int, I>{});
-    static_for<I + 1, N>(f);
-  }
-}
-
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
+constexpr int kMaxGroups = 64;
 
 struct GemvParams {
   const uint8_t* packed;
@@ -50,7 +44,27 @@ struct GemvParams {
   int M;
   int y_dtype;
   int wpt;
+  int num_groups;
+  int pdl;                               // launched with programmatic dependent launch
+  int group_tile_start[kMaxGroups + 1];  // first tile of each group, plus the total
+  int group_row_start[kMaxGroups + 1];   // first output row of each group, plus N
 };
+
+namespace {
+
+template <int I, int N, typename F>
+__device__ __forceinline__ void static_for(F&& f) {
+  if constexpr (I < N) {
+    f(std::integral_constant<int, I>{});
+    static_for<I + 1, N>(f);
+  }
+}
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kRing = 4;  // chunks in flight per warp (power of two)
+constexpr int kXSmemBudget = 64 * 1024;
+
 
 __device__ __forceinline__ void store_out(void* y, long long idx, float v, int dtype) {
   if (dtype == WAL_F32) {
@@ -62,23 +76,96 @@ __device__ __forceinline__ void store_out(void* y, long long idx, float v, int d
   }
 }
 
-// Process one chunk of one tile for one warp: D k-tiles of 16 columns.
-template <int D, int R, int IDW, bool REPL, int MT, bool MASK>
+__device__ __forceinline__ void named_barrier(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// Which group and tile range a CTA owns.  CTAs are dealt to groups in
+// proportion to their tile counts (at least one per group); inside a group the
+// tiles are split evenly.  Identical arithmetic in every CTA.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void grid_dependents_launch() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
+__device__ void cta_range(const GemvParams& p, int cta, int ctas, int* group, long long* tb, long long* te) {
+  const int G = p.num_groups;
+  const long long T = p.group_tile_start[G];
+  int assigned = 0;
+  for (int g = 0; g < G; ++g) {
+    const long long tg = p.group_tile_start[g + 1] - p.group_tile_start[g];
+    long long cum = (long long)((double)ctas * (double)p.group_tile_start[g + 1] / (double)T + 0.5);
+    if (cum < g + 1) cum = g + 1;
+    if (cum > ctas - (G - 1 - g)) cum = ctas - (G - 1 - g);
+    if (g == G - 1) cum = ctas;
+    const int n = (int)cum - assigned;
+    if (cta < cum) {
+      const int local = cta - assigned;
+      *group = g;
+      *tb = p.group_tile_start[g] + tg * local / n;
+      *te = p.group_tile_start[g] + tg * (local + 1) / n;
+      return;
+    }
+    assigned = (int)cum;
+  }
+  *group = 0;
+  *tb = *te = 0;
+}
+
+template <int D, int R, int IDW, bool REPL, int MT, bool XS>
+struct GemvCfg {
+  using L = CbLayout<D, REPL>;
+  // one CTA of 16 warps per SM shares one staged codebook
+  static constexpr int kW = 16;
+  static constexpr int kT = kW * 32;
+  static constexpr int V = R * IDW;               // 16-byte vectors per row-chunk
+  static constexpr int NW = V * 4;                // 32-bit code words per row-chunk
+  static constexpr int SB = L::stage_bytes(256);  // stage stride (R > 1 implies <= 256 entries)
+  static constexpr int kStageBytes = V * 256;     // one chunk of one tile (16 rows)
+  static constexpr int MC = MT * 8;
+  __host__ __device__ static int cb_bytes(int entries) { return R > 1 ? R * SB : L::stage_bytes(entries); }
+  // activations: M rows plus one zero row that lanes beyond M read; the row
+  // stride is padded by 32 bytes so rows read together fall in different banks
+  __host__ __device__ static int x_stride(int kpad) { return kpad * 2 + 32; }
+  __host__ __device__ static int x_bytes(int M, int kpad) {
+    return XS ? (((M + 1) * x_stride(kpad) + 127) / 128) * 128 : 0;
+  }
+  __host__ __device__ static int ring_bytes() { return kW * kRing * kStageBytes; }
+  __host__ __device__ static int red_bytes() { return 2 * kW * 16 * MC * 4; }
+  __host__ __device__ static int smem(int entries, int M, int kpad) {
+    return cb_bytes(entries) + x_bytes(M, kpad) + ring_bytes() + red_bytes();
+  }
+};
+
+template <int D, int R, int IDW, bool REPL, int MT, bool XS, bool MASK>
 __device__ __forceinline__ void gemv_chunk(float (&acc)[2][MT][4], const uint32_t (&c0)[R * IDW * 4],
-                                           const uint32_t (&c1)[R * IDW * 4], uint32_t cb_base, int stage_bytes,
-                                           uint32_t rho_a, uint32_t rho_b, int qh_shift, const uint16_t* xrow0,
-                                           const uint16_t* xrow1, bool xv0, bool xv1, int col_base, int K) {
-  constexpr int V = R * IDW;
+                                           const uint32_t (&c1)[R * IDW * 4], uint32_t cbl, uint32_t rho_a,
+                                           uint32_t rho_b, const LaneSel& ls, const uint16_t* xrow0,
+                                           const uint16_t* xrow1, uint32_t xs0, uint32_t xs1, bool xv0, bool xv1,
+                                           int col_base, int K) {
+  using C = GemvCfg<D, R, IDW, REPL, MT, XS>;
   static_for<0, D>([&](auto ktc) {
     constexpr int kt = decltype(ktc)::value;
     uint32_t ra[2], rb[2];
-    decode_row<D, R, IDW, REPL, kt, V>(ra, c0, cb_base, stage_bytes, rho_a, qh_shift);
-    decode_row<D, R, IDW, REPL, kt, V>(rb, c1, cb_base, stage_bytes, rho_b, qh_shift);
+    decode_row<D, R, IDW, REPL, kt, C::NW, C::SB>(ra, c0, cbl, rho_a, ls);
+    decode_row<D, R, IDW, REPL, kt, C::NW, C::SB>(rb, c1, cbl, rho_b, ls);
     const int col = col_base + kt * 16;  // lane's first physical column (includes 4q)
     uint2 xa = make_uint2(0u, 0u), xb = make_uint2(0u, 0u);
     const bool in_k = !MASK || col < K;
-    if (xv0 && in_k) xa = __ldg(reinterpret_cast<const uint2*>(xrow0 + col));
-    if (MT == 2 && xv1 && in_k) xb = __ldg(reinterpret_cast<const uint2*>(xrow1 + col));
+    if (XS) {  // rows beyond M read the zero row: no predicate
+      xa = lds64_ordered<kt * 32>(xs0 + col_base * 2);
+      if (MT == 2) xb = lds64_ordered<kt * 32>(xs1 + col_base * 2);
+    } else {
+      if (xv0 && in_k) xa = __ldg(reinterpret_cast<const uint2*>(xrow0 + col));
+      if (MT == 2 && xv1 && in_k) xb = __ldg(reinterpret_cast<const uint2*>(xrow1 + col));
+    }
     uint32_t a[4] = {ra[0], rb[0], ra[1], rb[1]};
     if (MASK && !in_k) {
       a[0] = a[1] = a[2] = a[3] = 0u;
@@ -89,104 +176,199 @@ __device__ __forceinline__ void gemv_chunk(float (&acc)[2][MT][4], const uint32_
   });
 }
 
-template <int D, int R, int IDW, bool REPL, int MT>
-__global__ void __launch_bounds__(kThreads) rvq_gemv_kernel(GemvParams p) {
+template <int D, int R, int IDW, bool REPL, int MT, bool XS>
+__global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
+    rvq_gemv_kernel(const __grid_constant__ GemvParams p) {
+  using C = GemvCfg<D, R, IDW, REPL, MT, XS>;
+  constexpr int kWarps = C::kW;
+  constexpr int kThreads = C::kT;
+  using L = typename C::L;
+  constexpr int V = C::V;
+  constexpr int MC = C::MC;
   extern __shared__ __align__(128) uint8_t smem[];
-  using L = CbLayout<D, REPL>;
-  constexpr int V = R * IDW;
-  const int sb = L::stage_bytes(p.entries);
+  const int kpad = p.chunks * kChunkBlocks * D;
   uint8_t* cb = smem;
-  float* red = reinterpret_cast<float*>(smem + R * sb);  // [kWarps][16][MT*8]
+  uint16_t* xs = reinterpret_cast<uint16_t*>(smem + C::cb_bytes(p.entries));
+  uint8_t* ring = smem + C::cb_bytes(p.entries) + C::x_bytes(p.M, kpad);
+  float* red = reinterpret_cast<float*>(ring + C::ring_bytes());  // [2][kW][16][MC]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, q = lane & 3;
   const int wpt = p.wpt;
   const int slots = kWarps / wpt;
   const int slot = warp / wpt, kpart = warp - slot * wpt;
-  const int qh_shift = 8 * (q >> 1);
-  const uint32_t cb_base = smem_u32(cb) + L::lane_offset(r, q);
-  // first physical column of this lane inside a chunk's first k-tile (for d = 8
-  // this is block q>>1, piece q&1: 8*(q>>1) + 4*(q&1) = 4q)
-  const int lane_col = 4 * q;
+  const LaneSel ls(q);
+
+  int group;
+  long long tb, te;
+  cta_range(p, blockIdx.x, gridDim.x, &group, &tb, &te);
+  if (tb >= te) {
+    if (p.pdl) grid_dependents_launch();
+    return;
+  }
+  const long long g_tile0 = p.group_tile_start[group];
+  const int g_row0 = p.group_row_start[group], g_row1 = p.group_row_start[group + 1];
+
+  // -- this warp's flat item list: rounds of `slots` tiles x its chunks -----
+  const int cpw = kpart < p.chunks ? (p.chunks - kpart + wpt - 1) / wpt : 0;  // chunks per tile
+  const long long ntiles = te - tb;
+  const long long rounds = (ntiles + slots - 1) / slots;
+  // tiles this warp owns: tb + slot + k * slots, k < my_rounds
+  const long long my_rounds = slot < ntiles ? (ntiles - slot + slots - 1) / slots : 0;
+  const long long items = my_rounds * cpw;
   const long long tile_bytes = (long long)p.chunks * V * 256;
-  const long long G = gridDim.x;
-  const long long t_begin = (p.num_tiles * blockIdx.x) / G;
-  const long long t_end = (p.num_tiles * (blockIdx.x + 1)) / G;
+  uint8_t* wring = ring + warp * kRing * C::kStageBytes;
+
+  // issue cursor: the next item's source (advanced incrementally), items left
+  // to issue, position inside the tile's chunk list, ring slot
+  constexpr int kLaneCopies = (C::kStageBytes + 511) / 512;  // 16-byte copies per lane per chunk
+  const bool copy_lane = lane * 16 < C::kStageBytes;
+  const uint8_t* is_src = p.packed + (tb + slot) * tile_bytes + (long long)kpart * V * 256 + lane * 16;
+  const long long step_chunk = (long long)wpt * V * 256;
+  const long long step_tile = (long long)slots * tile_bytes - (long long)cpw * step_chunk;
+  const uint32_t ring_lane = smem_u32(wring) + lane * 16;
+  long long is_left = items;
+  int is_j = 0;
+  uint32_t is_slot = 0;
+  auto issue = [&]() {
+    if (is_left > 0) {
+      if (copy_lane) {
+#pragma unroll
+        for (int k = 0; k < kLaneCopies; ++k)
+          cp_async_16(ring_lane + is_slot * C::kStageBytes + k * 512, is_src + k * 512);
+      }
+      --is_left;
+      is_src += step_chunk;
+      if (++is_j == cpw) {
+        is_j = 0;
+        is_src += step_tile;
+      }
+    }
+    is_slot = (is_slot + 1) & (kRing - 1);
+    cp_async_commit();
+  };
+
+  // -- prologue: weights (static) first, activations after the dependency --
+  // group 0: codebooks (+ activations); groups 1..kRing-1: the first id chunks
+  stage_codebooks_issue<D, R, REPL>(cb, p.codebooks + (size_t)group * R * p.entries * D, p.entries,
+                                    R > 1 ? C::SB : L::stage_bytes(p.entries));
+  if (p.pdl) grid_dependency_wait();  // x (and y) belong to the previous kernel in the stream
+  if (XS) {
+    // rows m < M, columns [0, kpad): zero beyond K
+    const int vec_per_row = kpad / 8;  // 16-byte vectors
+    for (int i = threadIdx.x; i < (p.M + 1) * vec_per_row; i += kThreads) {
+      const int m = i / vec_per_row, v = i - m * vec_per_row;
+      uint16_t* dst = xs + (size_t)m * (C::x_stride(kpad) / 2) + v * 8;
+      if (m == p.M) {  // the zero row
+        *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+        continue;
+      }
+      const int col = v * 8;
+      const uint16_t* src = p.x + (long long)m * p.ldx + col;
+      if (col + 8 <= p.K && ((uintptr_t)src & 15) == 0) {
+        cp_async_16((uint32_t)__cvta_generic_to_shared(dst), src);
+      } else if (col + 8 <= p.K) {
+        cp_async_8((uint32_t)__cvta_generic_to_shared(dst), src);
+        cp_async_8((uint32_t)__cvta_generic_to_shared(dst + 4), src + 4);
+      } else {
+        for (int j = 0; j < 8; ++j) dst[j] = col + j < p.K ? p.x[(long long)m * p.ldx + col + j] : (uint16_t)0;
+      }
+    }
+  }
+  cp_async_commit();
+#pragma unroll 1
+  for (int s = 0; s < kRing - 1; ++s) issue();
+  cp_async_wait<kRing - 1>();  // group 0 landed
+  __syncthreads();
+  stage_codebooks_finish<D, R, REPL>(cb, p.entries, R > 1 ? C::SB : L::stage_bytes(p.entries));
+  __syncthreads();
+
   const int m0 = r, m1 = 8 + r;
   const bool xv0 = m0 < p.M, xv1 = (MT == 2) && (m1 < p.M);
   const uint16_t* xrow0 = p.x + (long long)(xv0 ? m0 : 0) * p.ldx;
   const uint16_t* xrow1 = p.x + (long long)(xv1 ? m1 : 0) * p.ldx;
-  const int kpad = p.chunks * kChunkBlocks * D;
+  const uint32_t xs0 = smem_u32(xs) + (uint32_t)((xv0 ? m0 : p.M) * C::x_stride(kpad));
+  const uint32_t xs1 = smem_u32(xs) + (uint32_t)((xv1 ? m1 : p.M) * C::x_stride(kpad));
   const bool need_mask = kpad != p.K;
+  const uint32_t cbl = smem_u32(cb) + L::lane_offset(r, q);
 
-  int cur_group = -1;
-  long long t = t_begin;
-  while (t < t_end) {
-    const int g = p.tiles[t].x;
-    if (g != cur_group) {
-      __syncthreads();
-      stage_codebooks<D, R, REPL>(cb, p.codebooks + (size_t)g * R * p.entries * D, p.entries);
-      __syncthreads();
-      cur_group = g;
-    }
-    int n_here = 1;
-    while (n_here < slots && t + n_here < t_end && p.tiles[t + n_here].x == g) ++n_here;
-    const long long my_t = t + slot;
-    const bool active = slot < n_here;
+  // row scales of a tile: tile t covers rows g_row0 + 16 * (t - g_tile0) ...
+  auto tile_rows = [&](long long t, int* row0, int* nrows) {
+    *row0 = g_row0 + (int)(16 * (t - g_tile0));
+    const int left = g_row1 - *row0;
+    *nrows = left < 16 ? left : 16;
+  };
+  uint32_t nrho_a = 0u, nrho_b = 0u;
+  if (my_rounds > 0) {
+    int row0, nrows;
+    tile_rows(tb + slot, &row0, &nrows);
+    nrho_a = r < nrows ? rho_pair(p.row_scale[row0 + r]) : 0u;
+    nrho_b = r + 8 < nrows ? rho_pair(p.row_scale[row0 + r + 8]) : 0u;
+  }
+
+  long long it = 0;
+  for (long long k = 0; k < rounds; ++k) {
+    const bool slot_live = k < my_rounds;  // same for all warps of a slot
     float acc[2][MT][4];
 #pragma unroll
     for (int h = 0; h < 2; ++h)
 #pragma unroll
       for (int i = 0; i < MT; ++i) acc[h][i][0] = acc[h][i][1] = acc[h][i][2] = acc[h][i][3] = 0.f;
-    int4 ti = make_int4(0, 0, 0, 0);
-    if (active) {
-      ti = p.tiles[my_t];
-      const int row0 = ti.y, nrows = ti.z;
-      const uint32_t rho_a = r < nrows ? rho_pair(p.row_scale[row0 + r]) : 0u;
-      const uint32_t rho_b = r + 8 < nrows ? rho_pair(p.row_scale[row0 + r + 8]) : 0u;
-      const uint8_t* tbase = p.packed + my_t * tile_bytes;
-      uint32_t cur0[V * 4], cur1[V * 4], nxt0[V * 4], nxt1[V * 4];
-      int c = kpart;
-      if (c < p.chunks) {
+    int row0 = 0, nrows = 0;
+    if (slot_live) {
+      tile_rows(tb + slot + k * slots, &row0, &nrows);
+      const uint32_t rho_a = nrho_a, rho_b = nrho_b;
+      if (k + 1 < my_rounds) {  // prefetch the next round's row scales
+        int nr0, nn;
+        tile_rows(tb + slot + (k + 1) * slots, &nr0, &nn);
+        nrho_a = r < nn ? rho_pair(p.row_scale[nr0 + r]) : 0u;
+        nrho_b = r + 8 < nn ? rho_pair(p.row_scale[nr0 + r + 8]) : 0u;
+      }
+      for (int j = 0; j < cpw; ++j, ++it) {
+        cp_async_wait<kRing - 2>();
+        __syncwarp();
+        const uint8_t* st = wring + (int)(it & (kRing - 1)) * C::kStageBytes;
+        uint32_t c0[V * 4], c1[V * 4];
 #pragma unroll
         for (int v = 0; v < V; ++v) {
-          const uint4 a = ldg_stream_v4(tbase + ((long long)c * V + v) * 256 + r * 16);
-          const uint4 b = ldg_stream_v4(tbase + ((long long)c * V + v) * 256 + (r + 8) * 16);
-          cur0[4 * v] = a.x; cur0[4 * v + 1] = a.y; cur0[4 * v + 2] = a.z; cur0[4 * v + 3] = a.w;
-          cur1[4 * v] = b.x; cur1[4 * v + 1] = b.y; cur1[4 * v + 2] = b.z; cur1[4 * v + 3] = b.w;
+          const uint4 a = *reinterpret_cast<const uint4*>(st + v * 256 + r * 16);
+          const uint4 b = *reinterpret_cast<const uint4*>(st + v * 256 + (r + 8) * 16);
+          c0[4 * v] = a.x; c0[4 * v + 1] = a.y; c0[4 * v + 2] = a.z; c0[4 * v + 3] = a.w;
+          c1[4 * v] = b.x; c1[4 * v + 1] = b.y; c1[4 * v + 2] = b.z; c1[4 * v + 3] = b.w;
         }
-      }
-      for (; c < p.chunks; c += wpt) {
-        const int cn = c + wpt;
-        if (cn < p.chunks) {
-#pragma unroll
-          for (int v = 0; v < V; ++v) {
-            const uint4 a = ldg_stream_v4(tbase + ((long long)cn * V + v) * 256 + r * 16);
-            const uint4 b = ldg_stream_v4(tbase + ((long long)cn * V + v) * 256 + (r + 8) * 16);
-            nxt0[4 * v] = a.x; nxt0[4 * v + 1] = a.y; nxt0[4 * v + 2] = a.z; nxt0[4 * v + 3] = a.w;
-            nxt1[4 * v] = b.x; nxt1[4 * v + 1] = b.y; nxt1[4 * v + 2] = b.z; nxt1[4 * v + 3] = b.w;
-          }
-        }
-        const int col_base = c * kChunkBlocks * D + lane_col;
+        __syncwarp();
+        issue();
+        const int c = kpart + j * wpt;
+        const int col_base = c * kChunkBlocks * D + 4 * q;
         if (need_mask && c == p.chunks - 1) {
-          gemv_chunk<D, R, IDW, REPL, MT, true>(acc, cur0, cur1, cb_base, sb, rho_a, rho_b, qh_shift, xrow0, xrow1,
-                                                xv0, xv1, col_base, p.K);
+          gemv_chunk<D, R, IDW, REPL, MT, XS, true>(acc, c0, c1, cbl, rho_a, rho_b, ls, xrow0, xrow1, xs0, xs1, xv0,
+                                                    xv1, col_base, p.K);
         } else {
-          gemv_chunk<D, R, IDW, REPL, MT, false>(acc, cur0, cur1, cb_base, sb, rho_a, rho_b, qh_shift, xrow0,
-                                                 xrow1, xv0, xv1, col_base, p.K);
-        }
-        if (cn < p.chunks) {
-#pragma unroll
-          for (int i = 0; i < V * 4; ++i) {
-            cur0[i] = nxt0[i];
-            cur1[i] = nxt1[i];
-          }
+          gemv_chunk<D, R, IDW, REPL, MT, XS, false>(acc, c0, c1, cbl, rho_a, rho_b, ls, xrow0, xrow1, xs0, xs1,
+                                                     xv0, xv1, col_base, p.K);
         }
       }
     }
-    // partial sums -> shared memory: red[warp][row][m]
-    constexpr int MC = MT * 8;
-    float* wred = red + warp * 16 * MC;
+    if (p.pdl && k + 1 == rounds) grid_dependents_launch();
+    // -- reduce the slot's wpt partial sums, add bias, write y ---------------
+    if (!slot_live) continue;
+    if (wpt == 1) {
+#pragma unroll
+      for (int i = 0; i < MT; ++i) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int row = r + (e >= 2 ? 8 : 0);
+          const int m = i * 8 + 2 * q + (e & 1);
+          if (row < nrows && m < p.M) {
+            float v = acc[0][i][e] + acc[1][i][e];
+            if (p.bias) v += __bfloat162float(__ushort_as_bfloat16(p.bias[row0 + row]));
+            store_out(p.y, (long long)m * p.ldy + row0 + row, v, p.y_dtype);
+          }
+        }
+      }
+      continue;
+    }
+    float* wred = red + ((int)(k & 1) * kWarps + warp) * 16 * MC;
 #pragma unroll
     for (int i = 0; i < MT; ++i) {
       wred[r * MC + i * 8 + 2 * q] = acc[0][i][0] + acc[1][i][0];
@@ -194,83 +376,70 @@ __global__ void __launch_bounds__(kThreads) rvq_gemv_kernel(GemvParams p) {
       wred[(r + 8) * MC + i * 8 + 2 * q] = acc[0][i][2] + acc[1][i][2];
       wred[(r + 8) * MC + i * 8 + 2 * q + 1] = acc[0][i][3] + acc[1][i][3];
     }
-    __syncthreads();
-    const int per_slot = 16 * MC;
-    for (int e = threadIdx.x; e < n_here * per_slot; e += kThreads) {
-      const int s = e / per_slot;
-      const int rem = e - s * per_slot;
-      const int row = rem / MC, m = rem - row * MC;
-      const int4 tt = p.tiles[t + s];
-      if (row >= tt.z || m >= p.M) continue;
+    named_barrier(1 + slot, wpt * 32);
+    const float* sred = red + ((int)(k & 1) * kWarps + slot * wpt) * 16 * MC;
+    const int tid = kpart * 32 + lane;
+    for (int e = tid; e < 16 * MC; e += wpt * 32) {
+      const int row = e / MC, m = e - row * MC;
+      if (row >= nrows || m >= p.M) continue;
       float v = 0.f;
-      for (int w = 0; w < wpt; ++w) v += red[((s * wpt + w) * 16 + row) * MC + m];
-      const int orow = tt.y + row;
+      for (int w = 0; w < wpt; ++w) v += sred[(w * 16 + row) * MC + m];
+      const int orow = row0 + row;
       if (p.bias) v += __bfloat162float(__ushort_as_bfloat16(p.bias[orow]));
       store_out(p.y, (long long)m * p.ldy + orow, v, p.y_dtype);
     }
-    __syncthreads();
-    t += n_here;
   }
+  cp_async_wait<0>();
 }
 
-// Weight materialisation: same decode path, fragments stored instead of fed
-// to the tensor cores.  One warp per tile, all chunks.
+// Weight materialisation through the same decode path: fragments stored
+// instead of fed to the tensor cores.  One warp per tile.
 template <int D, int R, int IDW, bool REPL>
-__global__ void __launch_bounds__(kThreads) rvq_dequant_kernel(GemvParams p, uint16_t* w, long long ldw) {
+__global__ void __launch_bounds__(kThreads) rvq_dequant_kernel(const __grid_constant__ GemvParams p, uint16_t* w,
+                                                               long long ldw) {
+  using C = GemvCfg<D, R, IDW, REPL, 1, false>;
+  using L = typename C::L;
+  constexpr int V = C::V;
   extern __shared__ __align__(128) uint8_t smem[];
-  using L = CbLayout<D, REPL>;
-  constexpr int V = R * IDW;
-  const int sb = L::stage_bytes(p.entries);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, q = lane & 3;
-  const int qh_shift = 8 * (q >> 1);
-  const uint32_t cb_base = smem_u32(smem) + L::lane_offset(r, q);
+  const LaneSel ls(q);
+  int group;
+  long long tb, te;
+  cta_range(p, blockIdx.x, gridDim.x, &group, &tb, &te);
+  if (tb >= te) return;
+  stage_codebooks<D, R, REPL>(smem, p.codebooks + (size_t)group * R * p.entries * D, p.entries,
+                              R > 1 ? C::SB : L::stage_bytes(p.entries));
+  __syncthreads();
+  const uint32_t cbl = smem_u32(smem) + L::lane_offset(r, q);
   const long long tile_bytes = (long long)p.chunks * V * 256;
-  const long long G = gridDim.x;
-  const long long t_begin = (p.num_tiles * blockIdx.x) / G;
-  const long long t_end = (p.num_tiles * (blockIdx.x + 1)) / G;
-  int cur_group = -1;
-  long long t = t_begin;
-  while (t < t_end) {
-    const int g = p.tiles[t].x;
-    if (g != cur_group) {
-      __syncthreads();
-      stage_codebooks<D, R, REPL>(smem, p.codebooks + (size_t)g * R * p.entries * D, p.entries);
-      __syncthreads();
-      cur_group = g;
-    }
-    int n_here = 1;
-    while (n_here < kWarps && t + n_here < t_end && p.tiles[t + n_here].x == g) ++n_here;
-    if (warp < n_here) {
-      const long long my_t = t + warp;
-      const int4 ti = p.tiles[my_t];
-      const uint32_t rho_a = r < ti.z ? rho_pair(p.row_scale[ti.y + r]) : 0u;
-      const uint32_t rho_b = r + 8 < ti.z ? rho_pair(p.row_scale[ti.y + r + 8]) : 0u;
-      const uint8_t* tbase = p.packed + my_t * tile_bytes;
-      for (int c = 0; c < p.chunks; ++c) {
-        uint32_t c0[V * 4], c1[V * 4];
+  for (long long t = tb + warp; t < te; t += kWarps) {
+    const int4 ti = p.tiles[t];
+    const uint32_t rho_a = r < ti.z ? rho_pair(p.row_scale[ti.y + r]) : 0u;
+    const uint32_t rho_b = r + 8 < ti.z ? rho_pair(p.row_scale[ti.y + r + 8]) : 0u;
+    const uint8_t* tbase = p.packed + t * tile_bytes;
+    for (int c = 0; c < p.chunks; ++c) {
+      uint32_t c0[V * 4], c1[V * 4];
 #pragma unroll
-        for (int v = 0; v < V; ++v) {
-          const uint4 a = ldg_stream_v4(tbase + ((long long)c * V + v) * 256 + r * 16);
-          const uint4 b = ldg_stream_v4(tbase + ((long long)c * V + v) * 256 + (r + 8) * 16);
-          c0[4 * v] = a.x; c0[4 * v + 1] = a.y; c0[4 * v + 2] = a.z; c0[4 * v + 3] = a.w;
-          c1[4 * v] = b.x; c1[4 * v + 1] = b.y; c1[4 * v + 2] = b.z; c1[4 * v + 3] = b.w;
-        }
-        static_for<0, D>([&](auto ktc) {
-          constexpr int kt = decltype(ktc)::value;
-          uint32_t ra[2], rb[2];
-          decode_row<D, R, IDW, REPL, kt, V>(ra, c0, cb_base, sb, rho_a, qh_shift);
-          decode_row<D, R, IDW, REPL, kt, V>(rb, c1, cb_base, sb, rho_b, qh_shift);
-          const int col = c * kChunkBlocks * D + kt * 16 + 4 * q;
-          if (col < p.K) {
-            if (r < ti.z) *reinterpret_cast<uint2*>(w + (long long)(ti.y + r) * ldw + col) = make_uint2(ra[0], ra[1]);
-            if (r + 8 < ti.z)
-              *reinterpret_cast<uint2*>(w + (long long)(ti.y + r + 8) * ldw + col) = make_uint2(rb[0], rb[1]);
-          }
-        });
+      for (int v = 0; v < V; ++v) {
+        const uint4 a = ldg_stream_v4(tbase + ((long long)c * V + v) * 256 + r * 16);
+        const uint4 b = ldg_stream_v4(tbase + ((long long)c * V + v) * 256 + (r + 8) * 16);
+        c0[4 * v] = a.x; c0[4 * v + 1] = a.y; c0[4 * v + 2] = a.z; c0[4 * v + 3] = a.w;
+        c1[4 * v] = b.x; c1[4 * v + 1] = b.y; c1[4 * v + 2] = b.z; c1[4 * v + 3] = b.w;
       }
+      static_for<0, D>([&](auto ktc) {
+        constexpr int kt = decltype(ktc)::value;
+        uint32_t ra[2], rb[2];
+        decode_row<D, R, IDW, REPL, kt, C::NW, C::SB>(ra, c0, cbl, rho_a, ls);
+        decode_row<D, R, IDW, REPL, kt, C::NW, C::SB>(rb, c1, cbl, rho_b, ls);
+        const int col = c * kChunkBlocks * D + kt * 16 + 4 * q;
+        if (col < p.K) {
+          if (r < ti.z) *reinterpret_cast<uint2*>(w + (long long)(ti.y + r) * ldw + col) = make_uint2(ra[0], ra[1]);
+          if (r + 8 < ti.z)
+            *reinterpret_cast<uint2*>(w + (long long)(ti.y + r + 8) * ldw + col) = make_uint2(rb[0], rb[1]);
+        }
+      });
     }
-    t += n_here;
   }
 }
 
@@ -306,12 +475,7 @@ __global__ void rvq_unpack_kernel(const uint8_t* __restrict__ packed, const int4
 bool replicated(int d, int R, int entries) {
   if (entries > 256) return false;
   const int copies = d == 8 ? 8 : 4;
-  return (long long)R * entries * d * 2 * copies <= 160 * 1024;
-}
-
-int smem_bytes(int d, int R, int entries, bool repl, int mt) {
-  const int copies = repl ? (d == 8 ? 8 : 4) : 1;
-  return R * entries * d * 2 * copies + kWarps * 16 * mt * 8 * 4;
+  return (long long)R * 256 * d * 2 * copies <= 128 * 1024;
 }
 
 int check_layer(const wal_rvq_layer* L) {
@@ -323,29 +487,48 @@ int check_layer(const wal_rvq_layer* L) {
   if (g.num_entries < 1 || g.num_entries > 32767 || (g.num_stages > 1 && g.num_entries > 256))
     return WAL_ERR_UNSUPPORTED;
   if (g.in_features % 4 != 0) return WAL_ERR_UNSUPPORTED;
+  if (g.num_groups > kMaxGroups) return WAL_ERR_UNSUPPORTED;
   if (!L->packed_ids || !L->tile_table || !L->codebooks || !L->row_scale) return WAL_ERR_INVALID_ARGUMENT;
   if (((uintptr_t)L->packed_ids & 15) || ((uintptr_t)L->tile_table & 15) || ((uintptr_t)L->codebooks & 15))
     return WAL_ERR_ALIGNMENT;
-  const bool repl = replicated(g.block_size, g.num_stages, g.num_entries);
-  if (smem_bytes(g.block_size, g.num_stages, g.num_entries, repl, 2) > 227 * 1024) return WAL_ERR_UNSUPPORTED;
   return WAL_OK;
 }
 
-// Grid of one persistent wave: SMs x resident CTAs per SM, capped by the tile count.
+// Group boundaries along the tile table, from the host row counts.
+int group_starts(const wal_rvq_layer* L, GemvParams* p) {
+  const int G = L->geom.num_groups;
+  if (G > kMaxGroups) return WAL_ERR_UNSUPPORTED;
+  if (G > 1 && !L->group_rows) return WAL_ERR_INVALID_ARGUMENT;
+  long long t = 0, rows = 0;
+  p->group_tile_start[0] = 0;
+  p->group_row_start[0] = 0;
+  for (int g = 0; g < G; ++g) {
+    const long long n = G == 1 ? L->geom.out_features : L->group_rows[g];
+    if (n <= 0) return WAL_ERR_SHAPE;
+    rows += n;
+    t += (n + kTileRows - 1) / kTileRows;
+    p->group_tile_start[g + 1] = (int)t;
+    p->group_row_start[g + 1] = (int)rows;
+  }
+  if (t != L->num_tiles || rows != L->geom.out_features) return WAL_ERR_SHAPE;
+  p->num_groups = G;
+  return WAL_OK;
+}
+
 template <typename Kern>
-int persistent_grid(Kern kern, int smem, int num_ctas, long long num_tiles, int* grid_out) {
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+int persistent_grid(Kern kern, int threads, int smem, int num_ctas, const GemvParams& p, int* grid_out) {
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return WAL_ERR_CUDA;
+  cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   int dev = 0, sms = 0, per_sm = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return WAL_ERR_CUDA;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return WAL_ERR_CUDA;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem) != cudaSuccess)
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess)
     return WAL_ERR_CUDA;
   if (per_sm < 1) return WAL_ERR_UNSUPPORTED;
   long long grid = num_ctas > 0 ? num_ctas : (long long)sms * per_sm;
-  if (grid > num_tiles) grid = num_tiles;
-  if (grid < 1) grid = 1;
+  if (grid > p.num_tiles) grid = p.num_tiles;
+  if (grid < p.num_groups) grid = p.num_groups;
   *grid_out = (int)grid;
   return WAL_OK;
 }
@@ -355,88 +538,142 @@ int persistent_grid(Kern kern, int smem, int num_ctas, long long num_tiles, int*
 
 using namespace wal;
 
-template <int D, int R, int IDW, bool REPL, int MT>
-static int run_gemv(const GemvParams& p, int num_ctas, cudaStream_t stream, int entries) {
-  auto kern = rvq_gemv_kernel<D, R, IDW, REPL, MT>;
-  const int smem = smem_bytes(D, R, entries, REPL, MT);
+template <int D, int R, int IDW, bool REPL, int MT, bool XS>
+static int run_gemv(const GemvParams& p, int num_ctas, cudaStream_t stream) {
+  using C = GemvCfg<D, R, IDW, REPL, MT, XS>;
+  auto kern = rvq_gemv_kernel<D, R, IDW, REPL, MT, XS>;
+  const int kpad = p.chunks * kChunkBlocks * D;
+  const int smem = C::smem(p.entries, p.M, kpad);
+  if (smem > 227 * 1024) return WAL_ERR_UNSUPPORTED;
+  if (p.wpt > C::kW) return WAL_ERR_INVALID_ARGUMENT;
   int grid = 0;
-  const int st = persistent_grid(kern, smem, num_ctas, p.num_tiles, &grid);
+  const int st = persistent_grid(kern, C::kT, smem, num_ctas, p, &grid);
   if (st != WAL_OK) return st;
-  kern<<<grid, kThreads, smem, stream>>>(p);
+  // programmatic dependent launch: the weight prologue (codebooks, first id
+  // chunks) of this kernel overlaps the tail of the previous kernel in the
+  // stream; the kernel waits on the dependency before touching x or y.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(C::kT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = p.pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, p) != cudaSuccess) return WAL_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? WAL_OK : WAL_ERR_CUDA;
 }
 
 template <int D, int R, int IDW, bool REPL>
-static int run_dequant(const GemvParams& p, uint16_t* w, long long ldw, cudaStream_t stream, int entries) {
+static int run_dequant(const GemvParams& p, uint16_t* w, long long ldw, cudaStream_t stream) {
+  using C = GemvCfg<D, R, IDW, REPL, 1, false>;
   auto kern = rvq_dequant_kernel<D, R, IDW, REPL>;
-  const int smem = smem_bytes(D, R, entries, REPL, 1);
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-    return WAL_ERR_CUDA;
-  int dev = 0, sms = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return WAL_ERR_CUDA;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return WAL_ERR_CUDA;
-  long long grid = (p.num_tiles + kWarps - 1) / kWarps;
-  if (grid > 4LL * sms) grid = 4LL * sms;
-  kern<<<(int)grid, kThreads, smem, stream>>>(p, w, ldw);
+  const int smem = C::cb_bytes(p.entries);
+  if (smem > 227 * 1024) return WAL_ERR_UNSUPPORTED;
+  int grid = 0;
+  const int st = persistent_grid(kern, kThreads, smem, 0, p, &grid);
+  if (st != WAL_OK) return st;
+  kern<<<grid, kThreads, smem, stream>>>(p, w, ldw);
   return cudaGetLastError() == cudaSuccess ? WAL_OK : WAL_ERR_CUDA;
 }
 
 template <int D, int R, int IDW>
-static int dispatch_gemv(const GemvParams& p, int num_ctas, cudaStream_t stream, int entries, bool repl, int mt) {
-  if (repl) {
-    if constexpr (IDW == 1) {
-      return mt == 1 ? run_gemv<D, R, IDW, true, 1>(p, num_ctas, stream, entries)
-                     : run_gemv<D, R, IDW, true, 2>(p, num_ctas, stream, entries);
+static int dispatch_gemv(const GemvParams& p, int num_ctas, cudaStream_t stream, bool repl, int mt, bool xs) {
+  if constexpr (IDW == 1) {
+    if (repl) {
+      if (mt == 1) return xs ? run_gemv<D, R, IDW, true, 1, true>(p, num_ctas, stream)
+                             : run_gemv<D, R, IDW, true, 1, false>(p, num_ctas, stream);
+      return xs ? run_gemv<D, R, IDW, true, 2, true>(p, num_ctas, stream)
+                : run_gemv<D, R, IDW, true, 2, false>(p, num_ctas, stream);
     }
   }
-  return mt == 1 ? run_gemv<D, R, IDW, false, 1>(p, num_ctas, stream, entries)
-                 : run_gemv<D, R, IDW, false, 2>(p, num_ctas, stream, entries);
+  if (mt == 1) return xs ? run_gemv<D, R, IDW, false, 1, true>(p, num_ctas, stream)
+                         : run_gemv<D, R, IDW, false, 1, false>(p, num_ctas, stream);
+  return xs ? run_gemv<D, R, IDW, false, 2, true>(p, num_ctas, stream)
+            : run_gemv<D, R, IDW, false, 2, false>(p, num_ctas, stream);
 }
 
 template <int D, int R, int IDW>
-static int dispatch_dequant(const GemvParams& p, uint16_t* w, long long ldw, cudaStream_t stream, int entries,
-                            bool repl) {
-  if (repl) {
-    if constexpr (IDW == 1) return run_dequant<D, R, IDW, true>(p, w, ldw, stream, entries);
+static int dispatch_dequant(const GemvParams& p, uint16_t* w, long long ldw, cudaStream_t stream, bool repl) {
+  if constexpr (IDW == 1) {
+    if (repl) return run_dequant<D, R, IDW, true>(p, w, ldw, stream);
   }
-  return run_dequant<D, R, IDW, false>(p, w, ldw, stream, entries);
+  return run_dequant<D, R, IDW, false>(p, w, ldw, stream);
 }
 
-#define WAL_FOR_ALL_CONFIGS(FN, ...)                                                    \
-  switch (d * 100 + R * 10 + idw) {                                                    \
-    case 811: return FN<8, 1, 1>(__VA_ARGS__);                                          \
-    case 812: return FN<8, 1, 2>(__VA_ARGS__);                                          \
-    case 821: return FN<8, 2, 1>(__VA_ARGS__);                                          \
-    case 831: return FN<8, 3, 1>(__VA_ARGS__);                                          \
-    case 841: return FN<8, 4, 1>(__VA_ARGS__);                                          \
-    case 1611: return FN<16, 1, 1>(__VA_ARGS__);                                        \
-    case 1612: return FN<16, 1, 2>(__VA_ARGS__);                                        \
-    case 1621: return FN<16, 2, 1>(__VA_ARGS__);                                        \
-    case 1631: return FN<16, 3, 1>(__VA_ARGS__);                                        \
-    case 1641: return FN<16, 4, 1>(__VA_ARGS__);                                        \
-    case 3211: return FN<32, 1, 1>(__VA_ARGS__);                                        \
-    case 3212: return FN<32, 1, 2>(__VA_ARGS__);                                        \
-    case 3221: return FN<32, 2, 1>(__VA_ARGS__);                                        \
-    case 3231: return FN<32, 3, 1>(__VA_ARGS__);                                        \
-    case 3241: return FN<32, 4, 1>(__VA_ARGS__);                                        \
-    default: return WAL_ERR_UNSUPPORTED;                                                \
-  }
+// Per-block-size dispatchers.  Each block size is compiled in its own
+// translation unit (the build passes -DWAL_UNIT_D=8/16/32) so the kernel
+// instantiations build in parallel; the C entry points are in the unit built
+// with -DWAL_UNIT_API.
+int wal_gemv_dispatch_d8(const GemvParams&, int, cudaStream_t, int, int, bool, int, bool);
+int wal_gemv_dispatch_d16(const GemvParams&, int, cudaStream_t, int, int, bool, int, bool);
+int wal_gemv_dispatch_d32(const GemvParams&, int, cudaStream_t, int, int, bool, int, bool);
+int wal_dequant_dispatch_d8(const GemvParams&, uint16_t*, long long, cudaStream_t, int, int, bool);
+int wal_dequant_dispatch_d16(const GemvParams&, uint16_t*, long long, cudaStream_t, int, int, bool);
+int wal_dequant_dispatch_d32(const GemvParams&, uint16_t*, long long, cudaStream_t, int, int, bool);
 
-static GemvParams make_params(const wal_rvq_layer* L) {
-  GemvParams p{};
+#ifdef WAL_UNIT_D
+#define WAL_CAT2(a, b) a##b
+#define WAL_CAT(a, b) WAL_CAT2(a, b)
+int WAL_CAT(wal_gemv_dispatch_d, WAL_UNIT_D)(const GemvParams& p, int num_ctas, cudaStream_t s, int R, int idw,
+                                             bool repl, int mt, bool xs) {
+  constexpr int D = WAL_UNIT_D;
+  switch (R * 10 + idw) {
+    case 11: return dispatch_gemv<D, 1, 1>(p, num_ctas, s, repl, mt, xs);
+    case 12: return dispatch_gemv<D, 1, 2>(p, num_ctas, s, repl, mt, xs);
+    case 21: return dispatch_gemv<D, 2, 1>(p, num_ctas, s, repl, mt, xs);
+    case 31: return dispatch_gemv<D, 3, 1>(p, num_ctas, s, repl, mt, xs);
+    case 41: return dispatch_gemv<D, 4, 1>(p, num_ctas, s, repl, mt, xs);
+    default: return WAL_ERR_UNSUPPORTED;
+  }
+}
+int WAL_CAT(wal_dequant_dispatch_d, WAL_UNIT_D)(const GemvParams& p, uint16_t* w, long long ldw, cudaStream_t s,
+                                                int R, int idw, bool repl) {
+  constexpr int D = WAL_UNIT_D;
+  switch (R * 10 + idw) {
+    case 11: return dispatch_dequant<D, 1, 1>(p, w, ldw, s, repl);
+    case 12: return dispatch_dequant<D, 1, 2>(p, w, ldw, s, repl);
+    case 21: return dispatch_dequant<D, 2, 1>(p, w, ldw, s, repl);
+    case 31: return dispatch_dequant<D, 3, 1>(p, w, ldw, s, repl);
+    case 41: return dispatch_dequant<D, 4, 1>(p, w, ldw, s, repl);
+    default: return WAL_ERR_UNSUPPORTED;
+  }
+}
+#endif  // WAL_UNIT_D
+
+#ifdef WAL_UNIT_API
+static int gemv_by_d(int d, const GemvParams& p, int num_ctas, cudaStream_t s, int R, int idw, bool repl, int mt,
+                     bool xs) {
+  if (d == 8) return wal_gemv_dispatch_d8(p, num_ctas, s, R, idw, repl, mt, xs);
+  if (d == 16) return wal_gemv_dispatch_d16(p, num_ctas, s, R, idw, repl, mt, xs);
+  if (d == 32) return wal_gemv_dispatch_d32(p, num_ctas, s, R, idw, repl, mt, xs);
+  return WAL_ERR_UNSUPPORTED;
+}
+
+static int dequant_by_d(int d, const GemvParams& p, uint16_t* w, long long ldw, cudaStream_t s, int R, int idw,
+                        bool repl) {
+  if (d == 8) return wal_dequant_dispatch_d8(p, w, ldw, s, R, idw, repl);
+  if (d == 16) return wal_dequant_dispatch_d16(p, w, ldw, s, R, idw, repl);
+  if (d == 32) return wal_dequant_dispatch_d32(p, w, ldw, s, R, idw, repl);
+  return WAL_ERR_UNSUPPORTED;
+}
+
+static int make_params(const wal_rvq_layer* L, GemvParams* p) {
+  *p = GemvParams{};
   const wal_rvq_geometry& g = L->geom;
   const long long blocks = (g.in_features + g.block_size - 1) / g.block_size;
-  p.packed = static_cast<const uint8_t*>(L->packed_ids);
-  p.tiles = reinterpret_cast<const int4*>(L->tile_table);
-  p.codebooks = L->codebooks;
-  p.row_scale = L->row_scale;
-  p.bias = L->bias;
-  p.num_tiles = L->num_tiles;
-  p.K = (int)g.in_features;
-  p.chunks = (int)((blocks + kChunkBlocks - 1) / kChunkBlocks);
-  p.entries = g.num_entries;
-  return p;
+  p->packed = static_cast<const uint8_t*>(L->packed_ids);
+  p->tiles = reinterpret_cast<const int4*>(L->tile_table);
+  p->codebooks = L->codebooks;
+  p->row_scale = L->row_scale;
+  p->bias = L->bias;
+  p->num_tiles = L->num_tiles;
+  p->K = (int)g.in_features;
+  p->chunks = (int)((blocks + kChunkBlocks - 1) / kChunkBlocks);
+  p->entries = g.num_entries;
+  return group_starts(L, p);
 }
 
 extern "C" int wal_rvq_gemv_ex(const wal_rvq_layer* layer, const uint16_t* x, int64_t M, int64_t ldx, void* y,
@@ -450,26 +687,42 @@ extern "C" int wal_rvq_gemv_ex(const wal_rvq_layer* layer, const uint16_t* x, in
   if ((ldx % 4) || ((uintptr_t)x & 7)) return WAL_ERR_ALIGNMENT;
   if (y_dtype != WAL_BF16 && y_dtype != WAL_F32 && y_dtype != WAL_F16) return WAL_ERR_INVALID_ARGUMENT;
   if (warps_per_tile != 0 && warps_per_tile != 1 && warps_per_tile != 2 && warps_per_tile != 4 &&
-      warps_per_tile != 8)
+      warps_per_tile != 8 && warps_per_tile != 16)
     return WAL_ERR_INVALID_ARGUMENT;
   if (num_ctas < 0) return WAL_ERR_INVALID_ARGUMENT;
   const int d = g.block_size, R = g.num_stages, idw = g.num_entries <= 256 ? 1 : 2;
   const bool repl = replicated(d, R, g.num_entries);
-  GemvParams p = make_params(layer);
+  GemvParams p;
+  st = make_params(layer, &p);
+  if (st != WAL_OK) return st;
   int wpt = warps_per_tile;
   if (wpt == 0) {
-    // enough (tile, warp) work units to fill every SM with several warps
+    // per-warp work model: rounds of 16/wpt tiles, each round ceil(chunks/wpt)
+    // chunks, plus a small reduction cost per round that grows with wpt
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    wpt = 1;
-    while (wpt < kWarps && layer->num_tiles * wpt < (long long)sms * 16 && wpt * 2 <= p.chunks) wpt *= 2;
+    const long long grid = layer->num_tiles < sms ? layer->num_tiles : sms;
+    const long long tpc = (layer->num_tiles + grid - 1) / grid;  // tiles per CTA (max)
+    double best = 1e30;
+    for (int w = 1; w <= 16; w *= 2) {
+      const long long slots = 16 / w;
+      const long long rounds = (tpc + slots - 1) / slots;
+      const long long cpw = (p.chunks + w - 1) / w;
+      const double cost = (double)rounds * ((double)cpw + 0.25 * (w > 1 ? 1 + w / 4.0 : 0.0));
+      if (cost < best - 1e-9) {
+        best = cost;
+        wpt = w;
+      }
+    }
   }
   p.wpt = wpt;
   p.ldx = ldx;
   p.ldy = ldy;
   p.y_dtype = y_dtype;
+  p.pdl = 1;
   const size_t ysz = y_dtype == WAL_F32 ? 4 : 2;
+  const int kpad = p.chunks * kChunkBlocks * d;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   for (int64_t m0 = 0; m0 < M; m0 += 16) {
     const int mm = (int)((M - m0) < 16 ? (M - m0) : 16);
@@ -477,8 +730,10 @@ extern "C" int wal_rvq_gemv_ex(const wal_rvq_layer* layer, const uint16_t* x, in
     p.y = static_cast<uint8_t*>(y) + (size_t)(m0 * ldy) * ysz;
     p.M = mm;
     const int mt = mm <= 8 ? 1 : 2;
-    auto run = [&]() -> int { WAL_FOR_ALL_CONFIGS(dispatch_gemv, p, num_ctas, s, g.num_entries, repl, mt) };
-    const int rs = run();
+    const bool xs = (long long)mm * kpad * 2 <= kXSmemBudget;
+    int rs = gemv_by_d(d, p, num_ctas, s, R, idw, repl, mt, xs);
+    if (rs == WAL_ERR_UNSUPPORTED && xs)  // activations do not fit beside the codebook
+      rs = gemv_by_d(d, p, num_ctas, s, R, idw, repl, mt, false);
     if (rs != WAL_OK) return rs;
   }
   return WAL_OK;
@@ -498,9 +753,11 @@ extern "C" int wal_rvq_dequant(const wal_rvq_layer* layer, uint16_t* w, int64_t 
   if ((ldw % 4) || ((uintptr_t)w & 7)) return WAL_ERR_ALIGNMENT;
   const int d = g.block_size, R = g.num_stages, idw = g.num_entries <= 256 ? 1 : 2;
   const bool repl = replicated(d, R, g.num_entries);
-  GemvParams p = make_params(layer);
+  GemvParams p;
+  st = make_params(layer, &p);
+  if (st != WAL_OK) return st;
   p.wpt = 1;
-  WAL_FOR_ALL_CONFIGS(dispatch_dequant, p, w, ldw, static_cast<cudaStream_t>(stream), g.num_entries, repl)
+  return dequant_by_d(d, p, w, ldw, static_cast<cudaStream_t>(stream), R, idw, repl);
 }
 
 extern "C" int wal_rvq_unpack_ids(const wal_rvq_layer* layer, void* ids, void* stream) {
@@ -519,3 +776,4 @@ extern "C" int wal_rvq_unpack_ids(const wal_rvq_layer* layer, void* ids, void* s
       layer->num_tiles, g.num_stages, idw, blocks, chunks, g.out_features, static_cast<uint8_t*>(ids));
   return cudaGetLastError() == cudaSuccess ? WAL_OK : WAL_ERR_CUDA;
 }
+#endif  // WAL_UNIT_API

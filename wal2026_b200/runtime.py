@@ -159,8 +159,11 @@ class PackedGroupedBlockRVQLinear(nn.Module):
         geom = _abi.Geometry(out_features=self.out_features, in_features=self.in_features,
                              block_size=self.block_size, num_stages=self.num_stages,
                              num_entries=self.num_entries, num_groups=self.num_groups)
+        rows = [r1 - r0 for r0, r1 in self.row_slices]
+        self._group_rows = (ctypes.c_int64 * len(rows))(*rows)  # kept alive with the descriptor
         layer = _abi.Layer(geom=geom, num_tiles=self.num_tiles, packed_ids=key[0], tile_table=key[1],
-                           codebooks=key[2], row_scale=key[3], bias=key[4])
+                           codebooks=key[2], row_scale=key[3], bias=key[4],
+                           group_rows=ctypes.cast(self._group_rows, ctypes.POINTER(ctypes.c_int64)))
         self._layer_cache = (key, layer)
         return layer
 
@@ -180,8 +183,13 @@ class PackedGroupedBlockRVQLinear(nn.Module):
         if orig[-1] != self.in_features:
             raise ValueError(f"Feature mismatch: {orig[-1]} != {self.in_features}")
         x2 = x.reshape(-1, self.in_features)
-        if x2.stride(-1) != 1 or x2.stride(0) % 4 != 0 or x2.data_ptr() % 8 != 0:
-            x2 = x2.contiguous()
+        if x2.stride(-1) != 1 or x2.stride(0) % 8 != 0 or x2.data_ptr() % 16 != 0:
+            if self.in_features % 8 == 0:
+                x2 = x2.contiguous()
+            else:  # pad rows to a multiple of 8 elements so every row starts 16-byte aligned
+                xp = torch.zeros((x2.shape[0], -(-self.in_features // 8) * 8), device=x.device, dtype=x.dtype)
+                xp[:, :self.in_features] = x2
+                x2 = xp
         M = x2.shape[0]
         y = torch.empty((M, self.out_features), device=x.device, dtype=torch.bfloat16)
         if M > 0:
