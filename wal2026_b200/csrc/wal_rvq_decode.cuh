@@ -105,9 +105,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 // reads one piece per (row, stage, k-tile).  In the replicated layout every
 // piece is stored once per lane class so that the 16 lanes of a half-warp
 // phase always hit 16 distinct bank pairs whatever ids they hold:
-//   d = 8 : 8 copies, entry stride 128 B, lane offset (r&3)*32 + q*8
-//   d = 16: 4 copies, entry stride 128 B, lane offset (r&3)*32 + q*8
-//   d = 32: 4 copies, entry stride 256 B (+128 B for the second 16 columns)
+//   d = 8 : 8 copies x 16 B per stage entry, lane offset (r&3)*32 + q*8
+//   d = 16: 4 copies x 32 B per stage entry, lane offset (r&3)*32 + q*8
+//   d = 32: 4 copies x 64 B per stage entry (second 16 columns at +128 B)
+// Replicated entry rows are 256 bytes (two stages side by side for d = 8/16,
+// one stage for d = 32), so the byte address of a lane's piece is
+//   id * 256 + lane_offset + constant
+// and one byte permute builds id * 256 + lane_offset from the packed id word
+// (id byte -> byte 1, lane offset -> byte 0): no multiply, no add per gather.
 // The plain layout stores each entry once (entry stride 2*d bytes) and is used
 // when replication does not fit (large routed codebooks).
 // ---------------------------------------------------------------------------
@@ -115,14 +120,31 @@ template <int D, bool REPL>
 struct CbLayout {
   static constexpr int kPieces = D / 4;
   static constexpr int kCopies = REPL ? (D == 8 ? 8 : 4) : 1;
-  static constexpr int kEntryStride = REPL ? (D == 32 ? 256 : 128) : 2 * D;
+  static constexpr int kStagesPerRow = REPL ? (D == 32 ? 1 : 2) : 1;
+  static constexpr int kEntryStride = REPL ? 256 : 2 * D;
   static constexpr int kHalfStride = REPL ? 128 : 32;  // only D == 32 uses it
-  __host__ __device__ static constexpr int stage_bytes(int entries) { return entries * D * 2 * kCopies; }
-  __device__ static int piece_offset(int e, int j, int c) {
-    if (!REPL) return (e * kPieces + j) * 8;
-    if (D == 8) return ((e * 8 + c) * 2 + j) * 8;
-    if (D == 16) return ((e * 4 + c) * 4 + j) * 8;
-    return (((e * 2 + (j >> 2)) * 4 + c) * 4 + (j & 3)) * 8;
+  static constexpr int kTableBytesRepl = 256 * 256;
+  __host__ __device__ static constexpr int tables(int R) { return (R + kStagesPerRow - 1) / kStagesPerRow; }
+  // multi-stage codebooks have at most 256 entries, so plain stages sit 256 entries apart
+  __host__ __device__ static constexpr int total_bytes(int R, int entries) {
+    return REPL ? tables(R) * kTableBytesRepl : (R == 1 ? entries * D * 2 : R * 256 * D * 2);
+  }
+  // constant byte offset of stage s inside the staged codebooks
+  __host__ __device__ static constexpr int stage_offset(int s) {
+    return REPL ? (s / kStagesPerRow) * kTableBytesRepl + (s % kStagesPerRow) * 128 : s * 256 * D * 2;
+  }
+  __device__ static int piece_offset(int s, int e, int j, int c, int entries) {
+    (void)entries;
+    if (!REPL) return stage_offset(s) + (e * kPieces + j) * 8;
+    int inner;
+    if (D == 8) {
+      inner = c * 16 + j * 8;
+    } else if (D == 16) {
+      inner = c * 32 + j * 8;
+    } else {
+      inner = (j >> 2) * 128 + c * 32 + (j & 3) * 8;
+    }
+    return stage_offset(s) + e * 256 + inner;
   }
   __device__ static int lane_offset(int r, int q) {
     if (REPL) return (r & 3) * 32 + q * 8;
@@ -132,6 +154,22 @@ struct CbLayout {
 
 __device__ __forceinline__ void cp_async_16(uint32_t saddr, const void* gptr) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(saddr), "l"(gptr));
+}
+
+// L2 cache policies: codebooks and activations are re-read by every CTA (and
+// by the next launch), the id stream is read once.
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;\n" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ void cp_async_16_hint(uint32_t saddr, const void* gptr, uint64_t pol) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;\n" ::"r"(saddr), "l"(gptr), "l"(pol));
 }
 
 __device__ __forceinline__ void cp_async_8(uint32_t saddr, const void* gptr) {
@@ -150,40 +188,39 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 //                            (first rounding).  Follow it with __syncthreads().
 // `sb` is the byte stride between stages in shared memory.
 template <int D, int R, bool REPL>
-__device__ void stage_codebooks_issue(uint8_t* cb, const uint16_t* __restrict__ books, int entries, int sb) {
+__device__ void stage_codebooks_issue(uint8_t* cb, const uint16_t* __restrict__ books, int entries) {
   using L = CbLayout<D, REPL>;
   constexpr int kRuns = D / 8;  // 16-byte runs per entry (two pieces each)
   const uint32_t base = smem_u32(cb);
+  const uint64_t keep = l2_policy_evict_last();
 #pragma unroll
   for (int s = 0; s < R; ++s) {
     const uint16_t* sbooks = books + (size_t)s * entries * D;
-    const uint32_t sbase = base + s * sb;
     for (int e = threadIdx.x; e < entries; e += blockDim.x) {
 #pragma unroll
       for (int run = 0; run < kRuns; ++run)
-        cp_async_16(sbase + L::piece_offset(e, 2 * run, 0), sbooks + (size_t)e * D + 8 * run);
+        cp_async_16_hint(base + L::piece_offset(s, e, 2 * run, 0, entries), sbooks + (size_t)e * D + 8 * run, keep);
     }
   }
 }
 
 template <int D, int R, bool REPL>
-__device__ void stage_codebooks_finish(uint8_t* cb, int entries, int sb) {
+__device__ void stage_codebooks_finish(uint8_t* cb, int entries) {
   using L = CbLayout<D, REPL>;
   if (R > 1 && !REPL) return;  // raw fp16 table, single copy: nothing to do
 #pragma unroll
   for (int s = 0; s < R; ++s) {
-    uint8_t* sbase = cb + s * sb;
     for (int e = threadIdx.x; e < entries; e += blockDim.x) {
 #pragma unroll
       for (int j = 0; j < L::kPieces; ++j) {
-        uint2 v = *reinterpret_cast<const uint2*>(sbase + L::piece_offset(e, j, 0));
+        uint2 v = *reinterpret_cast<const uint2*>(cb + L::piece_offset(s, e, j, 0, entries));
         if (R == 1) {
           v.x = preround_pair(v.x);
           v.y = preround_pair(v.y);
-          *reinterpret_cast<uint2*>(sbase + L::piece_offset(e, j, 0)) = v;
+          *reinterpret_cast<uint2*>(cb + L::piece_offset(s, e, j, 0, entries)) = v;
         }
 #pragma unroll
-        for (int c = 1; c < L::kCopies; ++c) *reinterpret_cast<uint2*>(sbase + L::piece_offset(e, j, c)) = v;
+        for (int c = 1; c < L::kCopies; ++c) *reinterpret_cast<uint2*>(cb + L::piece_offset(s, e, j, c, entries)) = v;
       }
     }
   }
@@ -191,11 +228,11 @@ __device__ void stage_codebooks_finish(uint8_t* cb, int entries, int sb) {
 
 // One-call staging for kernels without other prologue work.
 template <int D, int R, bool REPL>
-__device__ void stage_codebooks(uint8_t* cb, const uint16_t* __restrict__ books, int entries, int sb) {
-  stage_codebooks_issue<D, R, REPL>(cb, books, entries, sb);
+__device__ void stage_codebooks(uint8_t* cb, const uint16_t* __restrict__ books, int entries) {
+  stage_codebooks_issue<D, R, REPL>(cb, books, entries);
   cp_async_wait_all();
   __syncthreads();
-  stage_codebooks_finish<D, R, REPL>(cb, entries, sb);
+  stage_codebooks_finish<D, R, REPL>(cb, entries);
 }
 
 // ---------------------------------------------------------------------------
@@ -208,15 +245,31 @@ __device__ void stage_codebooks(uint8_t* cb, const uint16_t* __restrict__ books,
 // ids, sel16 = (q>>1) ? 0x4432 : 0x4410 for 2-byte ids.
 // ---------------------------------------------------------------------------
 struct LaneSel {
-  uint32_t sel8[2];
+  uint32_t sel8[2];   // id byte -> byte 0
+  uint32_t self8[2];  // id byte -> byte 1, lane offset (second operand, byte 0) -> byte 0
   uint32_t sel16;
-  __device__ explicit LaneSel(int q) {
+  uint32_t lane_off;  // replicated-layout lane offset (< 256)
+  __device__ LaneSel(int r, int q) {
     const uint32_t qh = (uint32_t)(q >> 1);
     sel8[0] = 0x4440u + qh;
     sel8[1] = 0x4442u + qh;
+    self8[0] = 0x5504u | (qh << 4);
+    self8[1] = 0x5504u | ((2u + qh) << 4);
     sel16 = qh ? 0x4432u : 0x4410u;
+    lane_off = (uint32_t)((r & 3) * 32 + q * 8);
   }
 };
+
+// Replicated layouts: byte address id * 256 + lane offset from one permute.
+template <int D, int KT, int S, int NW>
+__device__ __forceinline__ uint32_t id_addr256(const uint32_t (&codes)[NW], const LaneSel& ls) {
+  if (D == 8) {
+    return __byte_perm(codes[S * 4 + (KT >> 1)], ls.lane_off, ls.self8[KT & 1]);
+  } else {
+    constexpr int b = (D == 16) ? KT : (KT >> 1);
+    return __byte_perm(codes[S * 4 + (b >> 2)], ls.lane_off, 0x5504u | ((uint32_t)(b & 3) << 4));
+  }
+}
 
 template <int D, int IDW, int KT, int S, int NW>
 __device__ __forceinline__ uint32_t extract_id(const uint32_t (&codes)[NW], const LaneSel& ls) {
@@ -257,30 +310,39 @@ __device__ __forceinline__ uint2 lds64_ordered(uint32_t saddr) {
   return v;
 }
 
-template <int D, int R, int IDW, bool REPL, int KT, int NW, int SB>
-__device__ __forceinline__ void decode_row(uint32_t (&out)[2], const uint32_t (&codes)[NW], uint32_t cbl,
+template <int D, int R, int IDW, bool REPL, int KT, int NW, int E>
+__device__ __forceinline__ uint32_t piece_addr(const uint32_t (&codes)[NW], uint32_t cb, const LaneSel& ls,
+                                               uint32_t cbl) {
+  using L = CbLayout<D, REPL>;
+  if constexpr (REPL && IDW == 1) {
+    return cb + id_addr256<D, KT, E, NW>(codes, ls);
+  } else {
+    return cbl + extract_id<D, IDW, KT, E, NW>(codes, ls) * L::kEntryStride;
+  }
+}
+
+// Decode the lane's two bf16x2 words of one row for k-tile KT:
+// out[0] = columns 4q, 4q+1; out[1] = columns 4q+2, 4q+3 (both already
+// multiplied by the row scale with the second rounding).
+// cb = shared codebook base, cbl = cb + this lane's offset (plain layouts).
+template <int D, int R, int IDW, bool REPL, int KT, int NW>
+__device__ __forceinline__ void decode_row(uint32_t (&out)[2], const uint32_t (&codes)[NW], uint32_t cb, uint32_t cbl,
                                            uint32_t rho2, const LaneSel& ls) {
   using L = CbLayout<D, REPL>;
   constexpr int half_off = (D == 32) ? (KT & 1) * L::kHalfStride : 0;
   if (R == 1) {
-    const uint32_t id = extract_id<D, IDW, KT, 0, NW>(codes, ls);
-    const uint2 p = lds64<half_off>(cbl + id * L::kEntryStride);
+    const uint2 p = lds64<half_off>(piece_addr<D, R, IDW, REPL, KT, NW, 0>(codes, cb, ls, cbl));
     out[0] = mul_bf16x2_rn(p.x, rho2);
     out[1] = mul_bf16x2_rn(p.y, rho2);
   } else {
     float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
     for (int s = 0; s < R; ++s) {
-      uint32_t id;
-      if (s == 0) id = extract_id<D, IDW, KT, 0, NW>(codes, ls);
-      if (s == 1) id = extract_id<D, IDW, KT, 1, NW>(codes, ls);
-      if (s == 2) id = extract_id<D, IDW, KT, 2, NW>(codes, ls);
-      if (s == 3) id = extract_id<D, IDW, KT, 3, NW>(codes, ls);
       uint2 p;
-      if (s == 0) p = lds64<0 * SB + half_off>(cbl + id * L::kEntryStride);
-      if (s == 1) p = lds64<1 * SB + half_off>(cbl + id * L::kEntryStride);
-      if (s == 2) p = lds64<2 * SB + half_off>(cbl + id * L::kEntryStride);
-      if (s == 3) p = lds64<3 * SB + half_off>(cbl + id * L::kEntryStride);
+      if (s == 0) p = lds64<L::stage_offset(0) + half_off>(piece_addr<D, R, IDW, REPL, KT, NW, 0>(codes, cb, ls, cbl));
+      if (s == 1) p = lds64<L::stage_offset(1) + half_off>(piece_addr<D, R, IDW, REPL, KT, NW, 1>(codes, cb, ls, cbl));
+      if (s == 2) p = lds64<L::stage_offset(2) + half_off>(piece_addr<D, R, IDW, REPL, KT, NW, 2>(codes, cb, ls, cbl));
+      if (s == 3) p = lds64<L::stage_offset(3) + half_off>(piece_addr<D, R, IDW, REPL, KT, NW, 3>(codes, cb, ls, cbl));
       add2_f32_f16x2(s0, s1, p.x);
       add2_f32_f16x2(s2, s3, p.y);
     }

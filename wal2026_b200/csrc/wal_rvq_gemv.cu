@@ -101,7 +101,7 @@ __device__ void cta_range(const GemvParams& p, int cta, int ctas, int* group, lo
   int assigned = 0;
   for (int g = 0; g < G; ++g) {
     const long long tg = p.group_tile_start[g + 1] - p.group_tile_start[g];
-    long long cum = (long long)((double)ctas * (double)p.group_tile_start[g + 1] / (double)T + 0.5);
+    long long cum = ((long long)ctas * p.group_tile_start[g + 1] + T / 2) / T;
     if (cum < g + 1) cum = g + 1;
     if (cum > ctas - (G - 1 - g)) cum = ctas - (G - 1 - g);
     if (g == G - 1) cum = ctas;
@@ -127,10 +127,9 @@ struct GemvCfg {
   static constexpr int kT = kW * 32;
   static constexpr int V = R * IDW;               // 16-byte vectors per row-chunk
   static constexpr int NW = V * 4;                // 32-bit code words per row-chunk
-  static constexpr int SB = L::stage_bytes(256);  // stage stride (R > 1 implies <= 256 entries)
   static constexpr int kStageBytes = V * 256;     // one chunk of one tile (16 rows)
   static constexpr int MC = MT * 8;
-  __host__ __device__ static int cb_bytes(int entries) { return R > 1 ? R * SB : L::stage_bytes(entries); }
+  __host__ __device__ static int cb_bytes(int entries) { return L::total_bytes(R, entries); }
   // activations: M rows plus one zero row that lanes beyond M read; the row
   // stride is padded by 32 bytes so rows read together fall in different banks
   __host__ __device__ static int x_stride(int kpad) { return kpad * 2 + 32; }
@@ -146,7 +145,7 @@ struct GemvCfg {
 
 template <int D, int R, int IDW, bool REPL, int MT, bool XS, bool MASK>
 __device__ __forceinline__ void gemv_chunk(float (&acc)[2][MT][4], const uint32_t (&c0)[R * IDW * 4],
-                                           const uint32_t (&c1)[R * IDW * 4], uint32_t cbl, uint32_t rho_a,
+                                           const uint32_t (&c1)[R * IDW * 4], uint32_t cb, uint32_t cbl, uint32_t rho_a,
                                            uint32_t rho_b, const LaneSel& ls, const uint16_t* xrow0,
                                            const uint16_t* xrow1, uint32_t xs0, uint32_t xs1, bool xv0, bool xv1,
                                            int col_base, int K) {
@@ -154,8 +153,8 @@ __device__ __forceinline__ void gemv_chunk(float (&acc)[2][MT][4], const uint32_
   static_for<0, D>([&](auto ktc) {
     constexpr int kt = decltype(ktc)::value;
     uint32_t ra[2], rb[2];
-    decode_row<D, R, IDW, REPL, kt, C::NW, C::SB>(ra, c0, cbl, rho_a, ls);
-    decode_row<D, R, IDW, REPL, kt, C::NW, C::SB>(rb, c1, cbl, rho_b, ls);
+    decode_row<D, R, IDW, REPL, kt, C::NW>(ra, c0, cb, cbl, rho_a, ls);
+    decode_row<D, R, IDW, REPL, kt, C::NW>(rb, c1, cb, cbl, rho_b, ls);
     const int col = col_base + kt * 16;  // lane's first physical column (includes 4q)
     uint2 xa = make_uint2(0u, 0u), xb = make_uint2(0u, 0u);
     const bool in_k = !MASK || col < K;
@@ -197,7 +196,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
   const int wpt = p.wpt;
   const int slots = kWarps / wpt;
   const int slot = warp / wpt, kpart = warp - slot * wpt;
-  const LaneSel ls(q);
+  const LaneSel ls(r, q);
 
   int group;
   long long tb, te;
@@ -227,6 +226,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
   const long long step_chunk = (long long)wpt * V * 256;
   const long long step_tile = (long long)slots * tile_bytes - (long long)cpw * step_chunk;
   const uint32_t ring_lane = smem_u32(wring) + lane * 16;
+  const uint64_t stream_pol = l2_policy_evict_first();
   long long is_left = items;
   int is_j = 0;
   uint32_t is_slot = 0;
@@ -235,7 +235,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
       if (copy_lane) {
 #pragma unroll
         for (int k = 0; k < kLaneCopies; ++k)
-          cp_async_16(ring_lane + is_slot * C::kStageBytes + k * 512, is_src + k * 512);
+          cp_async_16_hint(ring_lane + is_slot * C::kStageBytes + k * 512, is_src + k * 512, stream_pol);
       }
       --is_left;
       is_src += step_chunk;
@@ -250,10 +250,10 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
 
   // -- prologue: weights (static) first, activations after the dependency --
   // group 0: codebooks (+ activations); groups 1..kRing-1: the first id chunks
-  stage_codebooks_issue<D, R, REPL>(cb, p.codebooks + (size_t)group * R * p.entries * D, p.entries,
-                                    R > 1 ? C::SB : L::stage_bytes(p.entries));
+  stage_codebooks_issue<D, R, REPL>(cb, p.codebooks + (size_t)group * R * p.entries * D, p.entries);
   if (p.pdl) grid_dependency_wait();  // x (and y) belong to the previous kernel in the stream
   if (XS) {
+    const uint64_t x_pol = l2_policy_evict_last();
     // rows m < M, columns [0, kpad): zero beyond K
     const int vec_per_row = kpad / 8;  // 16-byte vectors
     for (int i = threadIdx.x; i < (p.M + 1) * vec_per_row; i += kThreads) {
@@ -266,7 +266,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
       const int col = v * 8;
       const uint16_t* src = p.x + (long long)m * p.ldx + col;
       if (col + 8 <= p.K && ((uintptr_t)src & 15) == 0) {
-        cp_async_16((uint32_t)__cvta_generic_to_shared(dst), src);
+        cp_async_16_hint((uint32_t)__cvta_generic_to_shared(dst), src, x_pol);
       } else if (col + 8 <= p.K) {
         cp_async_8((uint32_t)__cvta_generic_to_shared(dst), src);
         cp_async_8((uint32_t)__cvta_generic_to_shared(dst + 4), src + 4);
@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
   for (int s = 0; s < kRing - 1; ++s) issue();
   cp_async_wait<kRing - 1>();  // group 0 landed
   __syncthreads();
-  stage_codebooks_finish<D, R, REPL>(cb, p.entries, R > 1 ? C::SB : L::stage_bytes(p.entries));
+  stage_codebooks_finish<D, R, REPL>(cb, p.entries);
   __syncthreads();
 
   const int m0 = r, m1 = 8 + r;
@@ -290,7 +290,8 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
   const uint32_t xs0 = smem_u32(xs) + (uint32_t)((xv0 ? m0 : p.M) * C::x_stride(kpad));
   const uint32_t xs1 = smem_u32(xs) + (uint32_t)((xv1 ? m1 : p.M) * C::x_stride(kpad));
   const bool need_mask = kpad != p.K;
-  const uint32_t cbl = smem_u32(cb) + L::lane_offset(r, q);
+  const uint32_t cb_s = smem_u32(cb);
+  const uint32_t cbl = cb_s + L::lane_offset(r, q);
 
   // row scales of a tile: tile t covers rows g_row0 + 16 * (t - g_tile0) ...
   auto tile_rows = [&](long long t, int* row0, int* nrows) {
@@ -341,10 +342,10 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
         const int c = kpart + j * wpt;
         const int col_base = c * kChunkBlocks * D + 4 * q;
         if (need_mask && c == p.chunks - 1) {
-          gemv_chunk<D, R, IDW, REPL, MT, XS, true>(acc, c0, c1, cbl, rho_a, rho_b, ls, xrow0, xrow1, xs0, xs1, xv0,
+          gemv_chunk<D, R, IDW, REPL, MT, XS, true>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, xrow0, xrow1, xs0, xs1, xv0,
                                                     xv1, col_base, p.K);
         } else {
-          gemv_chunk<D, R, IDW, REPL, MT, XS, false>(acc, c0, c1, cbl, rho_a, rho_b, ls, xrow0, xrow1, xs0, xs1,
+          gemv_chunk<D, R, IDW, REPL, MT, XS, false>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, xrow0, xrow1, xs0, xs1,
                                                      xv0, xv1, col_base, p.K);
         }
       }
@@ -403,15 +404,15 @@ __global__ void __launch_bounds__(kThreads) rvq_dequant_kernel(const __grid_cons
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, q = lane & 3;
-  const LaneSel ls(q);
+  const LaneSel ls(r, q);
   int group;
   long long tb, te;
   cta_range(p, blockIdx.x, gridDim.x, &group, &tb, &te);
   if (tb >= te) return;
-  stage_codebooks<D, R, REPL>(smem, p.codebooks + (size_t)group * R * p.entries * D, p.entries,
-                              R > 1 ? C::SB : L::stage_bytes(p.entries));
+  stage_codebooks<D, R, REPL>(smem, p.codebooks + (size_t)group * R * p.entries * D, p.entries);
   __syncthreads();
-  const uint32_t cbl = smem_u32(smem) + L::lane_offset(r, q);
+  const uint32_t cb_s = smem_u32(smem);
+  const uint32_t cbl = cb_s + L::lane_offset(r, q);
   const long long tile_bytes = (long long)p.chunks * V * 256;
   for (long long t = tb + warp; t < te; t += kWarps) {
     const int4 ti = p.tiles[t];
@@ -430,8 +431,8 @@ __global__ void __launch_bounds__(kThreads) rvq_dequant_kernel(const __grid_cons
       static_for<0, D>([&](auto ktc) {
         constexpr int kt = decltype(ktc)::value;
         uint32_t ra[2], rb[2];
-        decode_row<D, R, IDW, REPL, kt, C::NW, C::SB>(ra, c0, cbl, rho_a, ls);
-        decode_row<D, R, IDW, REPL, kt, C::NW, C::SB>(rb, c1, cbl, rho_b, ls);
+        decode_row<D, R, IDW, REPL, kt, C::NW>(ra, c0, cb_s, cbl, rho_a, ls);
+        decode_row<D, R, IDW, REPL, kt, C::NW>(rb, c1, cb_s, cbl, rho_b, ls);
         const int col = c * kChunkBlocks * D + kt * 16 + 4 * q;
         if (col < p.K) {
           if (r < ti.z) *reinterpret_cast<uint2*>(w + (long long)(ti.y + r) * ldw + col) = make_uint2(ra[0], ra[1]);
@@ -474,8 +475,8 @@ __global__ void rvq_unpack_kernel(const uint8_t* __restrict__ packed, const int4
 // ---------------------------------------------------------------------------
 bool replicated(int d, int R, int entries) {
   if (entries > 256) return false;
-  const int copies = d == 8 ? 8 : 4;
-  return (long long)R * 256 * d * 2 * copies <= 128 * 1024;
+  const int per_row = d == 32 ? 1 : 2;  // stages per 256-byte entry row
+  return ((R + per_row - 1) / per_row) * 64 * 1024 <= 128 * 1024;
 }
 
 int check_layer(const wal_rvq_layer* L) {

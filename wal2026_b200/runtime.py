@@ -73,17 +73,18 @@ class PackedBlockRVQGroup(nn.Module):
     reaches the parent through a weak reference for ``reconstruct_weight``.
     """
 
-    def __init__(self, enc, parent: "PackedGroupedBlockRVQLinear", row0: int, row1: int) -> None:
+    def __init__(self, parent: "PackedGroupedBlockRVQLinear", row0: int, row1: int, *, block_size: int,
+                 in_features: int, num_stages: int, enc=None) -> None:
         super().__init__()
-        self.block_size = int(enc.block_size)
-        self.in_features = int(enc.original_shape[1])
-        self.out_features = int(enc.original_shape[0])
-        self.padded_cols = int(enc.padded_cols)
-        self.num_stages = len(enc.stage_ids)
-        self.product_splits = int(enc.product_splits)
-        self.stages_per_split = tuple(int(x) for x in enc.stages_per_split)
-        self.transform_kind = enc.transform_kind
-        self.residual_correction = enc.residual_correction
+        self.block_size = int(block_size)
+        self.in_features = int(in_features)
+        self.out_features = int(row1 - row0)
+        self.padded_cols = -(-self.in_features // self.block_size) * self.block_size
+        self.num_stages = int(num_stages)
+        self.product_splits = 1 if enc is None else int(enc.product_splits)
+        self.stages_per_split = (self.num_stages,) if enc is None else tuple(int(x) for x in enc.stages_per_split)
+        self.transform_kind = "none" if enc is None else enc.transform_kind
+        self.residual_correction = "none" if enc is None else enc.residual_correction
         self.row0, self.row1 = int(row0), int(row1)
         self._parent = weakref.ref(parent)
 
@@ -129,7 +130,9 @@ class PackedGroupedBlockRVQLinear(nn.Module):
         packed = _packed if _packed is not None else pack_grouped(enc)
         self._set_packed(packed)
         self.groups = nn.ModuleList(
-            PackedBlockRVQGroup(g, self, r0, r1) for g, (r0, r1) in zip(enc.groups, self.row_slices)
+            PackedBlockRVQGroup(self, r0, r1, block_size=g.block_size, in_features=self.in_features,
+                                num_stages=len(g.stage_ids), enc=g)
+            for g, (r0, r1) in zip(enc.groups, self.row_slices)
         )
         if bias is not None:
             self.register_buffer("bias", bias.detach().to(torch.bfloat16).reshape(-1).contiguous())
@@ -148,6 +151,80 @@ class PackedGroupedBlockRVQLinear(nn.Module):
         self.register_buffer("tile_table", packed.tile_table)
         self.register_buffer("codebooks", packed.codebooks)
         self.register_buffer("row_scale", packed.row_scale)
+
+    @classmethod
+    def random(
+        cls,
+        group_rows: list[int],
+        in_features: int,
+        *,
+        block_size: int = 8,
+        num_stages: int = 2,
+        entries: int = 256,
+        stage_std: tuple[float, ...] = (0.02, 0.005),
+        generator: Optional[torch.Generator] = None,
+        device: torch.device | str = "cuda",
+        bias: Optional[Tensor] = None,
+    ) -> "PackedGroupedBlockRVQLinear":
+        """A packed linear with seeded random ids, codebooks and row scales, built on ``device``.
+
+        For benchmark stacks whose weights are random by definition: uniform ids
+        are written straight into the packed stream (any permutation of
+        uniform ids is uniform), codebooks are N(0, stage_std[s]) fp16 and row
+        scales U(0.5, 1.5) fp16, so no dense weight and no host-side encoding
+        is ever materialised.  The result is a regular packed module (it
+        round-trips through ``unpack_ids``).
+        """
+        if entries > 256:
+            raise ValueError("random() builds 1-byte ids (<= 256 entries)")
+        device = torch.device(device)
+        gen = generator
+        d, R, K = int(block_size), int(num_stages), int(in_features)
+        N = int(sum(group_rows))
+        blocks = -(-K // d)
+        chunks = -(-blocks // 16)
+        tiles = [-(-int(n) // 16) for n in group_rows]
+        T = sum(tiles)
+        nbytes = T * chunks * R * 256
+        if entries == 256:
+            packed = torch.randint(0, 256, (nbytes,), dtype=torch.uint8, device=device, generator=gen)
+        else:
+            packed = torch.randint(0, entries, (nbytes,), dtype=torch.uint8, device=device, generator=gen)
+        table = []
+        row0 = 0
+        for g, (n, t) in enumerate(zip(group_rows, tiles)):
+            for lt in range(t):
+                table.append([g, row0 + 16 * lt, min(16, int(n) - 16 * lt), 0])
+            row0 += int(n)
+        books = torch.empty((len(group_rows), R, entries, d), device=device, dtype=torch.float32)
+        for s in range(R):
+            std = stage_std[s] if s < len(stage_std) else stage_std[-1]
+            books[:, s].normal_(0.0, std, generator=gen)
+        rho = torch.rand((N,), device=device, generator=gen) + 0.5
+        geom = _abi.Geometry(out_features=N, in_features=K, block_size=d, num_stages=R, num_entries=entries,
+                             num_groups=len(group_rows))
+        arrays = PackedArrays(geom, T, packed, torch.tensor(table, dtype=torch.int32, device=device),
+                              books.to(torch.float16).contiguous(), rho.to(torch.float16).contiguous())
+        obj = cls.__new__(cls)
+        nn.Module.__init__(obj)
+        obj.in_features, obj.out_features = K, N
+        slices, r = [], 0
+        for n in group_rows:
+            slices.append((r, r + int(n)))
+            r += int(n)
+        obj.row_slices = tuple(slices)
+        obj.matmul_strategy = "per_group"
+        obj.matmul_chunk_rows = obj.local_palette_group_cols = obj.hot_topk = None
+        obj.hot_score_mode, obj.hot_min_stage_share, obj.hot_score_threshold_ratio = "row_scale_norm", 0.0, 0.0
+        obj._set_packed(arrays)
+        obj.groups = nn.ModuleList(PackedBlockRVQGroup(obj, r0, r1, block_size=d, in_features=K, num_stages=R)
+                                   for r0, r1 in obj.row_slices)
+        if bias is not None:
+            obj.register_buffer("bias", bias.detach().to(device=device, dtype=torch.bfloat16).reshape(-1))
+        else:
+            obj.bias = None
+        obj._layer_cache = None
+        return obj
 
     # -- C ABI plumbing -----------------------------------------------------
     def layer_struct(self) -> _abi.Layer:
