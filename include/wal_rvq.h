@@ -136,6 +136,20 @@ WAL_API int wal_rvq_gemv(const wal_rvq_layer* layer, const uint16_t* x, int64_t 
                  void* y, int64_t ldy, int y_dtype, void* stream);
 
 /*
+ * Prefill GEMM (large M): y[M, N] = x[M, K] @ w^T (+ bias) on the tcgen05
+ * tensor cores.  Weight tiles are decoded exactly (same arithmetic as the
+ * GEMV) into shared memory per 64-column stage; x tiles arrive by TMA.
+ * Supports d = 8, R in {1, 2}, <= 256 entries; row groups must start at a
+ * multiple of 256 rows.  x: bf16, ldx % 8 == 0, 16-byte aligned base.
+ * y_dtype: WAL_BF16 or WAL_F32.  status: optional device int, set to 1 if a
+ * pipeline wait timed out (the CTA then stops and frees its resources), NULL
+ * to skip.  Returns WAL_ERR_UNSUPPORTED for other configurations (callers use
+ * wal_rvq_gemv).  Replaces reference src/runtime.py:1501-1507 for M >= 256.
+ */
+WAL_API int wal_rvq_gemm(const wal_rvq_layer* layer, const uint16_t* x, int64_t M, int64_t ldx,
+                 void* y, int64_t ldy, int y_dtype, int* status, void* stream);
+
+/*
  * Same as wal_rvq_gemv with an explicit split of each 16-row tile's blocks
  * over `warps_per_tile` warps (1, 2, 4 or 8; 0 = library default) and an
  * explicit CTA count (0 = one persistent wave).  For tuning and tests.

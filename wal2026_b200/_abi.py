@@ -72,6 +72,7 @@ SIGNATURES: dict[str, tuple] = {
     "wal_route_pack": (_c_int, [_GP, _vp, _vp, _vp, ctypes.c_size_t, ctypes.POINTER(ctypes.c_int32)]),
     "wal_rvq_gemv": (_c_int, [_LP, _vp, _c_i64, _c_i64, _vp, _c_i64, _c_int, _vp]),
     "wal_rvq_gemv_ex": (_c_int, [_LP, _vp, _c_i64, _c_i64, _vp, _c_i64, _c_int, _c_int, _c_int, _vp]),
+    "wal_rvq_gemm": (_c_int, [_LP, _vp, _c_i64, _c_i64, _vp, _c_i64, _c_int, _vp, _vp]),
     "wal_rvq_dequant": (_c_int, [_LP, _vp, _c_i64, _vp]),
     "wal_rvq_unpack_ids": (_c_int, [_LP, _vp, _vp]),
 }

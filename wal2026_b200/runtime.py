@@ -35,6 +35,9 @@ MATMUL_STRATEGIES = frozenset({
     "triton_block_rvq", "stacked_matmul",
 })
 
+# token count from which the forward uses the tensor-core prefill GEMM
+PREFILL_MIN_TOKENS = 128
+
 TARGET_LINEAR_SUFFIXES = (
     "self_attn.q_proj",
     "self_attn.k_proj",
@@ -269,9 +272,24 @@ class PackedGroupedBlockRVQLinear(nn.Module):
                 x2 = xp
         M = x2.shape[0]
         y = torch.empty((M, self.out_features), device=x.device, dtype=torch.bfloat16)
-        if M > 0:
+        if M >= PREFILL_MIN_TOKENS and self.gemm_into(x2, y):
+            pass
+        elif M > 0:
             self.gemv_into(x2, y)
         return y.reshape(*orig[:-1], self.out_features)
+
+    def gemm_into(self, x2: Tensor, y: Tensor, status: Optional[Tensor] = None) -> bool:
+        """Prefill GEMM on the tcgen05 path; False when this layer's format is not covered by it."""
+        lib = _abi.load()
+        layer = self.layer_struct()
+        with torch.cuda.device(x2.device):
+            st = lib.wal_rvq_gemm(ctypes.byref(layer), x2.data_ptr(), x2.shape[0], x2.stride(0), y.data_ptr(),
+                                  y.stride(0), _abi.DTYPE_CODE[y.dtype], None if status is None else status.data_ptr(),
+                                  _abi.stream_handle(x2.device))
+        if st == _abi.WAL_ERR_UNSUPPORTED:
+            return False
+        _abi.check(st, "wal_rvq_gemm")
+        return True
 
     def gemv_into(self, x2: Tensor, y: Tensor, *, warps_per_tile: int = 0, num_ctas: int = 0) -> None:
         """y[M, N] <- x2[M, K] @ w^T (+ bias) through ``wal_rvq_gemv_ex`` on the current stream."""
