@@ -46,7 +46,8 @@ typedef enum wal_status {
   WAL_ERR_ID_RANGE = 4,         /* an id or route is >= its codebook size     */
   WAL_ERR_UNSUPPORTED = 5,      /* valid input this build does not implement  */
   WAL_ERR_CUDA = 6,             /* a CUDA runtime call failed                  */
-  WAL_ERR_BUFFER_TOO_SMALL = 7  /* caller buffer smaller than required        */
+  WAL_ERR_BUFFER_TOO_SMALL = 7, /* caller buffer smaller than required        */
+  WAL_ERR_PEER_TIMEOUT = 8      /* a peer's data did not arrive in time       */
 } wal_status;
 
 typedef enum wal_dtype { WAL_BF16 = 0, WAL_F32 = 1, WAL_F16 = 2 } wal_dtype;
@@ -125,7 +126,8 @@ WAL_API int wal_route_pack(const wal_rvq_geometry* geom, const uint8_t* route, c
                    void* packed, size_t packed_bytes, int32_t* tile_table);
 
 /*
- * Decode GEMV (M <= 16 tokens): y[M, N] = x[M, K] @ w^T (+ bias).
+ * Decode GEMV (any M; up to 32 tokens per kernel launch, larger M in slabs of
+ * 32): y[M, N] = x[M, K] @ w^T (+ bias).
  * x: device bf16, row stride ldx elements (ldx >= K, ldx % 4 == 0, 8-byte
  * aligned base; ldx % 8 == 0 with a 16-byte aligned base is fastest).  y: device, row stride ldy elements, dtype y_dtype
  * (WAL_BF16: one rounding of the fp32 result; WAL_F32: the fp32 result).
@@ -171,6 +173,86 @@ WAL_API int wal_rvq_dequant(const wal_rvq_layer* layer, uint16_t* w, int64_t ldw
  * Used to prove the re-layout is lossless (ids must round-trip bit-exactly).
  */
 WAL_API int wal_rvq_unpack_ids(const wal_rvq_layer* layer, void* ids, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Tensor-parallel decode.  No reference counterpart: the reference runs one
+ * device.  A row-parallel linear (o_proj, down_proj split along K) produces
+ * an fp32 partial output on every rank.  wal_rvq_gemv_push stores each
+ * element of its partial straight into a receive slot in every rank's memory
+ * (peer pointers over NVLink, mapped with wal_peer_region_open) as one 8-byte
+ * word {fp32 value, uint32 tag}; the tag is the slot's call count + 1, so a
+ * word is fresh exactly when its tag matches and no fence or flag is needed
+ * (an aligned 8-byte store arrives whole).  wal_tp_reduce_rmsnorm on every
+ * rank waits (bounded) for all ranks' words, sums them in rank order (every
+ * rank then holds identical values), adds the residual, applies the next
+ * RMSNorm and advances the slot's call count.
+ * ------------------------------------------------------------------------ */
+#define WAL_MAX_RANKS 8
+#define WAL_IPC_HANDLE_BYTES 64
+
+typedef struct wal_tp_push {
+  int32_t num_ranks;            /* P in 1..WAL_MAX_RANKS                                    */
+  int32_t rank;                 /* this rank                                                */
+  void* dst[WAL_MAX_RANKS];     /* dst[p]: rank p's receive rows for this rank, 8-byte words */
+  int64_t ld_dst;               /* row stride of every dst[p] in words (>= N)               */
+  const uint32_t* epoch;        /* this rank's call count of the slot (device)              */
+} wal_tp_push;
+
+/*
+ * Decode GEMV whose fp32 output rows are stored, tagged with *epoch + 1,
+ * into dst[p] for every rank p.  Bias is not added (row-parallel partials).
+ */
+WAL_API int wal_rvq_gemv_push(const wal_rvq_layer* layer, const uint16_t* x, int64_t M, int64_t ldx,
+                      const wal_tp_push* push, void* stream);
+
+/*
+ * Receiving half of the exchange.  recv: this rank's receive slot, words
+ * [num_ranks][rank_stride] with rows ld words apart; epoch/done: this rank's
+ * call count and CTA counter of the slot (device, start at zero).  Waits
+ * until every word of rows < M carries tag *epoch + 1 (bounded, about 2 s),
+ * then h <- bf16(h + bf16(sum_p value_p)) (fp32 sum in rank order),
+ * x_out <- bf16(RMSNorm(h) * norm_weight), and *epoch += 1.  On timeout writes
+ * WAL_ERR_PEER_TIMEOUT to *status (if not NULL) and leaves h, x_out and the
+ * call count unchanged.  h, norm_weight, x_out: bf16; N % 8 == 0, N <= 16384.
+ */
+WAL_API int wal_tp_reduce_rmsnorm(const void* recv, int32_t num_ranks, int64_t rank_stride, int64_t ld,
+                          uint32_t* epoch, uint32_t* done, uint16_t* h, int64_t ldh,
+                          const uint16_t* norm_weight, float eps, uint16_t* x_out, int64_t ldx,
+                          int64_t M, int64_t N, int* status, void* stream);
+
+/*
+ * Local form: h <- bf16(h + bf16(partial)) when partial (fp32, rows ldp apart)
+ * is not NULL, then x_out <- bf16(h * rsqrt(mean(h^2) + eps) * norm_weight).
+ */
+WAL_API int wal_residual_rmsnorm(const float* partial, int64_t ldp, uint16_t* h, int64_t ldh,
+                         const uint16_t* norm_weight, float eps, uint16_t* x_out, int64_t ldx,
+                         int64_t M, int64_t N, void* stream);
+
+/*
+ * Rotary embedding (rotate-half) of q and k for one position plus the KV
+ * cache append.  qkv: bf16 [M, ld_qkv] holding q (hq heads), k, v (hkv heads
+ * each) of head_dim hd.  cos/sin: fp32 [hd].  q_out: bf16 [M, hq * hd].
+ * k_cache/v_cache: bf16 [M, hkv, cache_len, hd] (contiguous); position pos
+ * is written.  Rounding as x.float() * cos + rotate_half(x).float() * sin
+ * with separately rounded products, then one bf16 rounding.
+ */
+WAL_API int wal_rope_kv_append(const uint16_t* qkv, int64_t ld_qkv, int64_t M, int32_t hq, int32_t hkv,
+                       int32_t hd, const float* cos, const float* sin, int64_t pos, uint16_t* q_out,
+                       uint16_t* k_cache, uint16_t* v_cache, int64_t cache_len, void* stream);
+
+/* out[m, i] = bf16(bf16(silu(g[m, i])) * u[m, i]) with g = gu[m, 0:I], u = gu[m, I:2I] (bf16). */
+WAL_API int wal_silu_mul(const uint16_t* gu, int64_t ld_gu, int64_t M, int64_t I, uint16_t* out,
+                 int64_t ld_out, void* stream);
+
+/*
+ * Device memory shared with peer processes: create (cudaMalloc, zero-filled,
+ * IPC handle of WAL_IPC_HANDLE_BYTES written to handle_out), open a peer's
+ * handle (mapped with peer access), close a mapping, free own memory.
+ */
+WAL_API int wal_peer_region_create(size_t bytes, void** dev_ptr, void* handle_out);
+WAL_API int wal_peer_region_open(const void* handle, void** dev_ptr);
+WAL_API int wal_peer_region_close(void* dev_ptr);
+WAL_API int wal_peer_region_free(void* dev_ptr);
 
 #ifdef __cplusplus
 }

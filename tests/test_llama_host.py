@@ -7,7 +7,7 @@ import torch
 from wal2026_b200.llama import LLAMA_8B, LlamaShape, TPContext, dense_llama, rvq_llama
 from wal2026_b200.runtime import PackedGroupedBlockRVQLinear
 
-TINY = LlamaShape(layers=2, hidden=256, mlp=512, heads=8, kv_heads=4, vocab=1024)
+TINY = LlamaShape(layers=2, hidden=512, mlp=1024, heads=8, kv_heads=4, vocab=1024)
 
 
 def test_rvq_stack_builds_packed_projections():

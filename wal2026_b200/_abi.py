@@ -22,6 +22,10 @@ WAL_ERR_ID_RANGE = 4
 WAL_ERR_UNSUPPORTED = 5
 WAL_ERR_CUDA = 6
 WAL_ERR_BUFFER_TOO_SMALL = 7
+WAL_ERR_PEER_TIMEOUT = 8
+
+WAL_MAX_RANKS = 8
+WAL_IPC_HANDLE_BYTES = 64
 
 WAL_BF16 = 0
 WAL_F32 = 1
@@ -59,6 +63,17 @@ class Layer(ctypes.Structure):
     ]
 
 
+class TPPush(ctypes.Structure):
+    """``wal_tp_push``: where a row-parallel GEMV stores its tagged partial."""
+    _fields_ = [
+        ("num_ranks", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("dst", ctypes.c_void_p * WAL_MAX_RANKS),
+        ("ld_dst", ctypes.c_int64),
+        ("epoch", ctypes.c_void_p),
+    ]
+
+
 _GP = ctypes.POINTER(Geometry)
 _LP = ctypes.POINTER(Layer)
 
@@ -75,6 +90,18 @@ SIGNATURES: dict[str, tuple] = {
     "wal_rvq_gemm": (_c_int, [_LP, _vp, _c_i64, _c_i64, _vp, _c_i64, _c_int, _vp, _vp]),
     "wal_rvq_dequant": (_c_int, [_LP, _vp, _c_i64, _vp]),
     "wal_rvq_unpack_ids": (_c_int, [_LP, _vp, _vp]),
+    "wal_rvq_gemv_push": (_c_int, [_LP, _vp, _c_i64, _c_i64, ctypes.POINTER(TPPush), _vp]),
+    "wal_tp_reduce_rmsnorm": (_c_int, [_vp, ctypes.c_int32, _c_i64, _c_i64, _vp, _vp, _vp, _c_i64, _vp,
+                                       ctypes.c_float, _vp, _c_i64, _c_i64, _c_i64, _vp, _vp]),
+    "wal_residual_rmsnorm": (_c_int, [_vp, _c_i64, _vp, _c_i64, _vp, ctypes.c_float, _vp, _c_i64, _c_i64, _c_i64,
+                                      _vp]),
+    "wal_rope_kv_append": (_c_int, [_vp, _c_i64, _c_i64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _vp, _vp,
+                                    _c_i64, _vp, _vp, _vp, _c_i64, _vp]),
+    "wal_silu_mul": (_c_int, [_vp, _c_i64, _c_i64, _c_i64, _vp, _c_i64, _vp]),
+    "wal_peer_region_create": (_c_int, [ctypes.c_size_t, ctypes.POINTER(_vp), _vp]),
+    "wal_peer_region_open": (_c_int, [_vp, ctypes.POINTER(_vp)]),
+    "wal_peer_region_close": (_c_int, [_vp]),
+    "wal_peer_region_free": (_c_int, [_vp]),
 }
 
 _lib = None
@@ -117,7 +144,7 @@ def check(status: int, where: str) -> None:
     """Map a wal_status to the exception the reference raises for the same condition."""
     if status == WAL_OK:
         return
-    if status == WAL_ERR_CUDA:
+    if status in (WAL_ERR_CUDA, WAL_ERR_PEER_TIMEOUT):
         raise WalError(status, where)
     raise WalValueError(status, where)
 

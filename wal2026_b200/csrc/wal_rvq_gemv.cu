@@ -1,4 +1,4 @@
-// Decode-time fused gather-GEMV (M <= 16 tokens), weight materialisation and
+// Decode-time fused gather-GEMV (up to 32 tokens per launch), weight materialisation and
 // packed-id unpacking for the Block-RVQ runtime linear.
 //
 // GEMV structure (one persistent wave of CTAs, 8 warps each):
@@ -48,6 +48,13 @@ struct GemvParams {
   int pdl;                               // launched with programmatic dependent launch
   int group_tile_start[kMaxGroups + 1];  // first tile of each group, plus the total
   int group_row_start[kMaxGroups + 1];   // first output row of each group, plus N
+  // tensor-parallel push (push_ranks > 0): every fp32 output goes, as an
+  // 8-byte word {value, tag}, to push_dst[p] for every rank p instead of y;
+  // tag = *push_epoch + 1 (the slot's call count, read after the dependency)
+  int push_ranks;
+  long long push_ld;
+  uint2* push_dst[WAL_MAX_RANKS];
+  const unsigned* push_epoch;
 };
 
 namespace {
@@ -64,6 +71,7 @@ constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kRing = 4;  // chunks in flight per warp (power of two)
 constexpr int kXSmemBudget = 64 * 1024;
+constexpr int kMaxTokens = 32;  // tokens per GEMV launch (four n-tiles of 8); more run as slabs
 
 
 __device__ __forceinline__ void store_out(void* y, long long idx, float v, int dtype) {
@@ -73,6 +81,22 @@ __device__ __forceinline__ void store_out(void* y, long long idx, float v, int d
     static_cast<__nv_bfloat16*>(y)[idx] = __float2bfloat16_rn(v);
   } else {
     static_cast<__half*>(y)[idx] = __float2half_rn(v);
+  }
+}
+
+// One output element: y (dtype) or, in push mode, a tagged 8-byte word into
+// every rank's receive rows (remote ranks through NVLink peer mappings).
+__device__ __forceinline__ void emit_out(const GemvParams& p, unsigned tag, int m, int row, float v) {
+  if (p.push_ranks > 0) {
+    const long long idx = (long long)m * p.push_ld + row;
+#pragma unroll
+    for (int r = 0; r < WAL_MAX_RANKS; ++r)
+      if (r < p.push_ranks)
+        asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};\n" ::"l"(p.push_dst[r] + idx),
+                     "r"(__float_as_uint(v)), "r"(tag)
+                     : "memory");
+  } else {
+    store_out(p.y, (long long)m * p.ldy + row, v, p.y_dtype);
   }
 }
 
@@ -146,9 +170,8 @@ struct GemvCfg {
 template <int D, int R, int IDW, bool REPL, int MT, bool XS, bool MASK>
 __device__ __forceinline__ void gemv_chunk(float (&acc)[2][MT][4], const uint32_t (&c0)[R * IDW * 4],
                                            const uint32_t (&c1)[R * IDW * 4], uint32_t cb, uint32_t cbl, uint32_t rho_a,
-                                           uint32_t rho_b, const LaneSel& ls, const uint16_t* xrow0,
-                                           const uint16_t* xrow1, uint32_t xs0, uint32_t xs1, bool xv0, bool xv1,
-                                           int col_base, int K) {
+                                           uint32_t rho_b, const LaneSel& ls, const uint16_t* const (&xrow)[MT],
+                                           const uint32_t (&xsa)[MT], const bool (&xv)[MT], int col_base, int K) {
   using C = GemvCfg<D, R, IDW, REPL, MT, XS>;
   static_for<0, D>([&](auto ktc) {
     constexpr int kt = decltype(ktc)::value;
@@ -156,22 +179,24 @@ __device__ __forceinline__ void gemv_chunk(float (&acc)[2][MT][4], const uint32_
     decode_row<D, R, IDW, REPL, kt, C::NW>(ra, c0, cb, cbl, rho_a, ls);
     decode_row<D, R, IDW, REPL, kt, C::NW>(rb, c1, cb, cbl, rho_b, ls);
     const int col = col_base + kt * 16;  // lane's first physical column (includes 4q)
-    uint2 xa = make_uint2(0u, 0u), xb = make_uint2(0u, 0u);
     const bool in_k = !MASK || col < K;
-    if (XS) {  // rows beyond M read the zero row: no predicate
-      xa = lds64_ordered<kt * 32>(xs0 + col_base * 2);
-      if (MT == 2) xb = lds64_ordered<kt * 32>(xs1 + col_base * 2);
-    } else {
-      if (xv0 && in_k) xa = __ldg(reinterpret_cast<const uint2*>(xrow0 + col));
-      if (MT == 2 && xv1 && in_k) xb = __ldg(reinterpret_cast<const uint2*>(xrow1 + col));
+    uint2 xf[MT];
+#pragma unroll
+    for (int i = 0; i < MT; ++i) {
+      if (XS) {  // rows beyond M read the zero row: no predicate
+        xf[i] = lds64_ordered<kt * 32>(xsa[i] + col_base * 2);
+      } else {
+        xf[i] = make_uint2(0u, 0u);
+        if (xv[i] && in_k) xf[i] = __ldg(reinterpret_cast<const uint2*>(xrow[i] + col));
+      }
     }
     uint32_t a[4] = {ra[0], rb[0], ra[1], rb[1]};
     if (MASK && !in_k) {
       a[0] = a[1] = a[2] = a[3] = 0u;
     }
     // even and odd k-tiles feed separate accumulators: two independent MMA chains
-    mma_bf16_16816(acc[kt & 1][0], a, xa.x, xa.y);
-    if (MT == 2) mma_bf16_16816(acc[kt & 1][MT - 1], a, xb.x, xb.y);
+#pragma unroll
+    for (int i = 0; i < MT; ++i) mma_bf16_16816(acc[kt & 1][i], a, xf[i].x, xf[i].y);
   });
 }
 
@@ -250,7 +275,18 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
 
   // -- prologue: weights (static) first, activations after the dependency --
   // group 0: codebooks (+ activations); groups 1..kRing-1: the first id chunks
+  // Everything that depends only on the weights (codebooks, first id chunks,
+  // the replicated codebook build) happens before the grid-dependency wait,
+  // so with programmatic dependent launch it overlaps the previous kernel;
+  // only the activations wait for it.
+  // groups: 0 = codebooks, 1..kRing-1 = first id chunks, kRing = activations
   stage_codebooks_issue<D, R, REPL>(cb, p.codebooks + (size_t)group * R * p.entries * D, p.entries);
+  cp_async_commit();
+#pragma unroll 1
+  for (int s = 0; s < kRing - 1; ++s) issue();
+  cp_async_wait<kRing - 1>();  // codebooks landed
+  __syncthreads();
+  stage_codebooks_finish<D, R, REPL>(cb, p.entries);
   if (p.pdl) grid_dependency_wait();  // x (and y) belong to the previous kernel in the stream
   if (XS) {
     const uint64_t x_pol = l2_policy_evict_last();
@@ -276,19 +312,23 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
     }
   }
   cp_async_commit();
-#pragma unroll 1
-  for (int s = 0; s < kRing - 1; ++s) issue();
-  cp_async_wait<kRing - 1>();  // group 0 landed
-  __syncthreads();
-  stage_codebooks_finish<D, R, REPL>(cb, p.entries);
+  // push tag: the slot's call count advances only in the receiving kernel,
+  // which runs after this one
+  const unsigned tag = p.push_ranks > 0 ? *reinterpret_cast<const volatile unsigned*>(p.push_epoch) + 1u : 0u;
+  cp_async_wait<0>();
   __syncthreads();
 
-  const int m0 = r, m1 = 8 + r;
-  const bool xv0 = m0 < p.M, xv1 = (MT == 2) && (m1 < p.M);
-  const uint16_t* xrow0 = p.x + (long long)(xv0 ? m0 : 0) * p.ldx;
-  const uint16_t* xrow1 = p.x + (long long)(xv1 ? m1 : 0) * p.ldx;
-  const uint32_t xs0 = smem_u32(xs) + (uint32_t)((xv0 ? m0 : p.M) * C::x_stride(kpad));
-  const uint32_t xs1 = smem_u32(xs) + (uint32_t)((xv1 ? m1 : p.M) * C::x_stride(kpad));
+  // lane (r, q) feeds token 8 * i + r of n-tile i
+  const uint16_t* xrow[MT];
+  uint32_t xsa[MT];
+  bool xv[MT];
+#pragma unroll
+  for (int i = 0; i < MT; ++i) {
+    const int m = 8 * i + r;
+    xv[i] = m < p.M;
+    xrow[i] = p.x + (long long)(xv[i] ? m : 0) * p.ldx;
+    xsa[i] = smem_u32(xs) + (uint32_t)((xv[i] ? m : p.M) * C::x_stride(kpad));
+  }
   const bool need_mask = kpad != p.K;
   const uint32_t cb_s = smem_u32(cb);
   const uint32_t cbl = cb_s + L::lane_offset(r, q);
@@ -342,11 +382,11 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
         const int c = kpart + j * wpt;
         const int col_base = c * kChunkBlocks * D + 4 * q;
         if (need_mask && c == p.chunks - 1) {
-          gemv_chunk<D, R, IDW, REPL, MT, XS, true>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, xrow0, xrow1, xs0, xs1, xv0,
-                                                    xv1, col_base, p.K);
+          gemv_chunk<D, R, IDW, REPL, MT, XS, true>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, xrow, xsa, xv,
+                                                    col_base, p.K);
         } else {
-          gemv_chunk<D, R, IDW, REPL, MT, XS, false>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, xrow0, xrow1, xs0, xs1,
-                                                     xv0, xv1, col_base, p.K);
+          gemv_chunk<D, R, IDW, REPL, MT, XS, false>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, xrow, xsa, xv,
+                                                     col_base, p.K);
         }
       }
     }
@@ -363,7 +403,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
           if (row < nrows && m < p.M) {
             float v = acc[0][i][e] + acc[1][i][e];
             if (p.bias) v += __bfloat162float(__ushort_as_bfloat16(p.bias[row0 + row]));
-            store_out(p.y, (long long)m * p.ldy + row0 + row, v, p.y_dtype);
+            emit_out(p, tag, m, row0 + row, v);
           }
         }
       }
@@ -387,7 +427,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
       for (int w = 0; w < wpt; ++w) v += sred[(w * 16 + row) * MC + m];
       const int orow = row0 + row;
       if (p.bias) v += __bfloat162float(__ushort_as_bfloat16(p.bias[orow]));
-      store_out(p.y, (long long)m * p.ldy + orow, v, p.y_dtype);
+      emit_out(p, tag, m, orow, v);
     }
   }
   cp_async_wait<0>();
@@ -580,20 +620,24 @@ static int run_dequant(const GemvParams& p, uint16_t* w, long long ldw, cudaStre
   return cudaGetLastError() == cudaSuccess ? WAL_OK : WAL_ERR_CUDA;
 }
 
+// mt: n-tiles of 8 tokens per launch (1, 2 or 4); xs: activations staged in
+// shared memory (never for 4 n-tiles: 32 rows of activations do not fit)
 template <int D, int R, int IDW>
 static int dispatch_gemv(const GemvParams& p, int num_ctas, cudaStream_t stream, bool repl, int mt, bool xs) {
   if constexpr (IDW == 1) {
     if (repl) {
       if (mt == 1) return xs ? run_gemv<D, R, IDW, true, 1, true>(p, num_ctas, stream)
                              : run_gemv<D, R, IDW, true, 1, false>(p, num_ctas, stream);
-      return xs ? run_gemv<D, R, IDW, true, 2, true>(p, num_ctas, stream)
-                : run_gemv<D, R, IDW, true, 2, false>(p, num_ctas, stream);
+      if (mt == 2) return xs ? run_gemv<D, R, IDW, true, 2, true>(p, num_ctas, stream)
+                             : run_gemv<D, R, IDW, true, 2, false>(p, num_ctas, stream);
+      return run_gemv<D, R, IDW, true, 4, false>(p, num_ctas, stream);
     }
   }
   if (mt == 1) return xs ? run_gemv<D, R, IDW, false, 1, true>(p, num_ctas, stream)
                          : run_gemv<D, R, IDW, false, 1, false>(p, num_ctas, stream);
-  return xs ? run_gemv<D, R, IDW, false, 2, true>(p, num_ctas, stream)
-            : run_gemv<D, R, IDW, false, 2, false>(p, num_ctas, stream);
+  if (mt == 2) return xs ? run_gemv<D, R, IDW, false, 2, true>(p, num_ctas, stream)
+                         : run_gemv<D, R, IDW, false, 2, false>(p, num_ctas, stream);
+  return run_gemv<D, R, IDW, false, 4, false>(p, num_ctas, stream);
 }
 
 template <int D, int R, int IDW>
@@ -677,13 +721,27 @@ static int make_params(const wal_rvq_layer* L, GemvParams* p) {
   return group_starts(L, p);
 }
 
-extern "C" int wal_rvq_gemv_ex(const wal_rvq_layer* layer, const uint16_t* x, int64_t M, int64_t ldx, void* y,
-                               int64_t ldy, int y_dtype, int warps_per_tile, int num_ctas, void* stream) {
+// Shared body of the GEMV entry points; push == NULL writes y, otherwise the
+// fp32 rows go to every rank's receive rows (y, ldy, y_dtype unused).
+static int gemv_common(const wal_rvq_layer* layer, const uint16_t* x, int64_t M, int64_t ldx, void* y, int64_t ldy,
+                       int y_dtype, int warps_per_tile, int num_ctas, const wal_tp_push* push, void* stream) {
   int st = check_layer(layer);
   if (st != WAL_OK) return st;
-  if (!x || !y) return WAL_ERR_INVALID_ARGUMENT;
+  if (!x || (!y && !push)) return WAL_ERR_INVALID_ARGUMENT;
   if (M <= 0) return WAL_ERR_SHAPE;
   const wal_rvq_geometry& g = layer->geom;
+  if (push) {
+    if (push->num_ranks < 1 || push->num_ranks > WAL_MAX_RANKS || push->rank < 0 || push->rank >= push->num_ranks)
+      return WAL_ERR_INVALID_ARGUMENT;
+    if (!push->epoch) return WAL_ERR_INVALID_ARGUMENT;
+    for (int r = 0; r < push->num_ranks; ++r) {
+      if (!push->dst[r]) return WAL_ERR_INVALID_ARGUMENT;
+      if ((uintptr_t)push->dst[r] & 7) return WAL_ERR_ALIGNMENT;
+    }
+    if (push->ld_dst < g.out_features) return WAL_ERR_SHAPE;
+    ldy = g.out_features;
+    y_dtype = WAL_F32;
+  }
   if (ldx < g.in_features || ldy < g.out_features) return WAL_ERR_SHAPE;
   if ((ldx % 4) || ((uintptr_t)x & 7)) return WAL_ERR_ALIGNMENT;
   if (y_dtype != WAL_BF16 && y_dtype != WAL_F32 && y_dtype != WAL_F16) return WAL_ERR_INVALID_ARGUMENT;
@@ -722,16 +780,26 @@ extern "C" int wal_rvq_gemv_ex(const wal_rvq_layer* layer, const uint16_t* x, in
   p.ldy = ldy;
   p.y_dtype = y_dtype;
   p.pdl = 1;
+  if (push) {
+    p.push_ranks = push->num_ranks;
+    p.push_ld = push->ld_dst;
+    p.push_epoch = push->epoch;
+    p.bias = nullptr;  // partial sums of a row-parallel split carry no bias
+  }
   const size_t ysz = y_dtype == WAL_F32 ? 4 : 2;
   const int kpad = p.chunks * kChunkBlocks * d;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  for (int64_t m0 = 0; m0 < M; m0 += 16) {
-    const int mm = (int)((M - m0) < 16 ? (M - m0) : 16);
+  for (int64_t m0 = 0; m0 < M; m0 += kMaxTokens) {
+    const int mm = (int)((M - m0) < kMaxTokens ? (M - m0) : kMaxTokens);
     p.x = x + m0 * ldx;
-    p.y = static_cast<uint8_t*>(y) + (size_t)(m0 * ldy) * ysz;
+    if (push) {
+      for (int r = 0; r < push->num_ranks; ++r) p.push_dst[r] = static_cast<uint2*>(push->dst[r]) + m0 * push->ld_dst;
+    } else {
+      p.y = static_cast<uint8_t*>(y) + (size_t)(m0 * ldy) * ysz;
+    }
     p.M = mm;
-    const int mt = mm <= 8 ? 1 : 2;
-    const bool xs = (long long)mm * kpad * 2 <= kXSmemBudget;
+    const int mt = mm <= 8 ? 1 : (mm <= 16 ? 2 : 4);
+    const bool xs = mt < 4 && (long long)mm * kpad * 2 <= kXSmemBudget;
     int rs = gemv_by_d(d, p, num_ctas, s, R, idw, repl, mt, xs);
     if (rs == WAL_ERR_UNSUPPORTED && xs)  // activations do not fit beside the codebook
       rs = gemv_by_d(d, p, num_ctas, s, R, idw, repl, mt, false);
@@ -740,9 +808,20 @@ extern "C" int wal_rvq_gemv_ex(const wal_rvq_layer* layer, const uint16_t* x, in
   return WAL_OK;
 }
 
+extern "C" int wal_rvq_gemv_ex(const wal_rvq_layer* layer, const uint16_t* x, int64_t M, int64_t ldx, void* y,
+                               int64_t ldy, int y_dtype, int warps_per_tile, int num_ctas, void* stream) {
+  return gemv_common(layer, x, M, ldx, y, ldy, y_dtype, warps_per_tile, num_ctas, nullptr, stream);
+}
+
 extern "C" int wal_rvq_gemv(const wal_rvq_layer* layer, const uint16_t* x, int64_t M, int64_t ldx, void* y,
                             int64_t ldy, int y_dtype, void* stream) {
-  return wal_rvq_gemv_ex(layer, x, M, ldx, y, ldy, y_dtype, 0, 0, stream);
+  return gemv_common(layer, x, M, ldx, y, ldy, y_dtype, 0, 0, nullptr, stream);
+}
+
+extern "C" int wal_rvq_gemv_push(const wal_rvq_layer* layer, const uint16_t* x, int64_t M, int64_t ldx,
+                                 const wal_tp_push* push, void* stream) {
+  if (!push) return WAL_ERR_INVALID_ARGUMENT;
+  return gemv_common(layer, x, M, ldx, nullptr, 0, WAL_F32, 0, 0, push, stream);
 }
 
 extern "C" int wal_rvq_dequant(const wal_rvq_layer* layer, uint16_t* w, int64_t ldw, void* stream) {

@@ -83,6 +83,7 @@ const char* wal_status_string(int status) {
     case WAL_ERR_UNSUPPORTED: return "configuration not implemented by this build";
     case WAL_ERR_CUDA: return "CUDA runtime error";
     case WAL_ERR_BUFFER_TOO_SMALL: return "caller buffer too small";
+    case WAL_ERR_PEER_TIMEOUT: return "a peer rank's data did not arrive within the wait limit";
     default: return "unknown status";
   }
 }

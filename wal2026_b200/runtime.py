@@ -208,6 +208,16 @@ class PackedGroupedBlockRVQLinear(nn.Module):
                              num_groups=len(group_rows))
         arrays = PackedArrays(geom, T, packed, torch.tensor(table, dtype=torch.int32, device=device),
                               books.to(torch.float16).contiguous(), rho.to(torch.float16).contiguous())
+        return cls.from_packed(arrays, group_rows, bias=bias)
+
+    @classmethod
+    def from_packed(cls, arrays: PackedArrays, group_rows: list[int],
+                    bias: Optional[Tensor] = None) -> "PackedGroupedBlockRVQLinear":
+        """A module over already packed arrays (e.g. a tensor-parallel shard of another module)."""
+        g = arrays.geometry
+        K, N, d, R = int(g.in_features), int(g.out_features), int(g.block_size), int(g.num_stages)
+        if sum(int(n) for n in group_rows) != N or len(group_rows) != int(g.num_groups):
+            raise ValueError("group_rows do not match the packed geometry")
         obj = cls.__new__(cls)
         nn.Module.__init__(obj)
         obj.in_features, obj.out_features = K, N
@@ -223,11 +233,22 @@ class PackedGroupedBlockRVQLinear(nn.Module):
         obj.groups = nn.ModuleList(PackedBlockRVQGroup(obj, r0, r1, block_size=d, in_features=K, num_stages=R)
                                    for r0, r1 in obj.row_slices)
         if bias is not None:
-            obj.register_buffer("bias", bias.detach().to(device=device, dtype=torch.bfloat16).reshape(-1))
+            obj.register_buffer("bias", bias.detach().to(device=arrays.packed_ids.device,
+                                                         dtype=torch.bfloat16).reshape(-1).contiguous())
         else:
             obj.bias = None
         obj._layer_cache = None
         return obj
+
+    def packed_arrays(self) -> PackedArrays:
+        """This module's packed buffers (shared, not copied)."""
+        geom = _abi.Geometry(out_features=self.out_features, in_features=self.in_features,
+                             block_size=self.block_size, num_stages=self.num_stages,
+                             num_entries=self.num_entries, num_groups=self.num_groups)
+        return PackedArrays(geom, self.num_tiles, self.packed_ids, self.tile_table, self.codebooks, self.row_scale)
+
+    def group_rows(self) -> list[int]:
+        return [r1 - r0 for r0, r1 in self.row_slices]
 
     # -- C ABI plumbing -----------------------------------------------------
     def layer_struct(self) -> _abi.Layer:
