@@ -17,6 +17,16 @@ Arms:
 
 Multi-GPU (torchrun): every rank runs its own instances (weak scaling, no
 collective on the data path); the time is the max over ranks.
+
+Also reported in the same JSON line (BASELINE's second metric and config 3):
+  decode_8b   Llama-3-8B-shaped stack (random init, every projection Block-RVQ
+              d=8, R=2, 256 entries; dense bf16 lm_head), one CUDA graph per
+              decode step at a 2048-token context, tensor-parallel over all
+              N GPUs (NVLink push exchange after the row-parallel linears),
+              next to the same stack with dense bf16 cuBLAS projections;
+  prefill_8b  (N = 1) the stack's 128 projection GEMMs at M = 2048 tokens on
+              the tcgen05 decode-to-shared-memory GEMM, TFLOP/s against the
+              measured bf16 peak, next to cuBLAS on the same shapes.
 """
 from __future__ import annotations
 
@@ -210,6 +220,107 @@ def _config(args) -> dict:
     }
 
 
+def run_decode(args, rank: int, world: int, dev: torch.device) -> dict:
+    """8B-shaped decode tok/s, tensor-parallel over every rank (all ranks call this together)."""
+    import torch.distributed as dist
+
+    from wal2026_b200.llama import LLAMA_8B, TPContext, dense_llama, rvq_llama, time_decode
+
+    tp = TPContext(rank, world, dist.group.WORLD if world > 1 else None)
+    batches = [int(b) for b in args.decode_batches.split(",") if b]
+    out = {"model": "Llama-3-8B shape (32 layers, hidden 4096, MLP 14336, 32 q / 8 kv heads, vocab 128256), "
+                    "random init; q/k/v/o/gate/up/down Block-RVQ d=8 R=2 256 entries; lm_head dense bf16",
+           "context": args.context, "tp": world, "exchange": "nvlink push (tagged words)" if world > 1 else "none",
+           "graph": "one CUDA graph per decode step", "steps": args.decode_steps}
+    for kind, ctor, exchange in (("rvq", rvq_llama, "push"), ("dense_bf16_cublas", dense_llama, "nccl")):
+        if kind.startswith("dense") and not args.dense:
+            continue
+        st = ctor(LLAMA_8B, device=dev, seed=0, tp=tp)
+        res = {}
+        for b in batches:
+            r = time_decode(st, b, args.context, steps=args.decode_steps, warmup=3, fused=True, exchange=exchange)
+            res[str(b)] = {"tok_s": round(r["tok_s"], 1), "ms_per_step": round(r["ms_per_step"], 4)}
+        if kind == "rvq":
+            out["rvq_projection_bytes_per_rank"] = st.linear_bytes()
+        st.close()
+        del st
+        torch.cuda.empty_cache()
+        out[kind] = res
+    if "dense_bf16_cublas" in out:
+        out["rvq_speedup_vs_dense"] = {b: round(out["rvq"][b]["tok_s"] / out["dense_bf16_cublas"][b]["tok_s"], 3)
+                                       for b in out["rvq"]}
+    return out
+
+
+def run_prefill(args, dev: torch.device, peaks: dict) -> dict:
+    """8B-shaped prefill GEMMs (M = 2048) on the tcgen05 path, one CUDA graph of all 128 projections."""
+    import torch.nn.functional as F
+
+    from wal2026_b200.llama import LLAMA_8B, rvq_llama
+
+    M = args.prefill_tokens
+    st = rvq_llama(LLAMA_8B, device=dev, seed=0)
+    lins = [getattr(layer, n) for layer in st.layers for n in ("qkv", "o", "gate_up", "down")]
+    xs = {k: torch.randn(M, k, device=dev).to(torch.bfloat16) for k in {lin.in_features for lin in lins}}
+    ys = {n: torch.empty(M, n, device=dev, dtype=torch.bfloat16) for n in {lin.out_features for lin in lins}}
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def run():
+        for lin in lins:
+            if not lin.gemm_into(xs[lin.in_features], ys[lin.out_features], status):
+                raise RuntimeError("prefill GEMM path does not cover this layer")
+
+    run()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        run()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.prefill_steps):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if int(status.item()) != 0:
+        raise RuntimeError("prefill GEMM reported a pipeline timeout")
+    ms = e0.elapsed_time(e1) / args.prefill_steps
+    flops = sum(2.0 * M * lin.out_features * lin.in_features for lin in lins)
+    tflops = flops / (ms / 1e3) / 1e12
+    del g
+    # cuBLAS bf16 on the same shapes (one layer's four dense weights, repeated for 32 layers)
+    dense = None
+    if args.dense:
+        ws = [torch.randn(lin.out_features, lin.in_features, device=dev).to(torch.bfloat16) for lin in lins[:4]]
+        for w in ws:
+            F.linear(xs[w.shape[1]], w)
+        torch.cuda.synchronize()
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        d0.record(stream)
+        for _ in range(args.prefill_steps):
+            for _layer in range(LLAMA_8B.layers):
+                for w in ws:
+                    F.linear(xs[w.shape[1]], w)
+        d1.record(stream)
+        torch.cuda.synchronize()
+        dms = d0.elapsed_time(d1) / args.prefill_steps
+        dense = {"ms_per_step": round(dms, 3), "tflops": round(flops / (dms / 1e3) / 1e12, 1)}
+        del ws
+    peak = float(peaks.get("bf16_tflops_sustained") or 1400.0)
+    src = "measured bf16_tflops_sustained" if peaks.get("bf16_tflops_sustained") else "fallback"
+    launches = len(lins) * args.prefill_steps
+    del st, lins
+    torch.cuda.empty_cache()
+    return {"workload": f"Llama-3-8B-shaped stack, 128 projection GEMMs at M={M} tokens (x bf16, y bf16)",
+            "ms_per_step": round(ms, 3), "tokens_per_s": round(M / (ms / 1e3), 1), "tflops": round(tflops, 1),
+            "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(tflops / peak, 4), "peak_source": src, "kernel": "rvq_gemm_kernel"},
+            "gpu_launches": launches, "dense_bf16_cublas": dense}
+
+
 def run_ours(args) -> None:
     import torch.distributed as dist
 
@@ -316,7 +427,9 @@ def run_ours(args) -> None:
                  "rvq_speedup": round(dms / (per_launch_s * 1e3), 3)}
         del ws
 
+    decode = run_decode(args, rank, world, dev) if args.decode else None
     peaks = measured_peaks()
+    prefill = run_prefill(args, dev, peaks) if (args.prefill and world == 1) else None
     peak = peaks.get("hbm_gbs")
     peak_src = "measured" if peak else "fallback"
     peak = float(peak or 6650.0)
@@ -346,6 +459,8 @@ def run_ours(args) -> None:
             "clocks": clocks,
             "cpu_baseline": cpu,
             "dense_bf16_cublas": dense,
+            "decode_8b": decode,
+            "prefill_8b": prefill,
         }
         print(json.dumps(out), flush=True)
     if world > 1:
@@ -367,6 +482,13 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--dense", type=int, default=1)
+    ap.add_argument("--decode", type=int, default=1, help="also time the 8B-shaped decode step")
+    ap.add_argument("--decode-batches", default="1,8,32")
+    ap.add_argument("--decode-steps", type=int, default=20)
+    ap.add_argument("--context", type=int, default=2048)
+    ap.add_argument("--prefill", type=int, default=1, help="also time the 8B-shaped prefill GEMMs (N = 1)")
+    ap.add_argument("--prefill-tokens", type=int, default=2048)
+    ap.add_argument("--prefill-steps", type=int, default=5)
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
