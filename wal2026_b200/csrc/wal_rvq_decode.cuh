@@ -207,20 +207,50 @@ __device__ void stage_codebooks_issue(uint8_t* cb, const uint16_t* __restrict__ 
 template <int D, int R, bool REPL>
 __device__ void stage_codebooks_finish(uint8_t* cb, int entries) {
   using L = CbLayout<D, REPL>;
-  if (R > 1 && !REPL) return;  // raw fp16 table, single copy: nothing to do
+  if constexpr (!REPL) {
+    if constexpr (R == 1) {  // plain one-stage table: first rounding in place
+      for (int e = threadIdx.x; e < entries; e += blockDim.x) {
 #pragma unroll
-  for (int s = 0; s < R; ++s) {
-    for (int e = threadIdx.x; e < entries; e += blockDim.x) {
-#pragma unroll
-      for (int j = 0; j < L::kPieces; ++j) {
-        uint2 v = *reinterpret_cast<const uint2*>(cb + L::piece_offset(s, e, j, 0, entries));
-        if (R == 1) {
+        for (int j = 0; j < L::kPieces; ++j) {
+          uint2* pv = reinterpret_cast<uint2*>(cb + L::piece_offset(0, e, j, 0, entries));
+          uint2 v = *pv;
           v.x = preround_pair(v.x);
           v.y = preround_pair(v.y);
-          *reinterpret_cast<uint2*>(cb + L::piece_offset(s, e, j, 0, entries)) = v;
+          *pv = v;
+        }
+      }
+    }
+    return;  // raw multi-stage fp16 tables, single copy: nothing to do
+  } else {
+    // An entry's copy 0 is D / 8 runs of 16 bytes (D = 32: two per 128-byte
+    // half); copy c sits c * kCopyStride further.
+    constexpr int kRuns = D / 8;
+    constexpr int kCopyStride = D == 8 ? 16 : 32;
+#pragma unroll
+    for (int s = 0; s < R; ++s) {
+      for (int e = threadIdx.x; e < entries; e += blockDim.x) {
+        uint8_t* base = cb + L::stage_offset(s) + e * 256;
+        uint4 v[kRuns];
+#pragma unroll
+        for (int run = 0; run < kRuns; ++run) {
+          const int off = D == 32 ? (run >> 1) * 128 + (run & 1) * 16 : run * 16;
+          v[run] = *reinterpret_cast<const uint4*>(base + off);
+          if (R == 1) {
+            v[run].x = preround_pair(v[run].x);
+            v[run].y = preround_pair(v[run].y);
+            v[run].z = preround_pair(v[run].z);
+            v[run].w = preround_pair(v[run].w);
+            *reinterpret_cast<uint4*>(base + off) = v[run];
+          }
         }
 #pragma unroll
-        for (int c = 1; c < L::kCopies; ++c) *reinterpret_cast<uint2*>(cb + L::piece_offset(s, e, j, c, entries)) = v;
+        for (int c = 1; c < L::kCopies; ++c) {
+#pragma unroll
+          for (int run = 0; run < kRuns; ++run) {
+            const int off = D == 32 ? (run >> 1) * 128 + (run & 1) * 16 : run * 16;
+            *reinterpret_cast<uint4*>(base + c * kCopyStride + off) = v[run];
+          }
+        }
       }
     }
   }

@@ -46,8 +46,15 @@ struct GemvParams {
   int wpt;
   int num_groups;
   int pdl;                               // launched with programmatic dependent launch
+  int wpt_shift;                         // log2(wpt)
   int group_tile_start[kMaxGroups + 1];  // first tile of each group, plus the total
   int group_row_start[kMaxGroups + 1];   // first output row of each group, plus N
+  // CTA split (host-computed for the launch's grid): group g owns CTAs
+  // [cta_start[g], cta_start[g+1]); its k-th CTA gets tiles_q[g] tiles, plus
+  // one more when k < tiles_r[g]
+  int cta_start[kMaxGroups + 1];
+  int tiles_q[kMaxGroups];
+  int tiles_r[kMaxGroups];
   // tensor-parallel push (push_ranks > 0): every fp32 output goes, as an
   // 8-byte word {value, tag}, to push_dst[p] for every rank p instead of y;
   // tag = *push_epoch + 1 (the slot's call count, read after the dependency)
@@ -111,36 +118,20 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
-// Which group and tile range a CTA owns.  CTAs are dealt to groups in
-// proportion to their tile counts (at least one per group); inside a group the
-// tiles are split evenly.  Identical arithmetic in every CTA.
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 __device__ __forceinline__ void grid_dependents_launch() {
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 }
 
-__device__ void cta_range(const GemvParams& p, int cta, int ctas, int* group, long long* tb, long long* te) {
-  const int G = p.num_groups;
-  const long long T = p.group_tile_start[G];
-  int assigned = 0;
-  for (int g = 0; g < G; ++g) {
-    const long long tg = p.group_tile_start[g + 1] - p.group_tile_start[g];
-    long long cum = ((long long)ctas * p.group_tile_start[g + 1] + T / 2) / T;
-    if (cum < g + 1) cum = g + 1;
-    if (cum > ctas - (G - 1 - g)) cum = ctas - (G - 1 - g);
-    if (g == G - 1) cum = ctas;
-    const int n = (int)cum - assigned;
-    if (cta < cum) {
-      const int local = cta - assigned;
-      *group = g;
-      *tb = p.group_tile_start[g] + tg * local / n;
-      *te = p.group_tile_start[g] + tg * (local + 1) / n;
-      return;
-    }
-    assigned = (int)cum;
-  }
-  *group = 0;
-  *tb = *te = 0;
+// Which group and tile range a CTA owns (division-free: the split is host-computed).
+__device__ __forceinline__ void cta_range(const GemvParams& p, int cta, int* group, int* tb, int* te) {
+  int g = 0;
+  while (g + 1 < p.num_groups && cta >= p.cta_start[g + 1]) ++g;
+  const int local = cta - p.cta_start[g];
+  const int q = p.tiles_q[g], rem = p.tiles_r[g];
+  *group = g;
+  *tb = p.group_tile_start[g] + local * q + (local < rem ? local : rem);
+  *te = *tb + q + (local < rem ? 1 : 0);
 }
 
 template <int D, int R, int IDW, bool REPL, int MT, bool XS>
@@ -153,6 +144,7 @@ struct GemvCfg {
   static constexpr int NW = V * 4;                // 32-bit code words per row-chunk
   static constexpr int kStageBytes = V * 256;     // one chunk of one tile (16 rows)
   static constexpr int MC = MT * 8;
+  static constexpr int kAcc = MT >= 4 ? 1 : 2;  // accumulator sets (k-tile parity)
   __host__ __device__ static int cb_bytes(int entries) { return L::total_bytes(R, entries); }
   // activations: M rows plus one zero row that lanes beyond M read; the row
   // stride is padded by 32 bytes so rows read together fall in different banks
@@ -168,9 +160,9 @@ struct GemvCfg {
 };
 
 template <int D, int R, int IDW, bool REPL, int MT, bool XS, bool MASK>
-__device__ __forceinline__ void gemv_chunk(float (&acc)[2][MT][4], const uint32_t (&c0)[R * IDW * 4],
+__device__ __forceinline__ void gemv_chunk(float (&acc)[GemvCfg<D, R, IDW, REPL, MT, XS>::kAcc][MT][4], const uint32_t (&c0)[R * IDW * 4],
                                            const uint32_t (&c1)[R * IDW * 4], uint32_t cb, uint32_t cbl, uint32_t rho_a,
-                                           uint32_t rho_b, const LaneSel& ls, const uint16_t* const (&xrow)[MT],
+                                           uint32_t rho_b, const LaneSel& ls, const uint16_t* x, const uint32_t (&xoff)[MT],
                                            const uint32_t (&xsa)[MT], const bool (&xv)[MT], int col_base, int K) {
   using C = GemvCfg<D, R, IDW, REPL, MT, XS>;
   static_for<0, D>([&](auto ktc) {
@@ -187,16 +179,17 @@ __device__ __forceinline__ void gemv_chunk(float (&acc)[2][MT][4], const uint32_
         xf[i] = lds64_ordered<kt * 32>(xsa[i] + col_base * 2);
       } else {
         xf[i] = make_uint2(0u, 0u);
-        if (xv[i] && in_k) xf[i] = __ldg(reinterpret_cast<const uint2*>(xrow[i] + col));
+        if (xv[i] && in_k) xf[i] = __ldg(reinterpret_cast<const uint2*>(x + xoff[i] + col));
       }
     }
     uint32_t a[4] = {ra[0], rb[0], ra[1], rb[1]};
     if (MASK && !in_k) {
       a[0] = a[1] = a[2] = a[3] = 0u;
     }
-    // even and odd k-tiles feed separate accumulators: two independent MMA chains
+    // with one or two n-tiles, even and odd k-tiles feed separate accumulators
+    // (independent MMA chains); four n-tiles are four chains already
 #pragma unroll
-    for (int i = 0; i < MT; ++i) mma_bf16_16816(acc[kt & 1][i], a, xf[i].x, xf[i].y);
+    for (int i = 0; i < MT; ++i) mma_bf16_16816(acc[kt % C::kAcc][i], a, xf[i].x, xf[i].y);
   });
 }
 
@@ -218,28 +211,29 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, q = lane & 3;
-  const int wpt = p.wpt;
-  const int slots = kWarps / wpt;
-  const int slot = warp / wpt, kpart = warp - slot * wpt;
+  static_assert(kWarps == 16, "warp split assumes 16 warps");
+  const int wpt = p.wpt, wsh = p.wpt_shift;  // wpt = 1 << wsh
+  const int ssh = 4 - wsh;                    // slots = 16 / wpt = 1 << ssh
+  const int slots = 1 << ssh;
+  const int slot = warp >> wsh, kpart = warp & (wpt - 1);
   const LaneSel ls(r, q);
 
-  int group;
-  long long tb, te;
-  cta_range(p, blockIdx.x, gridDim.x, &group, &tb, &te);
+  int group, tb, te;
+  cta_range(p, blockIdx.x, &group, &tb, &te);
   if (tb >= te) {
     if (p.pdl) grid_dependents_launch();
     return;
   }
-  const long long g_tile0 = p.group_tile_start[group];
+  const int g_tile0 = p.group_tile_start[group];
   const int g_row0 = p.group_row_start[group], g_row1 = p.group_row_start[group + 1];
 
   // -- this warp's flat item list: rounds of `slots` tiles x its chunks -----
-  const int cpw = kpart < p.chunks ? (p.chunks - kpart + wpt - 1) / wpt : 0;  // chunks per tile
-  const long long ntiles = te - tb;
-  const long long rounds = (ntiles + slots - 1) / slots;
+  const int cpw = kpart < p.chunks ? (p.chunks - kpart + wpt - 1) >> wsh : 0;  // chunks per tile
+  const int ntiles = te - tb;
+  const int rounds = (ntiles + slots - 1) >> ssh;
   // tiles this warp owns: tb + slot + k * slots, k < my_rounds
-  const long long my_rounds = slot < ntiles ? (ntiles - slot + slots - 1) / slots : 0;
-  const long long items = my_rounds * cpw;
+  const int my_rounds = slot < ntiles ? (ntiles - slot + slots - 1) >> ssh : 0;
+  const int items = my_rounds * cpw;
   const long long tile_bytes = (long long)p.chunks * V * 256;
   uint8_t* wring = ring + warp * kRing * C::kStageBytes;
 
@@ -247,12 +241,15 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
   // to issue, position inside the tile's chunk list, ring slot
   constexpr int kLaneCopies = (C::kStageBytes + 511) / 512;  // 16-byte copies per lane per chunk
   const bool copy_lane = lane * 16 < C::kStageBytes;
-  const uint8_t* is_src = p.packed + (tb + slot) * tile_bytes + (long long)kpart * V * 256 + lane * 16;
-  const long long step_chunk = (long long)wpt * V * 256;
-  const long long step_tile = (long long)slots * tile_bytes - (long long)cpw * step_chunk;
+  // 64-bit base of this warp's first item plus a 32-bit running offset (the
+  // host keeps a CTA's tile span below 2^31 bytes)
+  const uint8_t* is_base = p.packed + (long long)(tb + slot) * tile_bytes + kpart * V * 256 + lane * 16;
+  const uint32_t step_chunk = (uint32_t)(wpt * V * 256);
+  const uint32_t step_tile = (uint32_t)(slots * tile_bytes) - (uint32_t)cpw * step_chunk;
+  uint32_t is_off = 0;
   const uint32_t ring_lane = smem_u32(wring) + lane * 16;
   const uint64_t stream_pol = l2_policy_evict_first();
-  long long is_left = items;
+  int is_left = items;
   int is_j = 0;
   uint32_t is_slot = 0;
   auto issue = [&]() {
@@ -260,13 +257,13 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
       if (copy_lane) {
 #pragma unroll
         for (int k = 0; k < kLaneCopies; ++k)
-          cp_async_16_hint(ring_lane + is_slot * C::kStageBytes + k * 512, is_src + k * 512, stream_pol);
+          cp_async_16_hint(ring_lane + is_slot * C::kStageBytes + k * 512, is_base + is_off + k * 512, stream_pol);
       }
       --is_left;
-      is_src += step_chunk;
+      is_off += step_chunk;
       if (++is_j == cpw) {
         is_j = 0;
-        is_src += step_tile;
+        is_off += step_tile;
       }
     }
     is_slot = (is_slot + 1) & (kRing - 1);
@@ -292,22 +289,25 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
     const uint64_t x_pol = l2_policy_evict_last();
     // rows m < M, columns [0, kpad): zero beyond K
     const int vec_per_row = kpad / 8;  // 16-byte vectors
-    for (int i = threadIdx.x; i < (p.M + 1) * vec_per_row; i += kThreads) {
-      const int m = i / vec_per_row, v = i - m * vec_per_row;
-      uint16_t* dst = xs + (size_t)m * (C::x_stride(kpad) / 2) + v * 8;
-      if (m == p.M) {  // the zero row
-        *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
-        continue;
-      }
-      const int col = v * 8;
-      const uint16_t* src = p.x + (long long)m * p.ldx + col;
-      if (col + 8 <= p.K && ((uintptr_t)src & 15) == 0) {
-        cp_async_16_hint((uint32_t)__cvta_generic_to_shared(dst), src, x_pol);
-      } else if (col + 8 <= p.K) {
-        cp_async_8((uint32_t)__cvta_generic_to_shared(dst), src);
-        cp_async_8((uint32_t)__cvta_generic_to_shared(dst + 4), src + 4);
-      } else {
-        for (int j = 0; j < 8; ++j) dst[j] = col + j < p.K ? p.x[(long long)m * p.ldx + col + j] : (uint16_t)0;
+    for (int m = 0; m <= p.M; ++m) {
+      uint16_t* xdst = xs + (size_t)m * (C::x_stride(kpad) / 2);
+      const uint16_t* xsrc = p.x + (long long)m * p.ldx;
+      for (int v = threadIdx.x; v < vec_per_row; v += kThreads) {
+        uint16_t* dst = xdst + v * 8;
+        if (m == p.M) {  // the zero row
+          *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+          continue;
+        }
+        const int col = v * 8;
+        const uint16_t* src = xsrc + col;
+        if (col + 8 <= p.K && ((uintptr_t)src & 15) == 0) {
+          cp_async_16_hint((uint32_t)__cvta_generic_to_shared(dst), src, x_pol);
+        } else if (col + 8 <= p.K) {
+          cp_async_8((uint32_t)__cvta_generic_to_shared(dst), src);
+          cp_async_8((uint32_t)__cvta_generic_to_shared(dst + 4), src + 4);
+        } else {
+          for (int j = 0; j < 8; ++j) dst[j] = col + j < p.K ? xsrc[col + j] : (uint16_t)0;
+        }
       }
     }
   }
@@ -319,23 +319,27 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
   __syncthreads();
 
   // lane (r, q) feeds token 8 * i + r of n-tile i
-  const uint16_t* xrow[MT];
-  uint32_t xsa[MT];
+  uint32_t xoff[MT];  // element offset of the lane's token row (unstaged activations)
+  uint32_t xsa[MT];   // shared address of the lane's token row (staged activations)
   bool xv[MT];
 #pragma unroll
   for (int i = 0; i < MT; ++i) {
     const int m = 8 * i + r;
     xv[i] = m < p.M;
-    xrow[i] = p.x + (long long)(xv[i] ? m : 0) * p.ldx;
+    xoff[i] = (uint32_t)((xv[i] ? m : 0) * p.ldx);
     xsa[i] = smem_u32(xs) + (uint32_t)((xv[i] ? m : p.M) * C::x_stride(kpad));
   }
-  const bool need_mask = kpad != p.K;
+  // Columns K..kpad of the last chunk decode padding ids.  Staged activations
+  // are zero there, so those products vanish (every decoded weight is finite
+  // for finite codebooks and row scales); only unstaged activations need the
+  // weight fragment masked.
+  const bool need_mask = !XS && kpad != p.K;
   const uint32_t cb_s = smem_u32(cb);
   const uint32_t cbl = cb_s + L::lane_offset(r, q);
 
   // row scales of a tile: tile t covers rows g_row0 + 16 * (t - g_tile0) ...
-  auto tile_rows = [&](long long t, int* row0, int* nrows) {
-    *row0 = g_row0 + (int)(16 * (t - g_tile0));
+  auto tile_rows = [&](int t, int* row0, int* nrows) {
+    *row0 = g_row0 + 16 * (t - g_tile0);
     const int left = g_row1 - *row0;
     *nrows = left < 16 ? left : 16;
   };
@@ -347,12 +351,12 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
     nrho_b = r + 8 < nrows ? rho_pair(p.row_scale[row0 + r + 8]) : 0u;
   }
 
-  long long it = 0;
-  for (long long k = 0; k < rounds; ++k) {
+  int it = 0;
+  for (int k = 0; k < rounds; ++k) {
     const bool slot_live = k < my_rounds;  // same for all warps of a slot
-    float acc[2][MT][4];
+    float acc[C::kAcc][MT][4];
 #pragma unroll
-    for (int h = 0; h < 2; ++h)
+    for (int h = 0; h < C::kAcc; ++h)
 #pragma unroll
       for (int i = 0; i < MT; ++i) acc[h][i][0] = acc[h][i][1] = acc[h][i][2] = acc[h][i][3] = 0.f;
     int row0 = 0, nrows = 0;
@@ -368,7 +372,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
       for (int j = 0; j < cpw; ++j, ++it) {
         cp_async_wait<kRing - 2>();
         __syncwarp();
-        const uint8_t* st = wring + (int)(it & (kRing - 1)) * C::kStageBytes;
+        const uint8_t* st = wring + (it & (kRing - 1)) * C::kStageBytes;
         uint32_t c0[V * 4], c1[V * 4];
 #pragma unroll
         for (int v = 0; v < V; ++v) {
@@ -382,10 +386,10 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
         const int c = kpart + j * wpt;
         const int col_base = c * kChunkBlocks * D + 4 * q;
         if (need_mask && c == p.chunks - 1) {
-          gemv_chunk<D, R, IDW, REPL, MT, XS, true>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, xrow, xsa, xv,
+          gemv_chunk<D, R, IDW, REPL, MT, XS, true>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, p.x, xoff, xsa, xv,
                                                     col_base, p.K);
         } else {
-          gemv_chunk<D, R, IDW, REPL, MT, XS, false>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, xrow, xsa, xv,
+          gemv_chunk<D, R, IDW, REPL, MT, XS, false>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, p.x, xoff, xsa, xv,
                                                      col_base, p.K);
         }
       }
@@ -401,7 +405,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
           const int row = r + (e >= 2 ? 8 : 0);
           const int m = i * 8 + 2 * q + (e & 1);
           if (row < nrows && m < p.M) {
-            float v = acc[0][i][e] + acc[1][i][e];
+            float v = C::kAcc == 2 ? acc[0][i][e] + acc[C::kAcc - 1][i][e] : acc[0][i][e];
             if (p.bias) v += __bfloat162float(__ushort_as_bfloat16(p.bias[row0 + row]));
             emit_out(p, tag, m, row0 + row, v);
           }
@@ -412,10 +416,13 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
     float* wred = red + ((int)(k & 1) * kWarps + warp) * 16 * MC;
 #pragma unroll
     for (int i = 0; i < MT; ++i) {
-      wred[r * MC + i * 8 + 2 * q] = acc[0][i][0] + acc[1][i][0];
-      wred[r * MC + i * 8 + 2 * q + 1] = acc[0][i][1] + acc[1][i][1];
-      wred[(r + 8) * MC + i * 8 + 2 * q] = acc[0][i][2] + acc[1][i][2];
-      wred[(r + 8) * MC + i * 8 + 2 * q + 1] = acc[0][i][3] + acc[1][i][3];
+      float v4[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v4[e] = C::kAcc == 2 ? acc[0][i][e] + acc[C::kAcc - 1][i][e] : acc[0][i][e];
+      wred[r * MC + i * 8 + 2 * q] = v4[0];
+      wred[r * MC + i * 8 + 2 * q + 1] = v4[1];
+      wred[(r + 8) * MC + i * 8 + 2 * q] = v4[2];
+      wred[(r + 8) * MC + i * 8 + 2 * q + 1] = v4[3];
     }
     named_barrier(1 + slot, wpt * 32);
     const float* sred = red + ((int)(k & 1) * kWarps + slot * wpt) * 16 * MC;
@@ -445,20 +452,19 @@ __global__ void __launch_bounds__(kThreads) rvq_dequant_kernel(const __grid_cons
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, q = lane & 3;
   const LaneSel ls(r, q);
-  int group;
-  long long tb, te;
-  cta_range(p, blockIdx.x, gridDim.x, &group, &tb, &te);
+  int group, tb, te;
+  cta_range(p, blockIdx.x, &group, &tb, &te);
   if (tb >= te) return;
   stage_codebooks<D, R, REPL>(smem, p.codebooks + (size_t)group * R * p.entries * D, p.entries);
   __syncthreads();
   const uint32_t cb_s = smem_u32(smem);
   const uint32_t cbl = cb_s + L::lane_offset(r, q);
   const long long tile_bytes = (long long)p.chunks * V * 256;
-  for (long long t = tb + warp; t < te; t += kWarps) {
+  for (int t = tb + warp; t < te; t += kWarps) {
     const int4 ti = p.tiles[t];
     const uint32_t rho_a = r < ti.z ? rho_pair(p.row_scale[ti.y + r]) : 0u;
     const uint32_t rho_b = r + 8 < ti.z ? rho_pair(p.row_scale[ti.y + r + 8]) : 0u;
-    const uint8_t* tbase = p.packed + t * tile_bytes;
+    const uint8_t* tbase = p.packed + (long long)t * tile_bytes;
     for (int c = 0; c < p.chunks; ++c) {
       uint32_t c0[V * 4], c1[V * 4];
 #pragma unroll
@@ -556,8 +562,29 @@ int group_starts(const wal_rvq_layer* L, GemvParams* p) {
   return WAL_OK;
 }
 
+// Deal the grid's CTAs to groups in proportion to their tile counts (at least
+// one each), and each group's tiles evenly over its CTAs.
+void assign_ctas(GemvParams& p, int ctas) {
+  const int G = p.num_groups;
+  const long long T = p.group_tile_start[G];
+  int assigned = 0;
+  for (int g = 0; g < G; ++g) {
+    long long cum = ((long long)ctas * p.group_tile_start[g + 1] + T / 2) / T;
+    if (cum < g + 1) cum = g + 1;
+    if (cum > ctas - (G - 1 - g)) cum = ctas - (G - 1 - g);
+    if (g == G - 1) cum = ctas;
+    const int n = (int)cum - assigned;
+    const int tg = p.group_tile_start[g + 1] - p.group_tile_start[g];
+    p.cta_start[g] = assigned;
+    p.tiles_q[g] = tg / n;
+    p.tiles_r[g] = tg % n;
+    assigned = (int)cum;
+  }
+  p.cta_start[G] = ctas;
+}
+
 template <typename Kern>
-int persistent_grid(Kern kern, int threads, int smem, int num_ctas, const GemvParams& p, int* grid_out) {
+int persistent_grid(Kern kern, int threads, int smem, int num_ctas, GemvParams& p, int* grid_out) {
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return WAL_ERR_CUDA;
   cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
@@ -571,6 +598,7 @@ int persistent_grid(Kern kern, int threads, int smem, int num_ctas, const GemvPa
   if (grid > p.num_tiles) grid = p.num_tiles;
   if (grid < p.num_groups) grid = p.num_groups;
   *grid_out = (int)grid;
+  assign_ctas(p, (int)grid);
   return WAL_OK;
 }
 
@@ -580,7 +608,7 @@ int persistent_grid(Kern kern, int threads, int smem, int num_ctas, const GemvPa
 using namespace wal;
 
 template <int D, int R, int IDW, bool REPL, int MT, bool XS>
-static int run_gemv(const GemvParams& p, int num_ctas, cudaStream_t stream) {
+static int run_gemv(GemvParams p, int num_ctas, cudaStream_t stream) {
   using C = GemvCfg<D, R, IDW, REPL, MT, XS>;
   auto kern = rvq_gemv_kernel<D, R, IDW, REPL, MT, XS>;
   const int kpad = p.chunks * kChunkBlocks * D;
@@ -590,6 +618,9 @@ static int run_gemv(const GemvParams& p, int num_ctas, cudaStream_t stream) {
   int grid = 0;
   const int st = persistent_grid(kern, C::kT, smem, num_ctas, p, &grid);
   if (st != WAL_OK) return st;
+  // the in-kernel id cursor is a 32-bit offset over one CTA's tiles
+  for (int g = 0; g < p.num_groups; ++g)
+    if ((long long)(p.tiles_q[g] + 1) * p.chunks * C::V * 256 >= (1LL << 31)) return WAL_ERR_UNSUPPORTED;
   // programmatic dependent launch: the weight prologue (codebooks, first id
   // chunks) of this kernel overlaps the tail of the previous kernel in the
   // stream; the kernel waits on the dependency before touching x or y.
@@ -608,7 +639,7 @@ static int run_gemv(const GemvParams& p, int num_ctas, cudaStream_t stream) {
 }
 
 template <int D, int R, int IDW, bool REPL>
-static int run_dequant(const GemvParams& p, uint16_t* w, long long ldw, cudaStream_t stream) {
+static int run_dequant(GemvParams p, uint16_t* w, long long ldw, cudaStream_t stream) {
   using C = GemvCfg<D, R, IDW, REPL, 1, false>;
   auto kern = rvq_dequant_kernel<D, R, IDW, REPL>;
   const int smem = C::cb_bytes(p.entries);
@@ -744,6 +775,7 @@ static int gemv_common(const wal_rvq_layer* layer, const uint16_t* x, int64_t M,
   }
   if (ldx < g.in_features || ldy < g.out_features) return WAL_ERR_SHAPE;
   if ((ldx % 4) || ((uintptr_t)x & 7)) return WAL_ERR_ALIGNMENT;
+  if (ldx >= (1LL << 26)) return WAL_ERR_UNSUPPORTED;  // activation row offsets are 32-bit
   if (y_dtype != WAL_BF16 && y_dtype != WAL_F32 && y_dtype != WAL_F16) return WAL_ERR_INVALID_ARGUMENT;
   if (warps_per_tile != 0 && warps_per_tile != 1 && warps_per_tile != 2 && warps_per_tile != 4 &&
       warps_per_tile != 8 && warps_per_tile != 16)
@@ -776,6 +808,7 @@ static int gemv_common(const wal_rvq_layer* layer, const uint16_t* x, int64_t M,
     }
   }
   p.wpt = wpt;
+  p.wpt_shift = wpt == 1 ? 0 : wpt == 2 ? 1 : wpt == 4 ? 2 : wpt == 8 ? 3 : 4;
   p.ldx = ldx;
   p.ldy = ldy;
   p.y_dtype = y_dtype;
@@ -837,6 +870,7 @@ extern "C" int wal_rvq_dequant(const wal_rvq_layer* layer, uint16_t* w, int64_t 
   st = make_params(layer, &p);
   if (st != WAL_OK) return st;
   p.wpt = 1;
+  p.wpt_shift = 0;
   return dequant_by_d(d, p, w, ldw, static_cast<cudaStream_t>(stream), R, idw, repl);
 }
 
