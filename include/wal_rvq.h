@@ -142,7 +142,7 @@ WAL_API int wal_rvq_gemv(const wal_rvq_layer* layer, const uint16_t* x, int64_t 
  * tensor cores.  Weight tiles are decoded exactly (same arithmetic as the
  * GEMV) into shared memory per 64-column stage; x tiles arrive by TMA.
  * Supports d = 8, R in {1, 2}, <= 256 entries; row groups must start at a
- * multiple of 256 rows.  x: bf16, ldx % 8 == 0, 16-byte aligned base.
+ * multiple of 128 rows.  x: bf16, ldx % 8 == 0, 16-byte aligned base.
  * y_dtype: WAL_BF16 or WAL_F32.  status: optional device int, set to 1 if a
  * pipeline wait timed out (the CTA then stops and frees its resources), NULL
  * to skip.  Returns WAL_ERR_UNSUPPORTED for other configurations (callers use

@@ -183,7 +183,8 @@ def gemm_f32(mod: PackedGroupedBlockRVQLinear, x: torch.Tensor) -> torch.Tensor:
 
 
 @pytest.mark.parametrize("M,N,K,R,bias", [(256, 512, 256, 2, False), (300, 1000, 520, 2, True), (128, 256, 1024, 1, False),
-                                          (517, 768, 2048, 2, True)])
+                                          (517, 768, 2048, 2, True), (1100, 640, 384, 2, False),
+                                          (2048, 384, 136, 1, True)])
 def test_prefill_gemm_matches_oracle(M, N, K, R, bias):
     enc = single_group(synthetic.rvq_encoding(N, K, d=8, R=R, seed=M + N))
     b = synthetic.bias_vector(N, seed=3) if bias else None
@@ -196,10 +197,11 @@ def test_prefill_gemm_matches_oracle(M, N, K, R, bias):
     assert_close(yb, ref, tol=8e-3)
 
 
-def test_prefill_gemm_grouped_rows():
-    enc = synthetic.grouped_encoding([256, 512, 256], 512, d=8, R=2, seed=8)
+@pytest.mark.parametrize("rows", [[256, 512, 256], [128, 384, 128]])
+def test_prefill_gemm_grouped_rows(rows):
+    enc = synthetic.grouped_encoding(rows, 512, d=8, R=2, seed=8)
     mod = PackedGroupedBlockRVQLinear(enc).cuda()
-    x = synthetic.activations(260, 512, seed=8)
+    x = synthetic.activations(600, 512, seed=8)
     ref = orc.forward_f32(bits_of(x), orc.groups_from_encoding(enc), 512)
     assert_close(gemm_f32(mod, x).cpu().numpy(), ref)
 

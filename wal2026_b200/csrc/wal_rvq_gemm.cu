@@ -1,21 +1,26 @@
 // Prefill path (M >= 256 tokens): fused Block-RVQ decode -> shared memory ->
 // tcgen05.mma (5th-generation tensor cores, fp32 accumulators in TMEM).
 //
-// One CTA computes a 128 (tokens) x 256 (output rows) tile of y over all of K
+// One CTA computes a 512 (tokens) x 128 (output rows) tile of y over all of K
 // in stages of 64 columns, with warp specialisation:
-//   warp 0      TMA producer: the activation tile [128 x 64] bf16 per stage,
-//               cp.async.bulk.tensor into a 128-byte-swizzled K-major buffer
-//               (no multicast), completion on full_a[stage];
+//   warp 0      TMA producer: the activation tile [512 x 64] bf16 per stage
+//               (two 256-row boxes), cp.async.bulk.tensor into a
+//               128-byte-swizzled K-major buffer (no multicast), completion
+//               on full_a[stage];
 //   warp 1      MMA issuer (one elected lane): waits full_a + full_b, issues
-//               4 x tcgen05.mma (M=128, N=256, K=16) into TMEM and commits to
-//               empty[stage] (the stage's buffers are free again) and, after
-//               the last stage, to acc_full;
-//   warps 2..9  decoders: for every stage decode the 256 x 64 weight tile
+//               16 x tcgen05.mma (M=128, N=128, K=16: four token tiles share
+//               each decoded weight tile) into four TMEM accumulators and
+//               commits to empty[stage] (the stage's buffers are free again)
+//               and, after the last stage, to acc_full;
+//   warps 2..9  decoders: for every stage decode the 128 x 64 weight tile
 //               exactly (same arithmetic as the decode GEMV: fp32 stage sum,
-//               two bf16 roundings) straight into the swizzled K-major B
-//               buffer, fence it for the async proxy and arrive on full_b;
-//               then the epilogue: TMEM -> registers (tcgen05.ld 32x32b),
-//               bias, bf16/fp32 store of y.
+//               two bf16 roundings; two threads per row, ids prefetched two
+//               stages ahead) straight into the swizzled K-major B buffer,
+//               fence it for the async proxy and arrive on full_b; then the
+//               epilogue: TMEM -> registers (tcgen05.ld 32x32b), bias,
+//               bf16/fp32 store of y.
+// Sharing each decoded tile over 512 tokens keeps the exact decode (CUDA
+// cores) below the tensor-core time of the same stage.
 // The dense weight never reaches global memory.  Every mbarrier wait is
 // bounded by a %globaltimer deadline; on expiry the CTA records an error code
 // (if a status word was supplied), stops issuing work, drains and frees TMEM.
@@ -30,18 +35,19 @@
 namespace wal {
 namespace gemm {
 
-constexpr int kBM = 256;   // tokens per CTA: two 128-row MMA tiles share each decoded weight tile
+constexpr int kBM = 512;   // tokens per CTA: four 128-row MMA tiles share each decoded weight tile
 constexpr int kUM = 128;   // MMA M
-constexpr int kBN = 256;
+constexpr int kBN = 128;   // output rows per CTA (MMA N)
 constexpr int kBK = 64;
 constexpr int kStages = 2;
+constexpr int kTmaRows = 256;  // TMA box height: two boxes per activation stage
 constexpr int kDecodeWarps = 8;
 constexpr int kThreads = (2 + kDecodeWarps) * 32;
-constexpr int kABytes = kBM * kBK * 2;  // 32 KB
-constexpr int kBBytes = kBN * kBK * 2;  // 32 KB
+constexpr int kABytes = kBM * kBK * 2;  // 64 KB
+constexpr int kBBytes = kBN * kBK * 2;  // 16 KB
 constexpr int kCbCopyBytes = 256 * 16;  // one stage table, one copy
 constexpr int kCbCopies = 8;            // 8-lane phases of 16-byte gathers hit 8 distinct bank quads
-constexpr int kTmemCols = 512;          // two 128 x 256 fp32 accumulators
+constexpr int kTmemCols = 512;          // four 128 x 128 fp32 accumulators
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s per wait, then give up
 
 struct GemmParams {
@@ -117,7 +123,7 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
   return d;
 }
 
-// Instruction descriptor: kind::f16, A = B = bf16, D = f32, both K-major, M = 128, N = 256.
+// Instruction descriptor: kind::f16, A = B = bf16, D = f32, both K-major, M = 128, N = kBN.
 constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) |
                             ((uint32_t)(kUM >> 4) << 24);
 
@@ -146,13 +152,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Decode the weights of one output row for one 64-column stage (eight d = 8
-// blocks) and store them, 16 bytes per block, into the swizzled B buffer.
+// Decode the weights of one output row for half of a 64-column stage (blocks
+// u0 .. u0+3 of the stage, d = 8) and store them, 16 bytes per block, into the
+// swizzled B buffer.  ids[st] holds the four 1-byte ids of those blocks.
 template <int R>
-__device__ __forceinline__ void decode_stage_row(uint32_t bsm_row, int nsw, const uint32_t (&ids)[R][2],
-                                                 uint32_t cb_lane, uint32_t rho2, int k_left) {
+__device__ __forceinline__ void decode_stage_half(uint32_t bsm_row, int nsw, const uint32_t (&ids)[R], int u0,
+                                                  uint32_t cb_lane, uint32_t rho2, int k_left) {
 #pragma unroll
-  for (int u = 0; u < 8; ++u) {
+  for (int j = 0; j < 4; ++j) {
+    const int u = u0 + j;
     uint4 o = make_uint4(0u, 0u, 0u, 0u);
     if (u * 8 < k_left) {
       float s[8];
@@ -161,7 +169,7 @@ __device__ __forceinline__ void decode_stage_row(uint32_t bsm_row, int nsw, cons
       uint32_t w[4];
 #pragma unroll
       for (int st = 0; st < R; ++st) {
-        const uint32_t id = (ids[st][u >> 2] >> (8 * (u & 3))) & 0xFFu;
+        const uint32_t id = (ids[st] >> (8 * j)) & 0xFFu;
         uint4 c;
         asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
                      : "=r"(c.x), "=r"(c.y), "=r"(c.z), "=r"(c.w)
@@ -272,7 +280,9 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_kernel(const __grid_cons
         }
         if (abort_flag) break;
         mbar_expect_tx(full_a + 8 * s, kABytes);
-        tma_load_2d(a_sm + s * kABytes, &xmap, kb * kBK, m0, full_a + 8 * s);
+#pragma unroll
+        for (int h = 0; h < kBM / kTmaRows; ++h)
+          tma_load_2d(a_sm + s * kABytes + h * (kTmaRows * 128), &xmap, kb * kBK, m0 + h * kTmaRows, full_a + 8 * s);
         ++issued;
       }
       // never leave a copy in flight: wait (bounded) for the last load of every stage
@@ -305,50 +315,48 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_kernel(const __grid_cons
     }
   } else {
     // ---------------- decoders, then epilogue -----------------------------
-    const int t = threadIdx.x - 64;  // 0..255: output row of the tile
-    const int n = n0 + t;
+    const int t = threadIdx.x - 64;  // 0..255: row t & 127 of the tile, column half t >> 7 of each stage
+    const int row = t & (kBN - 1), half = t >> 7;
+    const int n = n0 + row;
     const bool row_ok = n < g_row1;
     const uint32_t rho2 = row_ok ? rho_pair(p.row_scale[n]) : 0u;
     const int local = n - g_row0;
     const long long tile = (long long)g_tile0 + local / 16;
     const int rr = local % 16;
     const long long tile_bytes = (long long)p.chunks * R * 256;
-    const uint8_t* idrow = p.packed + tile * tile_bytes + rr * 16;
-    const uint32_t bsm_row0 = b_sm + (t >> 3) * 1024 + (t & 7) * 128;
+    const uint8_t* idrow = p.packed + tile * tile_bytes + rr * 16 + half * 4;
+    const uint32_t bsm_row0 = b_sm + (row >> 3) * 1024 + (row & 7) * 128;
     const uint32_t cb_lane = cb_sm + (uint32_t)(lane & 7) * 16;
-    const int nsw = t & 7;
-    uint32_t ids[R][2], nids[R][2];
-    auto load_ids = [&](int kb, uint32_t (&dst)[R][2]) {
-      // stage kb covers blocks 8kb..8kb+7 = bytes 8*(kb&1) of chunk kb/2
+    const int nsw = row & 7;
+    // stage kb covers blocks 8kb..8kb+7 = bytes 8*(kb&1) of chunk kb/2; this
+    // thread's four blocks are 4 more bytes in.  Ids run two stages ahead.
+    auto load_ids = [&](int kb, uint32_t (&dst)[R]) {
 #pragma unroll
-      for (int st = 0; st < R; ++st) {
-        if (row_ok && kb < kblocks) {
-          const uint2 v = *reinterpret_cast<const uint2*>(idrow + ((long long)(kb >> 1) * R + st) * 256 + 8 * (kb & 1));
-          dst[st][0] = v.x;
-          dst[st][1] = v.y;
-        } else {
-          dst[st][0] = dst[st][1] = 0u;
-        }
-      }
+      for (int st = 0; st < R; ++st)
+        dst[st] = (row_ok && kb < kblocks)
+                      ? *reinterpret_cast<const uint32_t*>(idrow + ((long long)(kb >> 1) * R + st) * 256 + 8 * (kb & 1))
+                      : 0u;
     };
-    load_ids(0, ids);
+    uint32_t ids0[R], ids1[R], ids2[R];
+    load_ids(0, ids0);
+    load_ids(1, ids1);
     for (int kb = 0; kb < kblocks; ++kb) {
       const int s = kb % kStages;
-      load_ids(kb + 1, nids);
+      load_ids(kb + 2, ids2);
       if (kb >= kStages && !mbar_wait(empty + 8 * s, ((kb / kStages) - 1) & 1)) {
         abort_flag = 1;
         break;
       }
       if (abort_flag) break;
       const int k_left = row_ok ? p.K - kb * kBK : 0;
-      decode_stage_row<R>(bsm_row0 + s * kBBytes, nsw, ids, cb_lane, rho2, k_left);
+      decode_stage_half<R>(bsm_row0 + s * kBBytes, nsw, ids0, half * 4, cb_lane, rho2, k_left);
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) mbar_arrive(full_b + 8 * s);
 #pragma unroll
       for (int st = 0; st < R; ++st) {
-        ids[st][0] = nids[st][0];
-        ids[st][1] = nids[st][1];
+        ids0[st] = ids1[st];
+        ids1[st] = ids2[st];
       }
     }
     // epilogue: TMEM lanes 32*(warp%4) .. +31 are this warp's tokens
@@ -357,9 +365,11 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_kernel(const __grid_cons
     tc_fence_after();
     if (ok) {
       const int quarter = warp & 3;
-      const int mt = (warp - 2) >> 2;  // two warps share a lane quarter: one per accumulator
-      const int m = m0 + mt * kUM + quarter * 32 + lane;
       const bool vec_ok = (p.ldy % 8) == 0 && ((uintptr_t)p.y & 15) == 0;
+      // two warps share a lane quarter; each takes two of the four accumulators
+      for (int mi = 0; mi < 2; ++mi) {
+      const int mt = 2 * ((warp - 2) >> 2) + mi;
+      const int m = m0 + mt * kUM + quarter * 32 + lane;
       for (int c0 = 0; c0 < kBN; c0 += 16) {
         uint32_t v[16];
         tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(mt * kBN + c0), v);
@@ -394,6 +404,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_kernel(const __grid_cons
               if (col0 + j < g_row1) yr[j] = __float2bfloat16_rn(f[j]);
           }
         }
+      }
       }
     }
   }
@@ -459,7 +470,7 @@ extern "C" int wal_rvq_gemm(const wal_rvq_layer* layer, const uint16_t* x, int64
   p.entries = g.num_entries;
   p.y_dtype = y_dtype;
   p.num_groups = g.num_groups;
-  // group boundaries; an N tile (256 rows) must not straddle two groups
+  // group boundaries; an N tile (kBN rows) must not straddle two groups
   long long t = 0, rows = 0;
   p.group_tile_start[0] = 0;
   p.group_row_start[0] = 0;
@@ -479,7 +490,7 @@ extern "C" int wal_rvq_gemm(const wal_rvq_layer* layer, const uint16_t* x, int64
   CUtensorMap map;
   const cuuint64_t dims[2] = {(cuuint64_t)g.in_features, (cuuint64_t)M};
   const cuuint64_t strides[1] = {(cuuint64_t)ldx * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kBM};  // 64 x 256: one load fills both MMA tiles
+  const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kTmaRows};  // 64 x 256: two loads per stage
   const cuuint32_t estr[2] = {1, 1};
   if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(x), dims, strides, box, estr,
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
