@@ -26,7 +26,10 @@ Also reported in the same JSON line (BASELINE's second metric and config 3):
               next to the same stack with dense bf16 cuBLAS projections;
   prefill_8b  (N = 1) the stack's 128 projection GEMMs at M = 2048 tokens on
               the tcgen05 decode-to-shared-memory GEMM, TFLOP/s against the
-              measured bf16 peak, next to cuBLAS on the same shapes.
+              measured bf16 peak, next to cuBLAS on the same shapes;
+  idroute_gemv (N = 1) the ID-route linear (reference PackedIDRouteLinear:
+              an int16 id per weight into fp16 route sums) on the 8B MLP
+              shape, GB/s against the measured HBM bandwidth.
 """
 from __future__ import annotations
 
@@ -321,6 +324,47 @@ def run_prefill(args, dev: torch.device, peaks: dict) -> dict:
             "gpu_launches": launches, "dense_bf16_cublas": dense}
 
 
+def run_idroute(args, dev: torch.device, peaks: dict) -> dict:
+    """ID-route GEMV (reference PackedIDRouteLinear, 2 bytes of ids per weight) on the 8B MLP shape, M = 1."""
+    from wal2026_b200.idroute import PackedIDRouteLinear
+
+    N, K, routes, M = N_OUT, K_IN, 1536, args.M
+    gen = torch.Generator(device=dev).manual_seed(5)
+    mods = [PackedIDRouteLinear.random(N, K, routes=routes, generator=gen, device=dev) for _ in range(4)]
+    x = torch.randn(M, K, device=dev).to(torch.bfloat16)
+    y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    for m in mods:
+        m.gemv_into(x, y)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for m in mods:
+            m.gemv_into(x, y)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(5, args.steps)
+    e0.record(stream)
+    for _ in range(reps):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * len(mods))
+    nbytes = N * K * 2 + routes * 2 + N * 2 + 2 * M * K + 2 * M * N
+    gbs = nbytes / (us * 1e-6) / 1e9
+    peak = float(peaks.get("hbm_gbs") or 6650.0)
+    del g, mods
+    torch.cuda.empty_cache()
+    return {"workload": f"ID-route linear {K}->{N}, int16 id per weight into {routes} fp16 route sums, M={M}, "
+                        f"4 instances ({4 * N * K * 2 / 1e6:.0f} MB, larger than L2) per graph",
+            "us_per_gemv": round(us, 3), "gbs": round(gbs, 1),
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "peak_source": "measured hbm_gbs" if peaks.get("hbm_gbs")
+                         else "fallback", "kernel": "idroute_gemv_kernel", "algorithmic_bytes_per_launch": nbytes}}
+
+
 def run_ours(args) -> None:
     import torch.distributed as dist
 
@@ -430,6 +474,7 @@ def run_ours(args) -> None:
     decode = run_decode(args, rank, world, dev) if args.decode else None
     peaks = measured_peaks()
     prefill = run_prefill(args, dev, peaks) if (args.prefill and world == 1) else None
+    idroute = run_idroute(args, dev, peaks) if (args.idroute and world == 1) else None
     peak = peaks.get("hbm_gbs")
     peak_src = "measured" if peak else "fallback"
     peak = float(peak or 6650.0)
@@ -461,6 +506,7 @@ def run_ours(args) -> None:
             "dense_bf16_cublas": dense,
             "decode_8b": decode,
             "prefill_8b": prefill,
+            "idroute_gemv": idroute,
         }
         print(json.dumps(out), flush=True)
     if world > 1:
@@ -489,6 +535,7 @@ def main() -> None:
     ap.add_argument("--prefill", type=int, default=1, help="also time the 8B-shaped prefill GEMMs (N = 1)")
     ap.add_argument("--prefill-tokens", type=int, default=2048)
     ap.add_argument("--prefill-steps", type=int, default=5)
+    ap.add_argument("--idroute", type=int, default=1, help="also time the ID-route GEMV (N = 1)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":

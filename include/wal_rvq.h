@@ -175,6 +175,54 @@ WAL_API int wal_rvq_dequant(const wal_rvq_layer* layer, uint16_t* w, int64_t ldw
 WAL_API int wal_rvq_unpack_ids(const wal_rvq_layer* layer, void* ids, void* stream);
 
 /* ------------------------------------------------------------------------
+ * ID-route linear (reference src/runtime.py:52-97, PackedIDRouteLinear; fused
+ * Triton kernel src/triton_id_matmul.py:19-67): one int16 id per weight into
+ * a scalar fp16 route table codebook_sum[num_routes].  The weight is, bit for
+ * bit, the reference's bf16 weight
+ *   w[n, k] = bf16_rn( fp16_rn( codebook_sum[ids[n, k]] * row_scale[n] ) ).
+ * Packed ids: tiles of 16 rows, chunks of 128 columns of 4 KB each (eight
+ * 512-byte warp-wide vectors; order in wal_idroute_pack), padding ids 0.
+ * ------------------------------------------------------------------------ */
+typedef struct wal_idroute_layer {
+  int64_t out_features;          /* N                                             */
+  int64_t in_features;           /* K, a multiple of 8                            */
+  int32_t num_routes;            /* table entries, <= 32767                       */
+  const void* packed_ids;        /* device, from wal_idroute_pack                 */
+  const uint16_t* codebook_sum;  /* device fp16 [num_routes]                      */
+  const uint16_t* row_scale;     /* device fp16 [N]                               */
+  const uint16_t* bias;          /* device bf16 [N] or NULL                       */
+} wal_idroute_layer;
+
+/* Bytes of the packed id stream for an N x K weight. */
+WAL_API int wal_idroute_packed_size(int64_t out_features, int64_t in_features, size_t* packed_bytes);
+
+/*
+ * Host re-layout of int16 ids [N][K] (row-major) into the packed stream:
+ * chunk (tile t, columns 128c..128c+127) at byte (t * chunks + c) * 4096;
+ * inside it, row 8h + r (h = 0, 1), columns 32g + 16u + 4q + j (g < 4, u < 2,
+ * q < 4, j < 4) at byte (h * 4 + g) * 512 + (r * 4 + q) * 16 + u * 8 + j * 2.
+ * Every id is checked against num_routes (WAL_ERR_ID_RANGE).  Replaces the
+ * int16 `ids` buffer of reference src/runtime.py:59-62.
+ */
+WAL_API int wal_idroute_pack(int64_t out_features, int64_t in_features, int32_t num_routes,
+                     const int16_t* ids, void* packed, size_t packed_bytes);
+
+/*
+ * y[M, N] = x[M, K] @ w^T (+ bias), x bf16 (ldx % 4 == 0, 8-byte aligned),
+ * y bf16 or fp32, fp32 accumulation, up to 16 tokens per launch (slabs
+ * beyond).  Replaces reference src/runtime.py:95-97 (forward) and
+ * src/triton_id_matmul.py:70-150 (id_route_linear_matmul).
+ */
+WAL_API int wal_idroute_gemv(const wal_idroute_layer* layer, const uint16_t* x, int64_t M, int64_t ldx,
+                     void* y, int64_t ldy, int y_dtype, void* stream);
+
+/* The weight [N, K] (row stride ldw): w_dtype WAL_F16 gives reference
+ * src/runtime.py:89-93 (reconstruct_weight) bit for bit, WAL_BF16 the same
+ * followed by .to(torch.bfloat16) (the forward's weight). */
+WAL_API int wal_idroute_dequant(const wal_idroute_layer* layer, uint16_t* w, int64_t ldw, int w_dtype,
+                        void* stream);
+
+/* ------------------------------------------------------------------------
  * Tensor-parallel decode.  No reference counterpart: the reference runs one
  * device.  A row-parallel linear (o_proj, down_proj split along K) produces
  * an fp32 partial output on every rank.  wal_rvq_gemv_push stores each

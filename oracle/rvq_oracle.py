@@ -122,3 +122,25 @@ def groups_from_encoding(enc) -> list[dict]:
             }
         )
     return out
+
+
+# ---------------------------------------------------------------------------
+# ID-route linear (reference src/runtime.py:52-97, PackedIDRouteLinear)
+# ---------------------------------------------------------------------------
+def idroute_weight_f16_bits(ids: np.ndarray, codebook_sum_bits: np.ndarray, row_scale_bits: np.ndarray) -> np.ndarray:
+    """fp16 weight bits of ``reconstruct_weight`` (src/runtime.py:89-93): gather, times row scale, fp16 rounding.
+
+    The product of two fp16 values is exact in float32, so one float32 multiply
+    followed by the round-to-nearest-even cast to float16 is the fp16 multiply.
+    """
+    cs = np.asarray(codebook_sum_bits, dtype=np.uint16).view(np.float16).astype(np.float32)
+    rho = np.asarray(row_scale_bits, dtype=np.uint16).view(np.float16).astype(np.float32).reshape(-1, 1)
+    w = (cs[np.asarray(ids).astype(np.int64)] * rho).astype(np.float16)
+    return w.view(np.uint16)
+
+
+def idroute_weight_bits(ids: np.ndarray, codebook_sum_bits: np.ndarray, row_scale_bits: np.ndarray) -> np.ndarray:
+    """bf16 weight bits of the forward (src/runtime.py:95-97: ``w.to(x.dtype)``)."""
+    w16 = idroute_weight_f16_bits(ids, codebook_sum_bits, row_scale_bits).view(np.float16)
+    return f32_to_bf16_bits(w16.astype(np.float32))
+

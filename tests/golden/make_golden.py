@@ -17,6 +17,9 @@ wraps it in the reference's ``PackedGroupedBlockRVQLinear`` with
 * SHA-256 digests of every input array, so the tests can prove that the
   synthetic generator still produces the same bytes.
 
+ID-route cases (``idroute_*``) run the reference's ``PackedIDRouteLinear``
+and record its route table, fp16 ``reconstruct_weight()`` and forward output.
+
 Small cases store all arrays; the two full-size configurations store input
 digests, the weight digest and a bounded slice of the outputs.
 """
@@ -98,6 +101,32 @@ def run_case(name, enc, Ms, x_seed, bias, ref_runtime, ref_block_vq, *, full: bo
     print(f"wrote {name}.npz  w_sha256={out['w_sha256']}")
 
 
+def run_idroute_case(name, inp, Ms, x_seed, bias, ref_runtime):
+    """Reference PackedIDRouteLinear (src/runtime.py:52-97) on seeded inputs."""
+    mod = ref_runtime.PackedIDRouteLinear(inp.ids, inp.codebook_w, inp.row_scale, bias)
+    with torch.no_grad():
+        w16 = mod.reconstruct_weight()
+    wb = w16.to(torch.bfloat16)
+    out = {"name": np.array(name), "N": np.array(inp.ids.shape[0]), "K": np.array(inp.ids.shape[1]),
+           "ids": inp.ids.to(torch.int16).numpy(), "codebook_w_bits": bits(inp.codebook_w),
+           "codebook_sum_bits": bits(mod.codebook_sum), "rho_bits": bits(inp.row_scale.reshape(-1)),
+           "w16_bits": bits(w16), "w16_sha256": np.array(sha(w16))}
+    if bias is not None:
+        out["bias_f16_bits"] = bits(bias)
+    for M in Ms:
+        x = synthetic.activations(M, inp.ids.shape[1], seed=x_seed)
+        with torch.no_grad():
+            y = mod(x)
+        y32 = x.double() @ wb.double().T
+        if bias is not None:
+            y32 = y32 + bias.to(torch.bfloat16).double()[None, :]
+        out[f"x{M}_bits"] = bits(x)
+        out[f"y{M}_ref32"] = y32.float().numpy()
+        out[f"y{M}_ref_bf16"] = bits(y)
+    np.savez_compressed(HERE / f"{name}.npz", **out)
+    print(f"wrote {name}.npz  w16_sha256={out['w16_sha256']}")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
@@ -120,6 +149,11 @@ def main() -> None:
     for name, enc, Ms, seed, with_bias in small:
         bias = synthetic.bias_vector(enc.original_shape[0], seed=seed) if with_bias else None
         run_case(name, enc, Ms, seed, bias, ref_runtime, ref_block_vq, full=True)
+    # ID-route linear (reference PackedIDRouteLinear): fp16 bias as the reference stores it
+    run_idroute_case("idroute_small", synthetic.idroute_inputs(40, 136, routes=300, seed=21), [1, 5], 21,
+                     synthetic.bias_vector(40, seed=21).to(torch.float16), ref_runtime)
+    run_idroute_case("idroute_medium", synthetic.idroute_inputs(256, 1024, routes=1536, seed=22), [3, 16], 22,
+                     None, ref_runtime)
     if args.skip_full:
         return
     run_case("cfg0", synthetic.cfg0_encoding(0), [1, 4, 16], 0, None, ref_runtime, ref_block_vq, full=False)

@@ -74,6 +74,19 @@ class TPPush(ctypes.Structure):
     ]
 
 
+class IDRouteLayer(ctypes.Structure):
+    """``wal_idroute_layer``: device buffers of one ID-route linear."""
+    _fields_ = [
+        ("out_features", ctypes.c_int64),
+        ("in_features", ctypes.c_int64),
+        ("num_routes", ctypes.c_int32),
+        ("packed_ids", ctypes.c_void_p),
+        ("codebook_sum", ctypes.c_void_p),
+        ("row_scale", ctypes.c_void_p),
+        ("bias", ctypes.c_void_p),
+    ]
+
+
 _GP = ctypes.POINTER(Geometry)
 _LP = ctypes.POINTER(Layer)
 
@@ -90,6 +103,10 @@ SIGNATURES: dict[str, tuple] = {
     "wal_rvq_gemm": (_c_int, [_LP, _vp, _c_i64, _c_i64, _vp, _c_i64, _c_int, _vp, _vp]),
     "wal_rvq_dequant": (_c_int, [_LP, _vp, _c_i64, _vp]),
     "wal_rvq_unpack_ids": (_c_int, [_LP, _vp, _vp]),
+    "wal_idroute_packed_size": (_c_int, [_c_i64, _c_i64, ctypes.POINTER(ctypes.c_size_t)]),
+    "wal_idroute_pack": (_c_int, [_c_i64, _c_i64, ctypes.c_int32, _vp, _vp, ctypes.c_size_t]),
+    "wal_idroute_gemv": (_c_int, [ctypes.POINTER(IDRouteLayer), _vp, _c_i64, _c_i64, _vp, _c_i64, _c_int, _vp]),
+    "wal_idroute_dequant": (_c_int, [ctypes.POINTER(IDRouteLayer), _vp, _c_i64, _c_int, _vp]),
     "wal_rvq_gemv_push": (_c_int, [_LP, _vp, _c_i64, _c_i64, ctypes.POINTER(TPPush), _vp]),
     "wal_tp_reduce_rmsnorm": (_c_int, [_vp, ctypes.c_int32, _c_i64, _c_i64, _vp, _vp, _vp, _c_i64, _vp,
                                        ctypes.c_float, _vp, _c_i64, _c_i64, _c_i64, _vp, _vp]),

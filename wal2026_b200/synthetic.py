@@ -125,3 +125,22 @@ def grouped_encoding(row_counts: list[int], K: int, *, d: int = 8, R: int = 2, C
         slices.append((row0, row0 + n))
         row0 += n
     return GroupedBlockRVQEncoding(groups=tuple(groups), row_slices=tuple(slices), original_shape=(row0, K))
+
+
+@dataclass
+class IDRouteInputs:
+    """Constructor arguments of an ID-route linear (reference ``PackedIDRouteLinear``)."""
+
+    ids: torch.Tensor         # int32 [N, K]
+    codebook_w: torch.Tensor  # fp16 [routes, L]
+    row_scale: torch.Tensor   # fp16 [N, 1]
+
+
+def idroute_inputs(N: int, K: int, *, routes: int = 1536, L: int = 12, seed: int = 21) -> IDRouteInputs:
+    """Seeded ID-route weight: uniform ids, fp16 route digits ~ N(0, 0.01), row scales ~ U(0.5, 1.5)."""
+    g = _gen(seed)
+    ids = torch.randint(0, routes, (N, K), generator=g, dtype=torch.int64).to(torch.int32)
+    codebook_w = (torch.randn(routes, L, generator=g) * 0.01).to(torch.float16)
+    rho = (torch.rand(N, 1, generator=g) + 0.5).to(torch.float16)
+    return IDRouteInputs(ids, codebook_w, rho)
+
