@@ -78,6 +78,9 @@ typedef struct wal_rvq_layer {
   const uint16_t* row_scale;  /* fp16 [N]                                            */
   const uint16_t* bias;       /* bf16 [N] or NULL                                    */
   const int64_t* group_rows;  /* HOST [num_groups] rows per group; NULL if 1 group   */
+  const float* stage_scales;  /* fp32 [num_groups][R] per-stage scales or NULL: each */
+                              /* stage value is RN(fp32(c) * scale) before the sum   */
+                              /* (reference src/block_vq.py:264-268)                 */
 } wal_rvq_layer;
 
 /* Human-readable text for a status code (static storage). */

@@ -43,6 +43,8 @@ def max_threads() -> int:
 
 
 def _group_args(g: dict):
+    if g.get("stage_scales") is not None:
+        raise ValueError("the C restatement covers unscaled stages only; use rvq_oracle for stage scales")
     ids = [np.ascontiguousarray(a) for a in g["stage_ids"]]
     idw = 1 if ids[0].dtype == np.uint8 else 2
     ids = [a if idw == 1 else a.view(np.uint16) for a in ids]

@@ -49,14 +49,22 @@ def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
     return (b.astype(np.uint32) << np.uint32(16)).view(np.float32)
 
 
-def stage_sum_f32(stage_ids: list[np.ndarray], codebooks: list[np.ndarray]) -> np.ndarray:
-    """fp32 sum of the gathered stage entries, ``[rows, blocks, d]`` (``src/runtime.py:381-388``)."""
+def stage_sum_f32(stage_ids: list[np.ndarray], codebooks: list[np.ndarray],
+                  stage_scales: np.ndarray | None = None) -> np.ndarray:
+    """fp32 sum of the gathered stage entries, ``[rows, blocks, d]`` (``src/runtime.py:381-388``).
+
+    With per-stage scales each stage is multiplied in fp32 before it is added
+    (``src/block_vq.py:264-268``).
+    """
     rows, blocks = stage_ids[0].shape
     d = codebooks[0].shape[1]
     acc = np.zeros((rows, blocks, d), dtype=np.float32)
-    for ids, book in zip(stage_ids, codebooks):
+    for s, (ids, book) in enumerate(zip(stage_ids, codebooks)):
         entries = np.asarray(book, dtype=np.float16).astype(np.float32)
-        acc += entries[np.asarray(ids).astype(np.int64)]
+        stage = entries[np.asarray(ids).astype(np.int64)]
+        if stage_scales is not None:
+            stage = stage * np.asarray(stage_scales, dtype=np.float32).reshape(-1)[s]
+        acc += stage
     return acc
 
 
@@ -65,9 +73,10 @@ def reconstruct_group_bits(
     codebooks: list[np.ndarray],
     row_scale: np.ndarray,
     in_features: int,
+    stage_scales: np.ndarray | None = None,
 ) -> np.ndarray:
     """bf16 weight bits ``[rows, in_features]`` of one plain group (``src/runtime.py:379-414``)."""
-    acc = stage_sum_f32(stage_ids, codebooks)
+    acc = stage_sum_f32(stage_ids, codebooks, stage_scales)
     rows = acc.shape[0]
     w = acc.reshape(rows, -1)[:, :in_features]
     w_bf = bf16_bits_to_f32(f32_to_bf16_bits(w))
@@ -82,7 +91,8 @@ def reconstruct_bits(groups: list[dict], in_features: int) -> np.ndarray:
     Each group is a dict with ``stage_ids`` (list of ``[rows, blocks]`` int arrays),
     ``codebooks`` (list of ``[entries, d]`` fp16 arrays) and ``row_scale``.
     """
-    parts = [reconstruct_group_bits(g["stage_ids"], g["codebooks"], g["row_scale"], in_features) for g in groups]
+    parts = [reconstruct_group_bits(g["stage_ids"], g["codebooks"], g["row_scale"], in_features,
+                                    g.get("stage_scales")) for g in groups]
     return np.concatenate(parts, axis=0)
 
 
@@ -119,6 +129,8 @@ def groups_from_encoding(enc) -> list[dict]:
                 "stage_ids": [t.cpu().numpy() for t in g.stage_ids],
                 "codebooks": [t.cpu().numpy().astype(np.float16) for t in g.codebooks],
                 "row_scale": g.row_scale.cpu().numpy(),
+                "stage_scales": None if getattr(g, "stage_scales", None) is None
+                else g.stage_scales.cpu().float().numpy(),
             }
         )
     return out

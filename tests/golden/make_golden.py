@@ -82,6 +82,8 @@ def run_case(name, enc, Ms, x_seed, bias, ref_runtime, ref_block_vq, *, full: bo
         out[f"g{gi}_rho_sha256"] = np.array(sha(g.row_scale))
         if full:
             out[f"g{gi}_rho"] = g.row_scale.numpy()
+            if g.stage_scales is not None:
+                out[f"g{gi}_scales"] = g.stage_scales.numpy()
     if bias is not None:
         out["bias_bits"] = bits(bias)
     for M in Ms:
@@ -149,6 +151,29 @@ def main() -> None:
     for name, enc, Ms, seed, with_bias in small:
         bias = synthetic.bias_vector(enc.original_shape[0], seed=seed) if with_bias else None
         run_case(name, enc, Ms, seed, bias, ref_runtime, ref_block_vq, full=True)
+    # per-stage scales (fp16, as the reference's encoder stores them, src/block_vq.py:522)
+    def scaled(enc, scales_per_group):
+        groups = tuple(dataclasses.replace(g, stage_scales=torch.tensor(sc, dtype=torch.float16))
+                       for g, sc in zip(enc.groups, scales_per_group))
+        return dataclasses.replace(enc, groups=groups)
+
+    run_case("small_scaled_r2", scaled(single_group(synthetic.rvq_encoding(48, 136, d=8, R=2, seed=18)),
+                                       [[0.8125, 1.3125]]), [1, 7], 18, None, ref_runtime, ref_block_vq, full=True)
+    run_case("small_scaled_r1", scaled(single_group(synthetic.rvq_encoding(32, 64, d=8, R=1, seed=19)),
+                                       [[1.2001953125]]), [2], 19, None, ref_runtime, ref_block_vq, full=True)
+    run_case("small_scaled_grouped",
+             scaled(synthetic.grouped_encoding([32, 16], 96, d=16, R=3, seed=20),
+                    [[1.0, 0.5, 0.333251953125], [0.9, 1.1, 0.7]]), [3], 20, None, ref_runtime, ref_block_vq,
+             full=True)
+    # an encoding map written by the reference's own saver (src/encoding_io.py:77-85)
+    from src import encoding_io as ref_io  # type: ignore
+
+    enc_a = to_reference(scaled(single_group(synthetic.rvq_encoding(48, 136, d=8, R=2, seed=18)),
+                                [[0.8125, 1.3125]]), ref_block_vq)
+    enc_b = to_reference(synthetic.grouped_encoding([16, 24, 9], 128, d=8, R=2, seed=14), ref_block_vq)
+    ref_io.save_grouped_encoding_map(HERE / "encoding_map_small.pt",
+                                     {"model.layers.0.mlp.up_proj": enc_a, "model.layers.0.self_attn.q_proj": enc_b})
+    print("wrote encoding_map_small.pt")
     # ID-route linear (reference PackedIDRouteLinear): fp16 bias as the reference stores it
     run_idroute_case("idroute_small", synthetic.idroute_inputs(40, 136, routes=300, seed=21), [1, 5], 21,
                      synthetic.bias_vector(40, seed=21).to(torch.float16), ref_runtime)

@@ -1,6 +1,7 @@
 """Helpers to load the reference-generated golden fixtures under ``tests/golden/``."""
 from __future__ import annotations
 
+import dataclasses
 import hashlib
 from pathlib import Path
 
@@ -9,7 +10,7 @@ import torch
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
 SMALL_CASES = ["small_r2_d8", "small_r1_ragged", "small_r3_d16", "small_grouped", "small_route",
-               "small_d32", "small_r4_wide"]
+               "small_d32", "small_r4_wide", "small_scaled_r2", "small_scaled_r1", "small_scaled_grouped"]
 
 
 def load(name: str) -> dict:
@@ -36,7 +37,8 @@ def groups_from_fixture(fx: dict) -> list[dict]:
             ids.append(fx[f"g{gi}_ids{s}"])
             books.append(fx[f"g{gi}_book{s}"])
             s += 1
-        groups.append({"stage_ids": ids, "codebooks": books, "row_scale": fx[f"g{gi}_rho"]})
+        groups.append({"stage_ids": ids, "codebooks": books, "row_scale": fx[f"g{gi}_rho"],
+                       "stage_scales": fx.get(f"g{gi}_scales")})
         gi += 1
     return groups
 
@@ -57,6 +59,8 @@ def encoding_from_fixture(fx: dict):
         books = [torch.from_numpy(np.ascontiguousarray(b)) for b in g["codebooks"]]
         rho = torch.from_numpy(np.ascontiguousarray(g["row_scale"]))
         enc = make_plain_encoding(ids, books, rho, in_features=K, block_size=d)
+        if g["stage_scales"] is not None:
+            enc = dataclasses.replace(enc, stage_scales=torch.from_numpy(np.ascontiguousarray(g["stage_scales"])))
         n = int(ids[0].shape[0])
         groups.append(enc)
         slices.append((row0, row0 + n))

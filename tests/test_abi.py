@@ -164,8 +164,11 @@ def test_unsupported_encodings_raise_value_error():
     import dataclasses
 
     bad = dataclasses.replace(enc, transform_kind="dct")
-    with pytest.raises(ValueError, match="plain"):
+    with pytest.raises(ValueError, match="per-block corrections"):
         PackedGroupedBlockRVQLinear(single_group(bad))
+    scaled = dataclasses.replace(enc, stage_scales=torch.tensor([1.5, 0.5], dtype=torch.float16))
+    mod = PackedGroupedBlockRVQLinear(single_group(scaled))  # per-stage scales are supported
+    assert torch.equal(mod.stage_scales, torch.tensor([[1.5, 0.5]]))
     odd = synthetic.rvq_encoding(16, 30, d=8, seed=1)
     with pytest.raises(ValueError, match="multiple of 4"):
         PackedGroupedBlockRVQLinear(single_group(odd))

@@ -93,8 +93,9 @@ def test_oracle_full_cfg1_pinned():
     assert np.array_equal(route, inp.route.numpy()) and np.array_equal(code, inp.code.numpy())
 
 
-@pytest.mark.parametrize("name", goldens.SMALL_CASES)
+@pytest.mark.parametrize("name", [c for c in goldens.SMALL_CASES if "scaled" not in c])
 def test_c_oracle_matches_reference(name):
+    """The C restatement (CPU baseline) covers unscaled stages; scaled ones are the numpy oracle's."""
     from oracle import c_oracle
 
     fx = goldens.load(name)

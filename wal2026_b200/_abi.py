@@ -60,6 +60,7 @@ class Layer(ctypes.Structure):
         ("row_scale", ctypes.c_void_p),
         ("bias", ctypes.c_void_p),
         ("group_rows", ctypes.POINTER(ctypes.c_int64)),
+        ("stage_scales", ctypes.c_void_p),
     ]
 
 

@@ -59,16 +59,16 @@ class BlockRVQEncoding:
         return tuple(int(v) for v in self.stage_ids[0].shape)
 
     def is_plain(self) -> bool:
-        """True when the encoding uses none of the optional corrections.
+        """True when the encoding uses none of the per-block corrections.
 
-        The fused CUDA path implements the plain sum-of-stages decode; block
-        scales, sign residuals, transforms and stage scales are rejected by the
-        packer with ``ValueError`` (the reference's fused path rejects the same
-        set, ``src/runtime.py:828-853``).
+        The fused CUDA path implements the sum-of-stages decode, with optional
+        per-stage scales (each stage value ``fp32(c) * scale`` before the sum,
+        reference ``src/block_vq.py:264-268``); block scales, sign residuals and
+        transforms are rejected by the packer with ``ValueError`` (the
+        reference's fused path rejects corrections too, ``src/runtime.py:828-853``).
         """
         return (
-            self.stage_scales is None
-            and self.block_scale is None
+            self.block_scale is None
             and self.transform_kind == "none"
             and self.transform_matrix is None
             and self.transform_bias is None

@@ -94,6 +94,15 @@ __device__ __forceinline__ uint2 lds_v2(uint32_t saddr) {
   return v;
 }
 
+// (a0, a1) += (b0, b1), two fp32 round-to-nearest adds in one packed instruction
+__device__ __forceinline__ void add_f32x2(float& a0, float& a1, float b0, float b1) {
+  unsigned long long a, b;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "f"(b0), "f"(b1));
+  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(a) : "l"(b));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(a));
+}
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
 }
@@ -116,7 +125,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 // The plain layout stores each entry once (entry stride 2*d bytes) and is used
 // when replication does not fit (large routed codebooks).
 // ---------------------------------------------------------------------------
-template <int D, bool REPL>
+// Scaled multi-stage tables (per-stage fp32 scales) use an fp32 replicated
+// layout: a lane's four columns are 16 bytes of fp32; the 8 lanes of a
+// quarter-warp phase of a 128-bit load are 8 lane classes (r & 1) * 4 + q, each
+// with its own 16-byte copy of the columns it reads (d = 8: half q & 1 of the
+// entry; d = 16: quarter q; d = 32: quarter q of 16-column half kt & 1, halves
+// 128 bytes apart).  Entry rows keep 128 bytes per stage (per half for
+// d = 32) and the same id * 256 addressing, lane offset ((r & 1) * 4 + q) * 16.
+template <int D, bool REPL, bool F32 = false>
 struct CbLayout {
   static constexpr int kPieces = D / 4;
   static constexpr int kCopies = REPL ? (D == 8 ? 8 : 4) : 1;
@@ -147,6 +163,7 @@ struct CbLayout {
     return stage_offset(s) + e * 256 + inner;
   }
   __device__ static int lane_offset(int r, int q) {
+    if (F32) return ((r & 1) * 4 + q) * 16;
     if (REPL) return (r & 3) * 32 + q * 8;
     return D == 8 ? (q & 1) * 8 : q * 8;
   }
@@ -178,6 +195,17 @@ __device__ __forceinline__ void cp_async_8(uint32_t saddr, const void* gptr) {
 
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::); }
 
+// One-stage tables with a stage scale: the staged bf16 value is
+// bf16_rn(+0.0f + RN(fp32(c) * scale)).  Applied in place after the plain
+// staging copied the raw fp16 entries (called instead of the unscaled
+// pre-rounding).
+__device__ __forceinline__ uint32_t preround_pair_scaled(uint32_t h2, float sc) {
+  const __half2 h = *reinterpret_cast<const __half2*>(&h2);
+  const float lo = __fadd_rn(0.0f, __fmul_rn(__half2float(__low2half(h)), sc));
+  const float hi = __fadd_rn(0.0f, __fmul_rn(__half2float(__high2half(h)), sc));
+  return pack_bf16x2_rn(lo, hi);
+}
+
 // Stage R codebooks of one group (fp16 [R][entries][D] in global memory) into
 // shared memory, in two steps so the copies overlap other prologue work:
 //   stage_codebooks_issue  - every 16-byte run of an entry is fetched with
@@ -205,18 +233,32 @@ __device__ void stage_codebooks_issue(uint8_t* cb, const uint16_t* __restrict__ 
 }
 
 template <int D, int R, bool REPL>
-__device__ void stage_codebooks_finish(uint8_t* cb, int entries) {
+__device__ void stage_codebooks_finish(uint8_t* cb, int entries, const float* scale = nullptr) {
   using L = CbLayout<D, REPL>;
+  const float sc = scale ? *scale : 1.0f;  // one-stage tables only
   if constexpr (!REPL) {
     if constexpr (R == 1) {  // plain one-stage table: first rounding in place
-      for (int e = threadIdx.x; e < entries; e += blockDim.x) {
+      if (scale) {
+        for (int e = threadIdx.x; e < entries; e += blockDim.x) {
 #pragma unroll
-        for (int j = 0; j < L::kPieces; ++j) {
-          uint2* pv = reinterpret_cast<uint2*>(cb + L::piece_offset(0, e, j, 0, entries));
-          uint2 v = *pv;
-          v.x = preround_pair(v.x);
-          v.y = preround_pair(v.y);
-          *pv = v;
+          for (int j = 0; j < L::kPieces; ++j) {
+            uint2* pv = reinterpret_cast<uint2*>(cb + L::piece_offset(0, e, j, 0, entries));
+            uint2 v = *pv;
+            v.x = preround_pair_scaled(v.x, sc);
+            v.y = preround_pair_scaled(v.y, sc);
+            *pv = v;
+          }
+        }
+      } else {
+        for (int e = threadIdx.x; e < entries; e += blockDim.x) {
+#pragma unroll
+          for (int j = 0; j < L::kPieces; ++j) {
+            uint2* pv = reinterpret_cast<uint2*>(cb + L::piece_offset(0, e, j, 0, entries));
+            uint2 v = *pv;
+            v.x = preround_pair(v.x);
+            v.y = preround_pair(v.y);
+            *pv = v;
+          }
         }
       }
     }
@@ -236,10 +278,17 @@ __device__ void stage_codebooks_finish(uint8_t* cb, int entries) {
           const int off = D == 32 ? (run >> 1) * 128 + (run & 1) * 16 : run * 16;
           v[run] = *reinterpret_cast<const uint4*>(base + off);
           if (R == 1) {
-            v[run].x = preround_pair(v[run].x);
-            v[run].y = preround_pair(v[run].y);
-            v[run].z = preround_pair(v[run].z);
-            v[run].w = preround_pair(v[run].w);
+            if (scale) {  // uniform branch: every thread takes the same side
+              v[run].x = preround_pair_scaled(v[run].x, sc);
+              v[run].y = preround_pair_scaled(v[run].y, sc);
+              v[run].z = preround_pair_scaled(v[run].z, sc);
+              v[run].w = preround_pair_scaled(v[run].w, sc);
+            } else {
+              v[run].x = preround_pair(v[run].x);
+              v[run].y = preround_pair(v[run].y);
+              v[run].z = preround_pair(v[run].z);
+              v[run].w = preround_pair(v[run].w);
+            }
             *reinterpret_cast<uint4*>(base + off) = v[run];
           }
         }
@@ -256,13 +305,67 @@ __device__ void stage_codebooks_finish(uint8_t* cb, int entries) {
   }
 }
 
+// fp32 replicated tables for scaled multi-stage codebooks: every thread
+// converts whole entries, value RN(fp32(c) * scale[s]) (stage 0 also + 0.0f,
+// as the reference's sum starts from +0.0), and writes the 8 lane-class
+// copies.  Follow with __syncthreads().
+template <int D, int R>
+__device__ void stage_codebooks_scaled(uint8_t* cb, const uint16_t* __restrict__ books, const float* scales,
+                                       int entries) {
+  using L = CbLayout<D, true, true>;
+  for (int s = 0; s < R; ++s) {
+    const float sc = scales[s];
+    for (int e = threadIdx.x; e < entries; e += blockDim.x) {
+      const uint16_t* src = books + ((size_t)s * entries + e) * D;
+      float v[D];
+#pragma unroll
+      for (int j = 0; j < D; j += 8) {
+        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(src + j));
+        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const __half2 h = *reinterpret_cast<const __half2*>(&w[t]);
+          v[j + 2 * t] = __fmul_rn(__half2float(__low2half(h)), sc);
+          v[j + 2 * t + 1] = __fmul_rn(__half2float(__high2half(h)), sc);
+        }
+      }
+      if (s == 0) {
+#pragma unroll
+        for (int j = 0; j < D; ++j) v[j] = __fadd_rn(0.0f, v[j]);
+      }
+      uint8_t* row = cb + L::stage_offset(s) + e * 256;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        if (D == 8) {
+          const int h = (c & 1) * 4;
+          *reinterpret_cast<float4*>(row + c * 16) = make_float4(v[h], v[h + 1], v[h + 2], v[h + 3]);
+        } else if (D == 16) {
+          const int q4 = (c & 3) * 4;
+          *reinterpret_cast<float4*>(row + c * 16) = make_float4(v[q4], v[q4 + 1], v[q4 + 2], v[q4 + 3]);
+        } else {
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            const int b = hf * 16 + (c & 3) * 4;
+            *reinterpret_cast<float4*>(row + hf * 128 + c * 16) = make_float4(v[b], v[b + 1], v[b + 2], v[b + 3]);
+          }
+        }
+      }
+    }
+  }
+}
+
 // One-call staging for kernels without other prologue work.
-template <int D, int R, bool REPL>
-__device__ void stage_codebooks(uint8_t* cb, const uint16_t* __restrict__ books, int entries) {
+template <int D, int R, bool REPL, bool SC = false>
+__device__ void stage_codebooks(uint8_t* cb, const uint16_t* __restrict__ books, int entries,
+                                const float* scales = nullptr) {
+  if constexpr (SC && REPL && R > 1) {
+    stage_codebooks_scaled<D, R>(cb, books, scales, entries);
+    return;
+  }
   stage_codebooks_issue<D, R, REPL>(cb, books, entries);
   cp_async_wait_all();
   __syncthreads();
-  stage_codebooks_finish<D, R, REPL>(cb, entries);
+  stage_codebooks_finish<D, R, REPL>(cb, entries, scales);
 }
 
 // ---------------------------------------------------------------------------
@@ -279,14 +382,14 @@ struct LaneSel {
   uint32_t self8[2];  // id byte -> byte 1, lane offset (second operand, byte 0) -> byte 0
   uint32_t sel16;
   uint32_t lane_off;  // replicated-layout lane offset (< 256)
-  __device__ LaneSel(int r, int q) {
+  __device__ LaneSel(int r, int q, bool f32 = false) {
     const uint32_t qh = (uint32_t)(q >> 1);
     sel8[0] = 0x4440u + qh;
     sel8[1] = 0x4442u + qh;
     self8[0] = 0x5504u | (qh << 4);
     self8[1] = 0x5504u | ((2u + qh) << 4);
     sel16 = qh ? 0x4432u : 0x4410u;
-    lane_off = (uint32_t)((r & 3) * 32 + q * 8);
+    lane_off = f32 ? (uint32_t)(((r & 1) * 4 + q) * 16) : (uint32_t)((r & 3) * 32 + q * 8);
   }
 };
 
@@ -332,6 +435,13 @@ __device__ __forceinline__ uint2 lds64(uint32_t saddr) {
   return v;
 }
 
+template <int OFF>
+__device__ __forceinline__ float4 lds128(uint32_t saddr) {
+  float4 v;
+  asm("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4+%5];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(saddr), "n"(OFF));
+  return v;
+}
+
 // Ordered variant for buffers written earlier in the kernel (activations).
 template <int OFF>
 __device__ __forceinline__ uint2 lds64_ordered(uint32_t saddr) {
@@ -355,12 +465,25 @@ __device__ __forceinline__ uint32_t piece_addr(const uint32_t (&codes)[NW], uint
 // out[0] = columns 4q, 4q+1; out[1] = columns 4q+2, 4q+3 (both already
 // multiplied by the row scale with the second rounding).
 // cb = shared codebook base, cbl = cb + this lane's offset (plain layouts).
-template <int D, int R, int IDW, bool REPL, int KT, int NW>
+template <int D, int R, int IDW, bool REPL, int KT, int NW, bool SC = false>
 __device__ __forceinline__ void decode_row(uint32_t (&out)[2], const uint32_t (&codes)[NW], uint32_t cb, uint32_t cbl,
                                            uint32_t rho2, const LaneSel& ls) {
   using L = CbLayout<D, REPL>;
   constexpr int half_off = (D == 32) ? (KT & 1) * L::kHalfStride : 0;
-  if (R == 1) {
+  if constexpr (SC && REPL && R > 1) {  // scaled fp32 tables (LaneSel built with f32 = true)
+    float4 t = lds128<L::stage_offset(0) + half_off>(cb + id_addr256<D, KT, 0, NW>(codes, ls));
+#pragma unroll
+    for (int s = 1; s < R; ++s) {
+      float4 u;
+      if (s == 1) u = lds128<L::stage_offset(1) + half_off>(cb + id_addr256<D, KT, 1, NW>(codes, ls));
+      if (s == 2) u = lds128<L::stage_offset(2) + half_off>(cb + id_addr256<D, KT, 2, NW>(codes, ls));
+      if (s == 3) u = lds128<L::stage_offset(3) + half_off>(cb + id_addr256<D, KT, 3, NW>(codes, ls));
+      add_f32x2(t.x, t.y, u.x, u.y);
+      add_f32x2(t.z, t.w, u.z, u.w);
+    }
+    out[0] = mul_bf16x2_rn(pack_bf16x2_rn(t.x, t.y), rho2);
+    out[1] = mul_bf16x2_rn(pack_bf16x2_rn(t.z, t.w), rho2);
+  } else if (R == 1) {
     const uint2 p = lds64<half_off>(piece_addr<D, R, IDW, REPL, KT, NW, 0>(codes, cb, ls, cbl));
     out[0] = mul_bf16x2_rn(p.x, rho2);
     out[1] = mul_bf16x2_rn(p.y, rho2);

@@ -449,6 +449,7 @@ extern "C" int wal_rvq_gemm(const wal_rvq_layer* layer, const uint16_t* x, int64
   if (g.block_size != 8 || g.num_stages < 1 || g.num_stages > 2 || g.num_entries > 256) return WAL_ERR_UNSUPPORTED;
   if (g.num_groups < 1 || g.num_groups > 64) return WAL_ERR_UNSUPPORTED;
   if (!layer->packed_ids || !layer->codebooks || !layer->row_scale) return WAL_ERR_INVALID_ARGUMENT;
+  if (layer->stage_scales) return WAL_ERR_UNSUPPORTED;  // scaled stages: the GEMV path handles them
   if (ldx < g.in_features || ldy < g.out_features) return WAL_ERR_SHAPE;
   if ((ldx % 8) || ((uintptr_t)x & 15) || ((uintptr_t)layer->codebooks & 15) || ((uintptr_t)layer->packed_ids & 15))
     return WAL_ERR_ALIGNMENT;

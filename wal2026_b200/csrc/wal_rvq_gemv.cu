@@ -34,6 +34,7 @@ struct GemvParams {
   const uint16_t* codebooks;
   const uint16_t* row_scale;
   const uint16_t* bias;
+  const float* stage_scales;  // fp32 [groups][R] or null
   const uint16_t* x;
   void* y;
   long long ldx, ldy;
@@ -159,7 +160,7 @@ struct GemvCfg {
   }
 };
 
-template <int D, int R, int IDW, bool REPL, int MT, bool XS, bool MASK>
+template <int D, int R, int IDW, bool REPL, int MT, bool XS, bool MASK, bool SC>
 __device__ __forceinline__ void gemv_chunk(float (&acc)[GemvCfg<D, R, IDW, REPL, MT, XS>::kAcc][MT][4], const uint32_t (&c0)[R * IDW * 4],
                                            const uint32_t (&c1)[R * IDW * 4], uint32_t cb, uint32_t cbl, uint32_t rho_a,
                                            uint32_t rho_b, const LaneSel& ls, const uint16_t* x, const uint32_t (&xoff)[MT],
@@ -168,8 +169,8 @@ __device__ __forceinline__ void gemv_chunk(float (&acc)[GemvCfg<D, R, IDW, REPL,
   static_for<0, D>([&](auto ktc) {
     constexpr int kt = decltype(ktc)::value;
     uint32_t ra[2], rb[2];
-    decode_row<D, R, IDW, REPL, kt, C::NW>(ra, c0, cb, cbl, rho_a, ls);
-    decode_row<D, R, IDW, REPL, kt, C::NW>(rb, c1, cb, cbl, rho_b, ls);
+    decode_row<D, R, IDW, REPL, kt, C::NW, SC>(ra, c0, cb, cbl, rho_a, ls);
+    decode_row<D, R, IDW, REPL, kt, C::NW, SC>(rb, c1, cb, cbl, rho_b, ls);
     const int col = col_base + kt * 16;  // lane's first physical column (includes 4q)
     const bool in_k = !MASK || col < K;
     uint2 xf[MT];
@@ -193,7 +194,7 @@ __device__ __forceinline__ void gemv_chunk(float (&acc)[GemvCfg<D, R, IDW, REPL,
   });
 }
 
-template <int D, int R, int IDW, bool REPL, int MT, bool XS>
+template <int D, int R, int IDW, bool REPL, int MT, bool XS, bool SC>
 __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
     rvq_gemv_kernel(const __grid_constant__ GemvParams p) {
   using C = GemvCfg<D, R, IDW, REPL, MT, XS>;
@@ -216,7 +217,8 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
   const int ssh = 4 - wsh;                    // slots = 16 / wpt = 1 << ssh
   const int slots = 1 << ssh;
   const int slot = warp >> wsh, kpart = warp & (wpt - 1);
-  const LaneSel ls(r, q);
+  constexpr bool kF32 = SC && REPL && R > 1;  // scaled fp32 tables
+  const LaneSel ls(r, q, kF32);
 
   int group, tb, te;
   cta_range(p, blockIdx.x, &group, &tb, &te);
@@ -277,13 +279,19 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
   // so with programmatic dependent launch it overlaps the previous kernel;
   // only the activations wait for it.
   // groups: 0 = codebooks, 1..kRing-1 = first id chunks, kRing = activations
-  stage_codebooks_issue<D, R, REPL>(cb, p.codebooks + (size_t)group * R * p.entries * D, p.entries);
+  const uint16_t* gbooks = p.codebooks + (size_t)group * R * p.entries * D;
+  const float* gscales = p.stage_scales ? p.stage_scales + (size_t)group * R : nullptr;
+  if constexpr (!kF32) stage_codebooks_issue<D, R, REPL>(cb, gbooks, p.entries);
   cp_async_commit();
 #pragma unroll 1
   for (int s = 0; s < kRing - 1; ++s) issue();
-  cp_async_wait<kRing - 1>();  // codebooks landed
-  __syncthreads();
-  stage_codebooks_finish<D, R, REPL>(cb, p.entries);
+  if constexpr (kF32) {
+    stage_codebooks_scaled<D, R>(cb, gbooks, gscales, p.entries);  // plain loads, id chunks in flight
+  } else {
+    cp_async_wait<kRing - 1>();  // codebooks landed
+    __syncthreads();
+    stage_codebooks_finish<D, R, REPL>(cb, p.entries, gscales);
+  }
   if (p.pdl) grid_dependency_wait();  // x (and y) belong to the previous kernel in the stream
   if (XS) {
     const uint64_t x_pol = l2_policy_evict_last();
@@ -386,10 +394,10 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
         const int c = kpart + j * wpt;
         const int col_base = c * kChunkBlocks * D + 4 * q;
         if (need_mask && c == p.chunks - 1) {
-          gemv_chunk<D, R, IDW, REPL, MT, XS, true>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, p.x, xoff, xsa, xv,
+          gemv_chunk<D, R, IDW, REPL, MT, XS, true, SC>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, p.x, xoff, xsa, xv,
                                                     col_base, p.K);
         } else {
-          gemv_chunk<D, R, IDW, REPL, MT, XS, false>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, p.x, xoff, xsa, xv,
+          gemv_chunk<D, R, IDW, REPL, MT, XS, false, SC>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, p.x, xoff, xsa, xv,
                                                      col_base, p.K);
         }
       }
@@ -442,7 +450,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
 
 // Weight materialisation through the same decode path: fragments stored
 // instead of fed to the tensor cores.  One warp per tile.
-template <int D, int R, int IDW, bool REPL>
+template <int D, int R, int IDW, bool REPL, bool SC>
 __global__ void __launch_bounds__(kThreads) rvq_dequant_kernel(const __grid_constant__ GemvParams p, uint16_t* w,
                                                                long long ldw) {
   using C = GemvCfg<D, R, IDW, REPL, 1, false>;
@@ -451,11 +459,12 @@ __global__ void __launch_bounds__(kThreads) rvq_dequant_kernel(const __grid_cons
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, q = lane & 3;
-  const LaneSel ls(r, q);
+  const LaneSel ls(r, q, SC && REPL && R > 1);
   int group, tb, te;
   cta_range(p, blockIdx.x, &group, &tb, &te);
   if (tb >= te) return;
-  stage_codebooks<D, R, REPL>(smem, p.codebooks + (size_t)group * R * p.entries * D, p.entries);
+  stage_codebooks<D, R, REPL, SC>(smem, p.codebooks + (size_t)group * R * p.entries * D, p.entries,
+                                  p.stage_scales ? p.stage_scales + (size_t)group * R : nullptr);
   __syncthreads();
   const uint32_t cb_s = smem_u32(smem);
   const uint32_t cbl = cb_s + L::lane_offset(r, q);
@@ -477,8 +486,8 @@ __global__ void __launch_bounds__(kThreads) rvq_dequant_kernel(const __grid_cons
       static_for<0, D>([&](auto ktc) {
         constexpr int kt = decltype(ktc)::value;
         uint32_t ra[2], rb[2];
-        decode_row<D, R, IDW, REPL, kt, C::NW>(ra, c0, cb_s, cbl, rho_a, ls);
-        decode_row<D, R, IDW, REPL, kt, C::NW>(rb, c1, cb_s, cbl, rho_b, ls);
+        decode_row<D, R, IDW, REPL, kt, C::NW, SC>(ra, c0, cb_s, cbl, rho_a, ls);
+        decode_row<D, R, IDW, REPL, kt, C::NW, SC>(rb, c1, cb_s, cbl, rho_b, ls);
         const int col = c * kChunkBlocks * D + kt * 16 + 4 * q;
         if (col < p.K) {
           if (r < ti.z) *reinterpret_cast<uint2*>(w + (long long)(ti.y + r) * ldw + col) = make_uint2(ra[0], ra[1]);
@@ -536,7 +545,8 @@ int check_layer(const wal_rvq_layer* L) {
   if (g.in_features % 4 != 0) return WAL_ERR_UNSUPPORTED;
   if (g.num_groups > kMaxGroups) return WAL_ERR_UNSUPPORTED;
   if (!L->packed_ids || !L->tile_table || !L->codebooks || !L->row_scale) return WAL_ERR_INVALID_ARGUMENT;
-  if (((uintptr_t)L->packed_ids & 15) || ((uintptr_t)L->tile_table & 15) || ((uintptr_t)L->codebooks & 15))
+  if (((uintptr_t)L->packed_ids & 15) || ((uintptr_t)L->tile_table & 15) || ((uintptr_t)L->codebooks & 15) ||
+      ((uintptr_t)L->stage_scales & 3))
     return WAL_ERR_ALIGNMENT;
   return WAL_OK;
 }
@@ -607,10 +617,10 @@ int persistent_grid(Kern kern, int threads, int smem, int num_ctas, GemvParams& 
 
 using namespace wal;
 
-template <int D, int R, int IDW, bool REPL, int MT, bool XS>
+template <int D, int R, int IDW, bool REPL, int MT, bool XS, bool SC = false>
 static int run_gemv(GemvParams p, int num_ctas, cudaStream_t stream) {
   using C = GemvCfg<D, R, IDW, REPL, MT, XS>;
-  auto kern = rvq_gemv_kernel<D, R, IDW, REPL, MT, XS>;
+  auto kern = rvq_gemv_kernel<D, R, IDW, REPL, MT, XS, SC>;
   const int kpad = p.chunks * kChunkBlocks * D;
   const int smem = C::smem(p.entries, p.M, kpad);
   if (smem > 227 * 1024) return WAL_ERR_UNSUPPORTED;
@@ -638,10 +648,10 @@ static int run_gemv(GemvParams p, int num_ctas, cudaStream_t stream) {
   return cudaGetLastError() == cudaSuccess ? WAL_OK : WAL_ERR_CUDA;
 }
 
-template <int D, int R, int IDW, bool REPL>
+template <int D, int R, int IDW, bool REPL, bool SC = false>
 static int run_dequant(GemvParams p, uint16_t* w, long long ldw, cudaStream_t stream) {
   using C = GemvCfg<D, R, IDW, REPL, 1, false>;
-  auto kern = rvq_dequant_kernel<D, R, IDW, REPL>;
+  auto kern = rvq_dequant_kernel<D, R, IDW, REPL, SC>;
   const int smem = C::cb_bytes(p.entries);
   if (smem > 227 * 1024) return WAL_ERR_UNSUPPORTED;
   int grid = 0;
@@ -655,6 +665,16 @@ static int run_dequant(GemvParams p, uint16_t* w, long long ldw, cudaStream_t st
 // shared memory (never for 4 n-tiles: 32 rows of activations do not fit)
 template <int D, int R, int IDW>
 static int dispatch_gemv(const GemvParams& p, int num_ctas, cudaStream_t stream, bool repl, int mt, bool xs) {
+  if constexpr (IDW == 1 && R > 1) {
+    if (p.stage_scales) {  // scaled multi-stage tables: fp32 replicated layout only
+      if (!repl) return WAL_ERR_UNSUPPORTED;
+      if (mt == 1) return xs ? run_gemv<D, R, IDW, true, 1, true, true>(p, num_ctas, stream)
+                             : run_gemv<D, R, IDW, true, 1, false, true>(p, num_ctas, stream);
+      if (mt == 2) return xs ? run_gemv<D, R, IDW, true, 2, true, true>(p, num_ctas, stream)
+                             : run_gemv<D, R, IDW, true, 2, false, true>(p, num_ctas, stream);
+      return run_gemv<D, R, IDW, true, 4, false, true>(p, num_ctas, stream);
+    }
+  }
   if constexpr (IDW == 1) {
     if (repl) {
       if (mt == 1) return xs ? run_gemv<D, R, IDW, true, 1, true>(p, num_ctas, stream)
@@ -673,6 +693,12 @@ static int dispatch_gemv(const GemvParams& p, int num_ctas, cudaStream_t stream,
 
 template <int D, int R, int IDW>
 static int dispatch_dequant(const GemvParams& p, uint16_t* w, long long ldw, cudaStream_t stream, bool repl) {
+  if constexpr (IDW == 1 && R > 1) {
+    if (p.stage_scales) {
+      if (!repl) return WAL_ERR_UNSUPPORTED;
+      return run_dequant<D, R, IDW, true, true>(p, w, ldw, stream);
+    }
+  }
   if constexpr (IDW == 1) {
     if (repl) return run_dequant<D, R, IDW, true>(p, w, ldw, stream);
   }
@@ -745,6 +771,7 @@ static int make_params(const wal_rvq_layer* L, GemvParams* p) {
   p->codebooks = L->codebooks;
   p->row_scale = L->row_scale;
   p->bias = L->bias;
+  p->stage_scales = L->stage_scales;
   p->num_tiles = L->num_tiles;
   p->K = (int)g.in_features;
   p->chunks = (int)((blocks + kChunkBlocks - 1) / kChunkBlocks);

@@ -9,6 +9,7 @@ from __future__ import annotations
 
 import ctypes
 from dataclasses import dataclass
+from typing import Optional
 
 import numpy as np
 import torch
@@ -27,6 +28,7 @@ class PackedArrays:
     tile_table: torch.Tensor  # int32 [num_tiles, 4]
     codebooks: torch.Tensor   # fp16 [groups, R, entries, d]
     row_scale: torch.Tensor   # fp16 [N]
+    stage_scales: Optional[torch.Tensor] = None  # fp32 [groups, R] per-stage scales
 
 
 def _geometry(N: int, K: int, d: int, R: int, entries: int, groups: int) -> _abi.Geometry:
@@ -50,8 +52,8 @@ def validate_grouped(enc: GroupedBlockRVQEncoding) -> tuple[int, int, int, int]:
     row = 0
     for g, (r0, r1) in zip(enc.groups, enc.row_slices):
         if not g.is_plain():
-            raise ValueError("packed CUDA path supports plain Block-RVQ encodings only "
-                             "(no stage_scales, block_scale, residual correction or transform)")
+            raise ValueError("packed CUDA path supports Block-RVQ encodings without per-block corrections "
+                             "(no block_scale, residual correction or transform)")
         if int(g.block_size) != d or int(g.num_stages) != R:
             raise ValueError("all row groups must share block_size and num_stages")
         if any(int(c.shape[0]) != entries or int(c.shape[1]) != d for c in g.codebooks):
@@ -126,7 +128,16 @@ def pack_grouped(enc: GroupedBlockRVQEncoding) -> PackedArrays:
         [torch.stack([c.detach().cpu().to(torch.float16) for c in g.codebooks]) for g in enc.groups]
     ).contiguous()
     rho = torch.cat([g.row_scale.detach().cpu().to(torch.float16).reshape(-1) for g in enc.groups]).contiguous()
-    return PackedArrays(geom, int(ntiles.value), packed, table, books, rho)
+    scales = None
+    if any(g.stage_scales is not None for g in enc.groups):
+        # groups without scales get 1.0 (fp32(c) * 1.0 == c: the same sum)
+        scales = torch.stack([
+            torch.ones(R, dtype=torch.float32) if g.stage_scales is None
+            else g.stage_scales.detach().cpu().to(torch.float32).reshape(-1)[:R]
+            for g in enc.groups]).contiguous()
+        if scales.shape != (G, R):
+            raise ValueError("stage_scales must hold one value per stage")
+    return PackedArrays(geom, int(ntiles.value), packed, table, books, rho, scales)
 
 
 def pack_routes(route: torch.Tensor, code: torch.Tensor, codebooks: torch.Tensor, row_scale: torch.Tensor,

@@ -154,6 +154,10 @@ class PackedGroupedBlockRVQLinear(nn.Module):
         self.register_buffer("tile_table", packed.tile_table)
         self.register_buffer("codebooks", packed.codebooks)
         self.register_buffer("row_scale", packed.row_scale)
+        if packed.stage_scales is not None:
+            self.register_buffer("stage_scales", packed.stage_scales.to(torch.float32).contiguous())
+        else:
+            self.stage_scales = None
 
     @classmethod
     def random(
@@ -245,7 +249,8 @@ class PackedGroupedBlockRVQLinear(nn.Module):
         geom = _abi.Geometry(out_features=self.out_features, in_features=self.in_features,
                              block_size=self.block_size, num_stages=self.num_stages,
                              num_entries=self.num_entries, num_groups=self.num_groups)
-        return PackedArrays(geom, self.num_tiles, self.packed_ids, self.tile_table, self.codebooks, self.row_scale)
+        return PackedArrays(geom, self.num_tiles, self.packed_ids, self.tile_table, self.codebooks, self.row_scale,
+                            self.stage_scales)
 
     def group_rows(self) -> list[int]:
         return [r1 - r0 for r0, r1 in self.row_slices]
@@ -254,7 +259,8 @@ class PackedGroupedBlockRVQLinear(nn.Module):
     def layer_struct(self) -> _abi.Layer:
         """The ``wal_rvq_layer`` descriptor of this module's current device buffers."""
         key = (self.packed_ids.data_ptr(), self.tile_table.data_ptr(), self.codebooks.data_ptr(),
-               self.row_scale.data_ptr(), None if self.bias is None else self.bias.data_ptr())
+               self.row_scale.data_ptr(), None if self.bias is None else self.bias.data_ptr(),
+               None if self.stage_scales is None else self.stage_scales.data_ptr())
         if self._layer_cache is not None and self._layer_cache[0] == key:
             return self._layer_cache[1]
         geom = _abi.Geometry(out_features=self.out_features, in_features=self.in_features,
@@ -264,7 +270,8 @@ class PackedGroupedBlockRVQLinear(nn.Module):
         self._group_rows = (ctypes.c_int64 * len(rows))(*rows)  # kept alive with the descriptor
         layer = _abi.Layer(geom=geom, num_tiles=self.num_tiles, packed_ids=key[0], tile_table=key[1],
                            codebooks=key[2], row_scale=key[3], bias=key[4],
-                           group_rows=ctypes.cast(self._group_rows, ctypes.POINTER(ctypes.c_int64)))
+                           group_rows=ctypes.cast(self._group_rows, ctypes.POINTER(ctypes.c_int64)),
+                           stage_scales=key[5])
         self._layer_cache = (key, layer)
         return layer
 

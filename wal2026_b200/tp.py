@@ -113,7 +113,7 @@ def shard_packed(lin: PackedGroupedBlockRVQLinear, rank: int, size: int, mode: s
         geom = _abi.Geometry(out_features=row_out, in_features=lin.in_features, block_size=d, num_stages=R,
                              num_entries=lin.num_entries, num_groups=lin.num_groups)
         arrays = PackedArrays(geom, len(table), new_packed, torch.tensor(table, dtype=torch.int32, device=dev),
-                              lin.codebooks, torch.cat(rho).contiguous())
+                              lin.codebooks, torch.cat(rho).contiguous(), lin.stage_scales)
         bias = None
         if lin.bias is not None:
             parts, r = [], 0
@@ -129,7 +129,7 @@ def shard_packed(lin: PackedGroupedBlockRVQLinear, rank: int, size: int, mode: s
         new_packed = packed.view(T, chunks, V * 256)[:, c0:c1].reshape(-1).contiguous()
         geom = _abi.Geometry(out_features=lin.out_features, in_features=k1 - k0, block_size=d, num_stages=R,
                              num_entries=lin.num_entries, num_groups=lin.num_groups)
-        arrays = PackedArrays(geom, T, new_packed, lin.tile_table, lin.codebooks, lin.row_scale)
+        arrays = PackedArrays(geom, T, new_packed, lin.tile_table, lin.codebooks, lin.row_scale, lin.stage_scales)
         return PackedGroupedBlockRVQLinear.from_packed(arrays, rows, bias=None)
     raise ValueError(f"unknown shard mode {mode!r}")
 
