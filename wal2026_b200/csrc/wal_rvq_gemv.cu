@@ -250,6 +250,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
   const uint32_t step_tile = (uint32_t)(slots * tile_bytes) - (uint32_t)cpw * step_chunk;
   uint32_t is_off = 0;
   const uint32_t ring_lane = smem_u32(wring) + lane * 16;
+  const uint32_t ring_row = smem_u32(wring) + r * 16;  // this lane's row r; row r + 8 is 128 bytes on
   const uint64_t stream_pol = l2_policy_evict_first();
   int is_left = items;
   int is_j = 0;
@@ -380,14 +381,17 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
       for (int j = 0; j < cpw; ++j, ++it) {
         cp_async_wait<kRing - 2>();
         __syncwarp();
-        const uint8_t* st = wring + (it & (kRing - 1)) * C::kStageBytes;
+        // 32-bit shared addresses (the ring slot of this item, this lane's rows)
+        const uint32_t st = ring_row + (uint32_t)(it & (kRing - 1)) * C::kStageBytes;
         uint32_t c0[V * 4], c1[V * 4];
 #pragma unroll
         for (int v = 0; v < V; ++v) {
-          const uint4 a = *reinterpret_cast<const uint4*>(st + v * 256 + r * 16);
-          const uint4 b = *reinterpret_cast<const uint4*>(st + v * 256 + (r + 8) * 16);
-          c0[4 * v] = a.x; c0[4 * v + 1] = a.y; c0[4 * v + 2] = a.z; c0[4 * v + 3] = a.w;
-          c1[4 * v] = b.x; c1[4 * v + 1] = b.y; c1[4 * v + 2] = b.z; c1[4 * v + 3] = b.w;
+          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(c0[4 * v]), "=r"(c0[4 * v + 1]), "=r"(c0[4 * v + 2]), "=r"(c0[4 * v + 3])
+                       : "r"(st + v * 256));
+          asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(c1[4 * v]), "=r"(c1[4 * v + 1]), "=r"(c1[4 * v + 2]), "=r"(c1[4 * v + 3])
+                       : "r"(st + v * 256 + 128));
         }
         __syncwarp();
         issue();
