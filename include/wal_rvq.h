@@ -296,6 +296,26 @@ WAL_API int wal_silu_mul(const uint16_t* gu, int64_t ld_gu, int64_t M, int64_t I
                  int64_t ld_out, void* stream);
 
 /*
+ * Decode attention (one query token per sequence, grouped-query heads):
+ * out[b, h*hd:(h+1)*hd] = softmax(q[b, h] . k[b, h/G, t] * scale) v[b, h/G, t]
+ * over positions t < n, G = hq / hkv.  q: bf16 rows ld_q apart (q heads
+ * contiguous, 8-byte aligned); k_cache/v_cache: bf16 [B, hkv, cache_len, hd]
+ * contiguous, 16-byte aligned; out: bf16 rows ld_out apart.  hd in {64, 128},
+ * G in {1, 2, 4, 8}.
+ * workspace: device scratch of at least wal_decode_attention_workspace(...)
+ * bytes, 256-byte aligned and zero-filled before its first use (the kernel
+ * leaves its counters at zero again); calls sharing one workspace must not
+ * overlap in time.  Split-K over positions with an exact (log-sum-exp)
+ * merge in split order: deterministic.  No reference counterpart (the
+ * reference runs Hugging Face attention).
+ */
+WAL_API size_t wal_decode_attention_workspace(int64_t B, int32_t hq, int32_t hkv, int32_t hd, int64_t n);
+WAL_API int wal_decode_attention(const uint16_t* q, int64_t ld_q, const uint16_t* k_cache,
+                         const uint16_t* v_cache, int64_t B, int32_t hq, int32_t hkv, int32_t hd,
+                         int64_t cache_len, int64_t n, float scale, uint16_t* out, int64_t ld_out,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Device memory shared with peer processes: create (cudaMalloc, zero-filled,
  * IPC handle of WAL_IPC_HANDLE_BYTES written to handle_out), open a peer's
  * handle (mapped with peer access), close a mapping, free own memory.

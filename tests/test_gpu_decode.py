@@ -12,7 +12,8 @@ import torch
 import torch.nn.functional as F
 
 from wal2026_b200 import _abi
-from wal2026_b200.decode_ops import residual_rmsnorm, rope_kv_append, silu_mul
+from wal2026_b200.decode_ops import (decode_attention, decode_attention_workspace, residual_rmsnorm, rope_kv_append,
+                                     silu_mul)
 from wal2026_b200.llama import LlamaShape, _rope, dense_llama, rvq_llama
 from wal2026_b200.runtime import PackedGroupedBlockRVQLinear
 from wal2026_b200.tp import PeerExchange
@@ -85,6 +86,30 @@ def test_silu_mul_matches_torch(M, I):
     torch.cuda.synchronize()
     _bf16_close(out, ref)
     assert float((out.float() != ref.float()).float().mean()) < 1e-3
+
+
+@pytest.mark.parametrize("B,hq,hkv,hd,L,n", [(1, 32, 8, 128, 2049, 2049), (3, 8, 2, 64, 600, 517), (2, 4, 4, 128, 40, 1),
+                                           (1, 64, 8, 128, 4096, 4000), (5, 8, 1, 128, 300, 300),
+                                           (64, 8, 1, 128, 4097, 4097)])
+def test_decode_attention_matches_reference_math(B, hq, hkv, hd, L, n):
+    g = _gen(B * 100 + n)
+    q = torch.randn(B, hq * hd, device=DEV, generator=g).to(torch.bfloat16)
+    kc = torch.randn(B, hkv, L, hd, device=DEV, generator=g).to(torch.bfloat16)
+    vc = torch.randn(B, hkv, L, hd, device=DEV, generator=g).to(torch.bfloat16)
+    out = torch.empty(B, hq * hd, device=DEV, dtype=torch.bfloat16)
+    ws = decode_attention_workspace(B, hq, hkv, hd, L, DEV)
+    decode_attention(q, kc, vc, n, out, ws)
+    # float64 reference on the same bf16 inputs
+    G = hq // hkv
+    qd = q.double().view(B, hkv, G, hd)
+    kd, vd = kc[:, :, :n].double(), vc[:, :, :n].double()
+    s = torch.einsum("bhgd,bhtd->bhgt", qd, kd) / hd ** 0.5
+    ref = torch.einsum("bhgt,bhtd->bhgd", torch.softmax(s, dim=-1), vd).reshape(B, hq * hd)
+    err = float((out.double() - ref).abs().max())
+    assert err <= 1e-2 * float(ref.abs().max()) + 1e-3, err
+    again = torch.empty_like(out)
+    decode_attention(q, kc, vc, n, again, ws)  # counters came back to zero: same bits
+    assert torch.equal(out, again)
 
 
 def _layer(N, K, seed=0):

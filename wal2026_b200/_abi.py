@@ -108,6 +108,10 @@ SIGNATURES: dict[str, tuple] = {
     "wal_idroute_pack": (_c_int, [_c_i64, _c_i64, ctypes.c_int32, _vp, _vp, ctypes.c_size_t]),
     "wal_idroute_gemv": (_c_int, [ctypes.POINTER(IDRouteLayer), _vp, _c_i64, _c_i64, _vp, _c_i64, _c_int, _vp]),
     "wal_idroute_dequant": (_c_int, [ctypes.POINTER(IDRouteLayer), _vp, _c_i64, _c_int, _vp]),
+    "wal_decode_attention_workspace": (ctypes.c_size_t, [_c_i64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                                         _c_i64]),
+    "wal_decode_attention": (_c_int, [_vp, _c_i64, _vp, _vp, _c_i64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                      _c_i64, _c_i64, ctypes.c_float, _vp, _c_i64, _vp, ctypes.c_size_t, _vp]),
     "wal_rvq_gemv_push": (_c_int, [_LP, _vp, _c_i64, _c_i64, ctypes.POINTER(TPPush), _vp]),
     "wal_tp_reduce_rmsnorm": (_c_int, [_vp, ctypes.c_int32, _c_i64, _c_i64, _vp, _vp, _vp, _c_i64, _vp,
                                        ctypes.c_float, _vp, _c_i64, _c_i64, _c_i64, _vp, _vp]),

@@ -63,3 +63,32 @@ def silu_mul(gu: Tensor, out: Tensor) -> None:
     st = lib.wal_silu_mul(gu.data_ptr(), gu.stride(0), M, I, out.data_ptr(), out.stride(0),
                           _abi.stream_handle(gu.device))
     _abi.check(st, "wal_silu_mul")
+
+
+def decode_attention_workspace(B: int, hq: int, hkv: int, hd: int, max_len: int, device) -> Tensor:
+    """Zero-filled scratch for ``decode_attention`` calls with up to ``max_len`` positions."""
+    nbytes = int(_abi.load().wal_decode_attention_workspace(B, hq, hkv, hd, max_len))
+    if nbytes == 0:
+        raise ValueError("invalid attention shape")
+    return torch.zeros(nbytes, dtype=torch.uint8, device=device)
+
+
+def decode_attention(q: Tensor, k_cache: Tensor, v_cache: Tensor, n: int, out: Tensor, workspace: Tensor,
+                     scale: Optional[float] = None) -> None:
+    """out[b] = softmax(q[b] k^T * scale) v over cache positions [0, n) (grouped-query heads).
+
+    q, out: bf16 [B, hq * hd]; caches: bf16 [B, hkv, cache_len, hd] contiguous;
+    ``workspace`` from ``decode_attention_workspace`` (not shared by overlapping calls).
+    """
+    _cuda(q, k_cache, v_cache, out, workspace)
+    B, hkv, L, hd = (int(v) for v in k_cache.shape)
+    hq = int(q.shape[1]) // hd
+    if not (k_cache.is_contiguous() and v_cache.is_contiguous()):
+        raise ValueError("caches must be contiguous")
+    scale = float(hd) ** -0.5 if scale is None else float(scale)
+    lib = _abi.load()
+    st = lib.wal_decode_attention(q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(), B, hq, hkv, hd,
+                                  L, int(n), scale, out.data_ptr(), out.stride(0), workspace.data_ptr(),
+                                  workspace.numel(), _abi.stream_handle(q.device))
+    _abi.check(st, "wal_decode_attention")
+

@@ -31,7 +31,7 @@ import torch
 import torch.nn.functional as F
 from torch import Tensor, nn
 
-from .decode_ops import residual_rmsnorm, rope_kv_append, silu_mul
+from .decode_ops import decode_attention, decode_attention_workspace, residual_rmsnorm, rope_kv_append, silu_mul
 from .runtime import PackedGroupedBlockRVQLinear
 from .tp import COLUMN, ROW, shard_bounds, shard_packed
 
@@ -160,15 +160,19 @@ class _DecodeBuffers:
         self.gu = torch.empty(batch, 2 * l0.mlp, device=dev, dtype=bf)
         self.act = torch.empty(batch, l0.mlp, device=dev, dtype=bf)
         self.y32 = torch.empty(batch, s.hidden, device=dev, dtype=torch.float32)
+        cache_len = stack.k_cache[0].shape[2] if stack.k_cache else 1
+        self.attn_ws = decode_attention_workspace(batch, l0.hq, l0.hkv, hd, cache_len, dev)
+        self.cache_len = cache_len
 
 
 class LlamaStack(nn.Module):
     """Decoder stack with a bf16 KV cache; ``decode_step`` advances every sequence by one token.
 
-    ``decode_step_fused`` is the production step: the linears plus three glue
-    kernels per block (RoPE/KV append, SiLU*mul, residual + RMSNorm after each
-    row-parallel linear) and, with ``exchange="push"`` under tensor
-    parallelism, the peer-memory exchange instead of an NCCL all-reduce.
+    ``decode_step_fused`` is the production step: the linears plus four glue
+    kernels per block (RoPE/KV append, split-K decode attention, SiLU*mul,
+    residual + RMSNorm after each row-parallel linear) and, with
+    ``exchange="push"`` under tensor parallelism, the peer-memory exchange
+    instead of an NCCL all-reduce.
     ``decode_step`` is the same computation with PyTorch operators.
     """
 
@@ -279,7 +283,7 @@ class LlamaStack(nn.Module):
             raise ValueError("call enable_push_exchange() before decode_step_fused(exchange='push')")
         B = tokens.shape[0]
         bufs = self._bufs.get(B)
-        if bufs is None:
+        if bufs is None or bufs.cache_len < self.k_cache[0].shape[2]:
             bufs = self._bufs[B] = _DecodeBuffers(self, B)
         s = self.shape
         hd = s.head_dim
@@ -289,9 +293,7 @@ class LlamaStack(nn.Module):
         for i, (layer, kc, vc) in enumerate(zip(self.layers, self.k_cache, self.v_cache)):
             _linear_into(layer.qkv, bufs.x, bufs.qkv)
             rope_kv_append(bufs.qkv, layer.hq, layer.hkv, hd, cos, sin, pos, bufs.q, kc, vc)
-            attn = F.scaled_dot_product_attention(bufs.q.view(B, layer.hq, 1, hd), kc[:, :, : pos + 1],
-                                                  vc[:, :, : pos + 1], enable_gqa=True)
-            bufs.attn.copy_(attn.reshape(B, layer.hq * hd))
+            decode_attention(bufs.q, kc, vc, pos + 1, bufs.attn, bufs.attn_ws)
             self._row_parallel_fused(layer.o, bufs.attn, 2 * i, layer.post_norm, bufs, exchange)
             _linear_into(layer.gate_up, bufs.x, bufs.gu)
             silu_mul(bufs.gu, bufs.act)
