@@ -316,6 +316,25 @@ WAL_API int wal_decode_attention(const uint16_t* q, int64_t ld_q, const uint16_t
                          void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * wal_decode_attention without a caller-provided workspace and without any
+ * allocation: scratch is a file-scope device array of 4 MiB per device
+ * (merge counters in a fixed 16 KiB region at its front, zero from module
+ * load and returned to zero by every call; partial outputs and stats after
+ * them).  Returns WAL_ERR_BUFFER_TOO_SMALL when B * hkv > 4096 or the
+ * partials need more than the remaining 4 MiB - 16 KiB (the bytes
+ * wal_decode_attention_workspace reports minus B * hkv * 4, rounded to 256).
+ * The first call on each device looks up the array's address
+ * (cudaGetSymbolAddress) and must come before any stream capture that
+ * records a later call.  All calls on one device share the array: calls that
+ * overlap in time (other streams, other host threads) race.  Results are
+ * bit-identical to wal_decode_attention.  No reference counterpart.
+ */
+WAL_API int wal_decode_attention_static(const uint16_t* q, int64_t ld_q, const uint16_t* k_cache,
+                         const uint16_t* v_cache, int64_t B, int32_t hq, int32_t hkv, int32_t hd,
+                         int64_t cache_len, int64_t n, float scale, uint16_t* out, int64_t ld_out,
+                         void* stream);
+
+/*
  * Device memory shared with peer processes: create (cudaMalloc, zero-filled,
  * IPC handle of WAL_IPC_HANDLE_BYTES written to handle_out), open a peer's
  * handle (mapped with peer access), close a mapping, free own memory.

@@ -21,6 +21,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 namespace {
 
 constexpr int kThreads = 128;     // 4 warps
@@ -268,6 +270,14 @@ void plan(long long B, int hkv, long long n, int* nsplit, int* chunk) {
   *chunk = (int)c;
 }
 
+// Scratch of wal_decode_attention_static, zero-filled at module load: the
+// merge counters occupy a fixed region at the front (so they are zero for any
+// shape, each call returning them to zero), partial outputs and stats follow.
+constexpr size_t kStaticScratchBytes = 4u << 20;  // 4 MiB
+constexpr size_t kStaticCounters = 4096;         // max B * hkv
+constexpr size_t kStaticDataOffset = kStaticCounters * sizeof(unsigned);
+static __device__ __align__(256) unsigned char g_attn_scratch[kStaticScratchBytes];
+
 size_t part_bytes(long long B, int hkv, int nsplit, int G, int hd) {
   return ((size_t)B * hkv * nsplit * G * hd * sizeof(float) + 255) & ~(size_t)255;
 }
@@ -318,39 +328,94 @@ size_t wal_decode_attention_workspace(int64_t B, int32_t hq, int32_t hkv, int32_
   return part_bytes(B, hkv, nsplit, G, hd) + stats_bytes(B, hkv, nsplit, G) + (size_t)B * hkv * sizeof(unsigned);
 }
 
-int wal_decode_attention(const uint16_t* q, int64_t ld_q, const uint16_t* k_cache, const uint16_t* v_cache, int64_t B,
-                         int32_t hq, int32_t hkv, int32_t hd, int64_t cache_len, int64_t n, float scale,
-                         uint16_t* out, int64_t ld_out, void* workspace, size_t workspace_bytes, void* stream) {
-  if (!q || !k_cache || !v_cache || !out || !workspace) return WAL_ERR_INVALID_ARGUMENT;
+}  // extern "C"
+
+namespace {
+
+// Argument checks and parameters shared by both entry points (scratch pointers left unset).
+int prepare(const uint16_t* q, int64_t ld_q, const uint16_t* k_cache, const uint16_t* v_cache, int64_t B, int32_t hq,
+            int32_t hkv, int32_t hd, int64_t cache_len, int64_t n, float scale, uint16_t* out, int64_t ld_out,
+            AttnParams* p) {
+  if (!q || !k_cache || !v_cache || !out) return WAL_ERR_INVALID_ARGUMENT;
   if (B <= 0 || hq <= 0 || hkv <= 0 || n <= 0 || cache_len <= 0 || n > cache_len) return WAL_ERR_SHAPE;
   if (hq % hkv || B * hkv > 0x7fffffff) return WAL_ERR_SHAPE;
   if (hd != 64 && hd != 128) return WAL_ERR_UNSUPPORTED;
   if (ld_q < (int64_t)hq * hd || ld_out < (int64_t)hq * hd) return WAL_ERR_SHAPE;
   if (((uintptr_t)q & 7) || ((uintptr_t)k_cache & 15) || ((uintptr_t)v_cache & 15) || ((uintptr_t)out & 7) ||
-      (ld_q % 4) || (ld_out % 4) || ((uintptr_t)workspace & 255))
+      (ld_q % 4) || (ld_out % 4))
     return WAL_ERR_ALIGNMENT;
-  const size_t need = wal_decode_attention_workspace(B, hq, hkv, hd, n);
-  if (workspace_bytes < need) return WAL_ERR_BUFFER_TOO_SMALL;
+  p->q = q;
+  p->ld_q = ld_q;
+  p->k = k_cache;
+  p->v = v_cache;
+  p->cache_len = cache_len;
+  p->n = (int)n;
+  p->hq = hq;
+  p->hkv = hkv;
+  p->hd = hd;
+  plan(B, hkv, n, &p->nsplit, &p->chunk);
+  p->qscale = scale * 1.4426950408889634f;  // log2(e)
+  p->out = out;
+  p->ld_out = ld_out;
+  return WAL_OK;
+}
+
+int run(const AttnParams& p, long long B, void* stream) {
+  const int G = p.hq / p.hkv;
+  return p.hd == 128 ? launch_g<128>(p, B, G, stream) : launch_g<64>(p, B, G, stream);
+}
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices];
+
+}  // namespace
+
+extern "C" {
+
+int wal_decode_attention(const uint16_t* q, int64_t ld_q, const uint16_t* k_cache, const uint16_t* v_cache, int64_t B,
+                         int32_t hq, int32_t hkv, int32_t hd, int64_t cache_len, int64_t n, float scale,
+                         uint16_t* out, int64_t ld_out, void* workspace, size_t workspace_bytes, void* stream) {
   AttnParams p;
-  p.q = q;
-  p.ld_q = ld_q;
-  p.k = k_cache;
-  p.v = v_cache;
-  p.cache_len = cache_len;
-  p.n = (int)n;
-  p.hq = hq;
-  p.hkv = hkv;
-  p.hd = hd;
-  plan(B, hkv, n, &p.nsplit, &p.chunk);
-  p.qscale = scale * 1.4426950408889634f;  // log2(e)
-  p.out = out;
-  p.ld_out = ld_out;
+  int st = prepare(q, ld_q, k_cache, v_cache, B, hq, hkv, hd, cache_len, n, scale, out, ld_out, &p);
+  if (st != WAL_OK) return st;
+  if (!workspace) return WAL_ERR_INVALID_ARGUMENT;
+  if ((uintptr_t)workspace & 255) return WAL_ERR_ALIGNMENT;
+  if (workspace_bytes < wal_decode_attention_workspace(B, hq, hkv, hd, n)) return WAL_ERR_BUFFER_TOO_SMALL;
   const int G = hq / hkv;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   p.part = reinterpret_cast<float*>(ws);
   p.stats = reinterpret_cast<float2*>(ws + part_bytes(B, hkv, p.nsplit, G, hd));
   p.counter = reinterpret_cast<unsigned*>(ws + part_bytes(B, hkv, p.nsplit, G, hd) + stats_bytes(B, hkv, p.nsplit, G));
-  return hd == 128 ? launch_g<128>(p, B, G, stream) : launch_g<64>(p, B, G, stream);
+  return run(p, B, stream);
+}
+
+int wal_decode_attention_static(const uint16_t* q, int64_t ld_q, const uint16_t* k_cache, const uint16_t* v_cache,
+                                int64_t B, int32_t hq, int32_t hkv, int32_t hd, int64_t cache_len, int64_t n,
+                                float scale, uint16_t* out, int64_t ld_out, void* stream) {
+  AttnParams p;
+  int st = prepare(q, ld_q, k_cache, v_cache, B, hq, hkv, hd, cache_len, n, scale, out, ld_out, &p);
+  if (st != WAL_OK) return st;
+  const int G = hq / hkv;
+  const size_t data = part_bytes(B, hkv, p.nsplit, G, hd) + stats_bytes(B, hkv, p.nsplit, G);
+  if ((size_t)B * hkv > kStaticCounters || data > kStaticScratchBytes - kStaticDataOffset)
+    return WAL_ERR_BUFFER_TOO_SMALL;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return WAL_ERR_CUDA;
+  void* base = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (!g_scratch_addr[dev] && cudaGetSymbolAddress(&g_scratch_addr[dev], g_attn_scratch) != cudaSuccess) {
+      g_scratch_addr[dev] = nullptr;
+      return WAL_ERR_CUDA;
+    }
+    base = g_scratch_addr[dev];
+  }
+  uint8_t* ws = static_cast<uint8_t*>(base);
+  p.counter = reinterpret_cast<unsigned*>(ws);
+  p.part = reinterpret_cast<float*>(ws + kStaticDataOffset);
+  p.stats = reinterpret_cast<float2*>(ws + kStaticDataOffset + part_bytes(B, hkv, p.nsplit, G, hd));
+  return run(p, B, stream);
 }
 
 }  // extern "C"
