@@ -27,6 +27,10 @@ Also reported in the same JSON line (BASELINE's second metric and config 3):
   prefill_8b  (N = 1) the stack's 128 projection GEMMs at M = 2048 tokens on
               the tcgen05 decode-to-shared-memory GEMM, TFLOP/s against the
               measured bf16 peak, next to cuBLAS on the same shapes;
+  decode_70b  (--decode-70b 1) config 4: the Llama-3-70B-shaped stack at
+              batch 1/16/64 on a 4096-token context, tensor-parallel over all
+              N GPUs; configurations that do not fit a GPU's memory at this
+              N are listed as skipped;
   idroute_gemv (N = 1) the ID-route linear (reference PackedIDRouteLinear:
               an int16 id per weight into fp16 route sums) on the 8B MLP
               shape, GB/s against the measured HBM bandwidth.
@@ -223,35 +227,61 @@ def _config(args) -> dict:
     }
 
 
-def run_decode(args, rank: int, world: int, dev: torch.device) -> dict:
-    """8B-shaped decode tok/s, tensor-parallel over every rank (all ranks call this together)."""
+def _decode_bytes_per_rank(shape, kind: str, batch: int, context: int, world: int) -> int:
+    """Device bytes one rank needs for a decode stack of this shape (weights, embeddings, KV cache, slack)."""
+    hd = shape.head_dim
+    per_layer = (shape.heads * hd + 2 * shape.kv_heads * hd) * shape.hidden + shape.heads * hd * shape.hidden \
+        + 3 * shape.mlp * shape.hidden
+    weights = shape.layers * per_layer * (2.0 if kind.startswith("dense") else 0.25) / world
+    embed = shape.vocab * shape.hidden * 2 * (1 + 1.0 / world)
+    kv = shape.layers * 2 * batch * (shape.kv_heads // world) * (context + 1) * hd * 2
+    draw = 2 * shape.mlp * shape.hidden * 6  # one full gate/up layer drawn before sharding (fp32 + bf16)
+    return int(weights + embed + kv + draw + 4e9)
+
+
+def run_decode(args, rank: int, world: int, dev: torch.device, which: str = "8b") -> dict:
+    """Llama-shaped decode tok/s, tensor-parallel over every rank (all ranks call this together)."""
     import torch.distributed as dist
 
-    from wal2026_b200.llama import LLAMA_8B, TPContext, dense_llama, rvq_llama, time_decode
+    from wal2026_b200.llama import SHAPES, TPContext, dense_llama, rvq_llama, time_decode
 
+    shape = SHAPES[which]
     tp = TPContext(rank, world, dist.group.WORLD if world > 1 else None)
-    batches = [int(b) for b in args.decode_batches.split(",") if b]
-    out = {"model": "Llama-3-8B shape (32 layers, hidden 4096, MLP 14336, 32 q / 8 kv heads, vocab 128256), "
-                    "random init; q/k/v/o/gate/up/down Block-RVQ d=8 R=2 256 entries; lm_head dense bf16",
-           "context": args.context, "tp": world, "exchange": "nvlink push (tagged words)" if world > 1 else "none",
+    if which == "8b":
+        batches, context = [int(b) for b in args.decode_batches.split(",") if b], args.context
+    else:
+        batches, context = [int(b) for b in args.decode70_batches.split(",") if b], args.context70
+    total = torch.cuda.get_device_properties(dev).total_memory
+    name = {"8b": "Llama-3-8B", "70b": "Llama-3-70B"}[which]
+    out = {"model": f"{name} shape ({shape.layers} layers, hidden {shape.hidden}, MLP {shape.mlp}, "
+                    f"{shape.heads} q / {shape.kv_heads} kv heads, vocab {shape.vocab}), random init; "
+                    "q/k/v/o/gate/up/down Block-RVQ d=8 R=2 256 entries; lm_head dense bf16",
+           "context": context, "tp": world, "exchange": "nvlink push (tagged words)" if world > 1 else "none",
            "graph": "one CUDA graph per decode step", "steps": args.decode_steps}
     for kind, ctor, exchange in (("rvq", rvq_llama, "push"), ("dense_bf16_cublas", dense_llama, "nccl")):
         if kind.startswith("dense") and not args.dense:
             continue
-        st = ctor(LLAMA_8B, device=dev, seed=0, tp=tp)
-        res = {}
-        for b in batches:
-            r = time_decode(st, b, args.context, steps=args.decode_steps, warmup=3, fused=True, exchange=exchange)
-            res[str(b)] = {"tok_s": round(r["tok_s"], 1), "ms_per_step": round(r["ms_per_step"], 4)}
-        if kind == "rvq":
-            out["rvq_projection_bytes_per_rank"] = st.linear_bytes()
-        st.close()
-        del st
-        torch.cuda.empty_cache()
-        out[kind] = res
+        fits = [b for b in batches if _decode_bytes_per_rank(shape, kind, b, context, world) < 0.85 * total]
+        res = {str(b): {"skipped": f"needs ~{_decode_bytes_per_rank(shape, kind, b, context, world) / 1e9:.0f} GB "
+                                   f"per GPU at tp={world}"} for b in batches if b not in fits}
+        if fits:
+            st = ctor(shape, device=dev, seed=0, tp=tp)
+            for b in fits:
+                r = time_decode(st, b, context, steps=args.decode_steps, warmup=3, fused=True, exchange=exchange)
+                res[str(b)] = {"tok_s": round(r["tok_s"], 1), "ms_per_step": round(r["ms_per_step"], 4)}
+                st.k_cache, st.v_cache = [], []
+                st._bufs.clear()
+                torch.cuda.empty_cache()
+            if kind == "rvq":
+                out["rvq_projection_bytes_per_rank"] = st.linear_bytes()
+            st.close()
+            del st
+            torch.cuda.empty_cache()
+        out[kind] = {b: res[b] for b in map(str, batches)}
     if "dense_bf16_cublas" in out:
-        out["rvq_speedup_vs_dense"] = {b: round(out["rvq"][b]["tok_s"] / out["dense_bf16_cublas"][b]["tok_s"], 3)
-                                       for b in out["rvq"]}
+        out["rvq_speedup_vs_dense"] = {
+            b: round(out["rvq"][b]["tok_s"] / out["dense_bf16_cublas"][b]["tok_s"], 3)
+            for b in out["rvq"] if "tok_s" in out["rvq"][b] and "tok_s" in out["dense_bf16_cublas"][b]}
     return out
 
 
@@ -472,6 +502,7 @@ def run_ours(args) -> None:
         del ws
 
     decode = run_decode(args, rank, world, dev) if args.decode else None
+    decode70 = run_decode(args, rank, world, dev, "70b") if args.decode_70b else None
     peaks = measured_peaks()
     prefill = run_prefill(args, dev, peaks) if (args.prefill and world == 1) else None
     idroute = run_idroute(args, dev, peaks) if (args.idroute and world == 1) else None
@@ -505,6 +536,7 @@ def run_ours(args) -> None:
             "cpu_baseline": cpu,
             "dense_bf16_cublas": dense,
             "decode_8b": decode,
+            "decode_70b": decode70,
             "prefill_8b": prefill,
             "idroute_gemv": idroute,
         }
@@ -532,6 +564,9 @@ def main() -> None:
     ap.add_argument("--decode-batches", default="1,8,32")
     ap.add_argument("--decode-steps", type=int, default=20)
     ap.add_argument("--context", type=int, default=2048)
+    ap.add_argument("--decode-70b", type=int, default=0, help="also time the 70B-shaped decode step (config 4)")
+    ap.add_argument("--decode70-batches", default="1,16,64")
+    ap.add_argument("--context70", type=int, default=4096)
     ap.add_argument("--prefill", type=int, default=1, help="also time the 8B-shaped prefill GEMMs (N = 1)")
     ap.add_argument("--prefill-tokens", type=int, default=2048)
     ap.add_argument("--prefill-steps", type=int, default=5)

@@ -114,6 +114,36 @@ def test_every_token_count(M):
     assert_close(gemv_f32(mod, x).cpu().numpy(), ref)
 
 
+# Activations too large to stage whole (M * K * 2 > 64 KB) stream through the
+# CTA's window ring: every n-tile count, ragged K (a partial last window and a
+# partial last block), 16-byte and 8-byte aligned activation rows, d = 8/16/32.
+@pytest.mark.parametrize("M,N,K,d,R,pad", [(9, 300, 4096, 8, 2, 0), (16, 200, 2052, 8, 2, 0), (8, 150, 8196, 8, 1, 0),
+                                          (16, 96, 4096, 8, 2, 4), (32, 100, 2560, 8, 2, 0), (24, 64, 4100, 8, 3, 0),
+                                          (12, 80, 4096, 16, 2, 0), (16, 48, 4128, 32, 1, 0)])
+def test_activation_window_ring(M, N, K, d, R, pad):
+    enc = single_group(synthetic.rvq_encoding(N, K, d=d, R=R, seed=M + K))
+    bias = synthetic.bias_vector(N, seed=K)
+    mod = PackedGroupedBlockRVQLinear(enc, bias).cuda()
+    x = synthetic.activations(M, K, seed=M)
+    xp = torch.zeros(M, K + pad, dtype=torch.bfloat16)
+    xp[:, :K] = x
+    xd = xp.cuda()[:, :K]
+    ref = orc.forward_f32(bits_of(x), orc.groups_from_encoding(enc), K, bits_of(bias))
+    for wpt in (0, 1, 4, 16):  # 16 warps per tile is cut down until the ring fits
+        y = torch.full((M, N), float("nan"), device="cuda")
+        mod.gemv_into(xd, y, warps_per_tile=wpt)
+        assert_close(y.cpu().numpy(), ref)
+
+
+def test_window_ring_routed_codebook_at_batch_16():
+    inp = synthetic.route_inputs(272, 4096, d=16, G=4, seed=8)
+    mod = RouteCodebookLinear.from_routes(inp.route, inp.code, inp.codebooks, inp.row_scale, in_features=4096).cuda()
+    enc = single_group(inp.encoding())
+    x = synthetic.activations(16, 4096, seed=8)
+    ref = orc.forward_f32(bits_of(x), orc.groups_from_encoding(enc), 4096)
+    assert_close(gemv_f32(mod, x).cpu().numpy(), ref)
+
+
 @pytest.mark.parametrize("wpt", [1, 2, 4, 8, 16])
 @pytest.mark.parametrize("ctas", [0, 1, 3])
 def test_work_split_variants_agree(wpt, ctas):

@@ -193,6 +193,16 @@ __device__ __forceinline__ void cp_async_8(uint32_t saddr, const void* gptr) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(saddr), "l"(gptr));
 }
 
+// Zero-filling copies: only the first src_bytes are read, the rest of the
+// destination is written as zeros (src_bytes = 0 reads nothing).
+__device__ __forceinline__ void cp_async_16_zfill(uint32_t saddr, const void* gptr, uint32_t src_bytes, uint64_t pol) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;\n" ::"r"(saddr), "l"(gptr),
+               "r"(src_bytes), "l"(pol));
+}
+__device__ __forceinline__ void cp_async_8_zfill(uint32_t saddr, const void* gptr, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(saddr), "l"(gptr), "r"(src_bytes));
+}
+
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::); }
 
 // One-stage tables with a stage scale: the staged bf16 value is

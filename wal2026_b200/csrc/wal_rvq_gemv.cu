@@ -1,11 +1,17 @@
 // Decode-time fused gather-GEMV (up to 32 tokens per launch), weight materialisation and
 // packed-id unpacking for the Block-RVQ runtime linear.
 //
-// GEMV structure (one persistent wave of CTAs, 8 warps each):
+// GEMV structure (one persistent wave of CTAs, 16 warps each):
 //   * every CTA works inside one row group: it stages that group's codebooks
-//     in shared memory once (cp.async) and, when they fit, the activations;
+//     in shared memory once (cp.async);
 //   * the CTA's tiles are processed in rounds of `slots` tiles; the 16-block
-//     chunks of a tile are split over `wpt` warps (slots * wpt = 8);
+//     chunks of a tile are split over `wpt` warps (slots * wpt = 16), warp
+//     `kpart` of a slot taking chunks kpart, kpart + wpt, ...;
+//   * activations: staged whole in shared memory when they fit; otherwise
+//     streamed through a three-deep window ring shared by the CTA: step j of a
+//     round needs the same wpt chunks' columns in every slot, so all warps step
+//     together (one CTA barrier per step) and each window of x is copied from
+//     L2 once per CTA instead of once per 16-row tile;
 //   * each warp walks its own flat list of (tile, chunk) items with a
 //     kRing-deep cp.async ring in shared memory, so id loads for later items
 //     are in flight while the current one is decoded (no spin-waits: the copy
@@ -135,7 +141,11 @@ __device__ __forceinline__ void cta_range(const GemvParams& p, int cta, int* gro
   *te = *tb + q + (local < rem ? 1 : 0);
 }
 
-template <int D, int R, int IDW, bool REPL, int MT, bool XS>
+// Activation modes: XM = 0 read from global memory per fragment (fallback),
+// 1 staged whole, 2 window ring.
+constexpr int kXBufs = 3;  // window ring depth
+
+template <int D, int R, int IDW, bool REPL, int MT, int XM>
 struct GemvCfg {
   using L = CbLayout<D, REPL>;
   // one CTA of 16 warps per SM shares one staged codebook
@@ -150,22 +160,28 @@ struct GemvCfg {
   // activations: M rows plus one zero row that lanes beyond M read; the row
   // stride is padded by 32 bytes so rows read together fall in different banks
   __host__ __device__ static int x_stride(int kpad) { return kpad * 2 + 32; }
-  __host__ __device__ static int x_bytes(int M, int kpad) {
-    return XS ? (((M + 1) * x_stride(kpad) + 127) / 128) * 128 : 0;
+  // window ring: kXBufs buffers of MC rows x wpt chunks (rows >= M stay zero)
+  __host__ __device__ static int xw_stride(int wpt) { return wpt * kChunkBlocks * D * 2 + 32; }
+  __host__ __device__ static int x_bytes(int M, int kpad, int wpt) {
+    if (XM == 1) return (((M + 1) * x_stride(kpad) + 127) / 128) * 128;
+    if (XM == 2) return ((kXBufs * MC * xw_stride(wpt) + 127) / 128) * 128;
+    return 0;
   }
   __host__ __device__ static int ring_bytes() { return kW * kRing * kStageBytes; }
   __host__ __device__ static int red_bytes() { return 2 * kW * 16 * MC * 4; }
-  __host__ __device__ static int smem(int entries, int M, int kpad) {
-    return cb_bytes(entries) + x_bytes(M, kpad) + ring_bytes() + red_bytes();
+  __host__ __device__ static int smem(int entries, int M, int kpad, int wpt) {
+    return cb_bytes(entries) + x_bytes(M, kpad, wpt) + ring_bytes() + red_bytes();
   }
 };
 
-template <int D, int R, int IDW, bool REPL, int MT, bool XS, bool MASK, bool SC>
-__device__ __forceinline__ void gemv_chunk(float (&acc)[GemvCfg<D, R, IDW, REPL, MT, XS>::kAcc][MT][4], const uint32_t (&c0)[R * IDW * 4],
+// col_base: the lane's first global column of the chunk (unstaged activations,
+// masking); xcol: the same column inside the staged buffer.
+template <int D, int R, int IDW, bool REPL, int MT, int XM, bool MASK, bool SC>
+__device__ __forceinline__ void gemv_chunk(float (&acc)[GemvCfg<D, R, IDW, REPL, MT, XM>::kAcc][MT][4], const uint32_t (&c0)[R * IDW * 4],
                                            const uint32_t (&c1)[R * IDW * 4], uint32_t cb, uint32_t cbl, uint32_t rho_a,
                                            uint32_t rho_b, const LaneSel& ls, const uint16_t* x, const uint32_t (&xoff)[MT],
-                                           const uint32_t (&xsa)[MT], const bool (&xv)[MT], int col_base, int K) {
-  using C = GemvCfg<D, R, IDW, REPL, MT, XS>;
+                                           const uint32_t (&xsa)[MT], const bool (&xv)[MT], int col_base, int xcol, int K) {
+  using C = GemvCfg<D, R, IDW, REPL, MT, XM>;
   static_for<0, D>([&](auto ktc) {
     constexpr int kt = decltype(ktc)::value;
     uint32_t ra[2], rb[2];
@@ -176,8 +192,8 @@ __device__ __forceinline__ void gemv_chunk(float (&acc)[GemvCfg<D, R, IDW, REPL,
     uint2 xf[MT];
 #pragma unroll
     for (int i = 0; i < MT; ++i) {
-      if (XS) {  // rows beyond M read the zero row: no predicate
-        xf[i] = lds64_ordered<kt * 32>(xsa[i] + col_base * 2);
+      if constexpr (XM != 0) {  // rows beyond M read zero rows: no predicate
+        xf[i] = lds64_ordered<kt * 32>(xsa[i] + xcol * 2);
       } else {
         xf[i] = make_uint2(0u, 0u);
         if (xv[i] && in_k) xf[i] = __ldg(reinterpret_cast<const uint2*>(x + xoff[i] + col));
@@ -194,10 +210,10 @@ __device__ __forceinline__ void gemv_chunk(float (&acc)[GemvCfg<D, R, IDW, REPL,
   });
 }
 
-template <int D, int R, int IDW, bool REPL, int MT, bool XS, bool SC>
-__global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
+template <int D, int R, int IDW, bool REPL, int MT, int XM, bool SC>
+__global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
     rvq_gemv_kernel(const __grid_constant__ GemvParams p) {
-  using C = GemvCfg<D, R, IDW, REPL, MT, XS>;
+  using C = GemvCfg<D, R, IDW, REPL, MT, XM>;
   constexpr int kWarps = C::kW;
   constexpr int kThreads = C::kT;
   using L = typename C::L;
@@ -207,7 +223,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
   const int kpad = p.chunks * kChunkBlocks * D;
   uint8_t* cb = smem;
   uint16_t* xs = reinterpret_cast<uint16_t*>(smem + C::cb_bytes(p.entries));
-  uint8_t* ring = smem + C::cb_bytes(p.entries) + C::x_bytes(p.M, kpad);
+  uint8_t* ring = smem + C::cb_bytes(p.entries) + C::x_bytes(p.M, kpad, p.wpt);
   float* red = reinterpret_cast<float*>(ring + C::ring_bytes());  // [2][kW][16][MC]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -242,7 +258,8 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
   // issue cursor: the next item's source (advanced incrementally), items left
   // to issue, position inside the tile's chunk list, ring slot
   constexpr int kLaneCopies = (C::kStageBytes + 511) / 512;  // 16-byte copies per lane per chunk
-  const bool copy_lane = lane * 16 < C::kStageBytes;
+  // copies of this lane inside the chunk (three stages: 768 bytes, lanes 16..31 make one copy)
+  const int lane_copies = (C::kStageBytes - lane * 16 + 511) / 512;
   // 64-bit base of this warp's first item plus a 32-bit running offset (the
   // host keeps a CTA's tile span below 2^31 bytes)
   const uint8_t* is_base = p.packed + (long long)(tb + slot) * tile_bytes + kpart * V * 256 + lane * 16;
@@ -255,13 +272,12 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
   int is_left = items;
   int is_j = 0;
   uint32_t is_slot = 0;
-  auto issue = [&]() {
+  auto issue_ids = [&]() {
     if (is_left > 0) {
-      if (copy_lane) {
 #pragma unroll
-        for (int k = 0; k < kLaneCopies; ++k)
+      for (int k = 0; k < kLaneCopies; ++k)
+        if (k < lane_copies)
           cp_async_16_hint(ring_lane + is_slot * C::kStageBytes + k * 512, is_base + is_off + k * 512, stream_pol);
-      }
       --is_left;
       is_off += step_chunk;
       if (++is_j == cpw) {
@@ -270,7 +286,46 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
       }
     }
     is_slot = (is_slot + 1) & (kRing - 1);
+  };
+  auto issue = [&]() {
+    issue_ids();
     cp_async_commit();
+  };
+
+  // window ring (XM == 2): window w of a round covers chunks [w * wpt, (w + 1) * wpt);
+  // step s reads buffer s % kXBufs and the copies for step s + 2 go out during step s
+  const int spr = (p.chunks + wpt - 1) >> wsh;  // steps per round, equal for every warp
+  const uint32_t xw_stride = (uint32_t)C::xw_stride(wpt);
+  const uint32_t xbuf_bytes = (uint32_t)MC * xw_stride;
+  const uint32_t xs_s = smem_u32(xs);
+  const bool x16 = (((uintptr_t)p.x & 15) == 0) && ((p.ldx & 7) == 0);
+  int xi_w = 0;       // window of the next copy
+  uint32_t xi_b = 0;  // its buffer
+  int xi_left = 0;    // windows left to copy
+  auto issue_x = [&](uint64_t pol) {
+    if (xi_left <= 0) return;
+    --xi_left;
+    const int col0 = xi_w * wpt * kChunkBlocks * D;
+    const uint32_t dst0 = xs_s + xi_b * xbuf_bytes;
+    constexpr int kVecShift = D == 8 ? 4 : (D == 16 ? 5 : 6);  // log2(16-byte vectors per chunk row)
+    const int vsh = wsh + kVecShift;
+    const int nvec = p.M << vsh;
+    for (int v = threadIdx.x; v < nvec; v += kThreads) {
+      const int m = v >> vsh, vec = v & ((1 << vsh) - 1);
+      const int col = col0 + vec * 8;
+      const int left = p.K - col;
+      const uint32_t nb = left >= 8 ? 16u : (left > 0 ? (uint32_t)left * 2u : 0u);
+      const uint16_t* src = nb ? p.x + (long long)m * p.ldx + col : p.x;
+      const uint32_t dst = dst0 + (uint32_t)m * xw_stride + (uint32_t)vec * 16;
+      if (x16) {
+        cp_async_16_zfill(dst, src, nb, pol);
+      } else {
+        cp_async_8_zfill(dst, src, nb > 8 ? 8u : nb);
+        cp_async_8_zfill(dst + 8, nb > 8 ? src + 4 : p.x, nb > 8 ? nb - 8 : 0u);
+      }
+    }
+    if (++xi_w == spr) xi_w = 0;
+    if (++xi_b == kXBufs) xi_b = 0;
   };
 
   // -- prologue: weights (static) first, activations after the dependency --
@@ -294,8 +349,21 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
     stage_codebooks_finish<D, R, REPL>(cb, p.entries, gscales);
   }
   if (p.pdl) grid_dependency_wait();  // x (and y) belong to the previous kernel in the stream
-  if (XS) {
-    const uint64_t x_pol = l2_policy_evict_last();
+  const uint64_t x_pol = l2_policy_evict_last();
+  if constexpr (XM == 2) {
+    // rows M..MC-1 of every buffer stay zero (the copies only write rows < M)
+    const int zw = (int)(xw_stride / 16), per_buf = (MC - p.M) * zw;
+    for (int v = threadIdx.x; v < kXBufs * per_buf; v += kThreads) {
+      const int b = v / per_buf, rem = v - b * per_buf;
+      const int m = p.M + rem / zw, w16 = rem - (m - p.M) * zw;
+      *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(xs) + (size_t)b * xbuf_bytes + (size_t)m * xw_stride +
+                                (size_t)w16 * 16) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    xi_left = rounds * spr;
+    issue_x(x_pol);  // steps 0 and 1
+    issue_x(x_pol);
+  }
+  if constexpr (XM == 1) {
     // rows m < M, columns [0, kpad): zero beyond K
     const int vec_per_row = kpad / 8;  // 16-byte vectors
     for (int m = 0; m <= p.M; ++m) {
@@ -329,20 +397,24 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
 
   // lane (r, q) feeds token 8 * i + r of n-tile i
   uint32_t xoff[MT];  // element offset of the lane's token row (unstaged activations)
-  uint32_t xsa[MT];   // shared address of the lane's token row (staged activations)
+  uint32_t xsa[MT];   // shared address of the lane's token row (staged activations; window: row offset)
   bool xv[MT];
 #pragma unroll
   for (int i = 0; i < MT; ++i) {
     const int m = 8 * i + r;
     xv[i] = m < p.M;
     xoff[i] = (uint32_t)((xv[i] ? m : 0) * p.ldx);
-    xsa[i] = smem_u32(xs) + (uint32_t)((xv[i] ? m : p.M) * C::x_stride(kpad));
+    if constexpr (XM == 2) {
+      xsa[i] = (uint32_t)m * xw_stride;  // rows >= M are zero rows
+    } else {
+      xsa[i] = smem_u32(xs) + (uint32_t)((xv[i] ? m : p.M) * C::x_stride(kpad));
+    }
   }
   // Columns K..kpad of the last chunk decode padding ids.  Staged activations
   // are zero there, so those products vanish (every decoded weight is finite
   // for finite codebooks and row scales); only unstaged activations need the
   // weight fragment masked.
-  const bool need_mask = !XS && kpad != p.K;
+  const bool need_mask = XM == 0 && kpad != p.K;
   const uint32_t cb_s = smem_u32(cb);
   const uint32_t cbl = cb_s + L::lane_offset(r, q);
 
@@ -361,6 +433,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
   }
 
   int it = 0;
+  uint32_t xs_buf = 0;  // window ring: buffer of the current step
   for (int k = 0; k < rounds; ++k) {
     const bool slot_live = k < my_rounds;  // same for all warps of a slot
     float acc[C::kAcc][MT][4];
@@ -369,15 +442,55 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
 #pragma unroll
       for (int i = 0; i < MT; ++i) acc[h][i][0] = acc[h][i][1] = acc[h][i][2] = acc[h][i][3] = 0.f;
     int row0 = 0, nrows = 0;
+    uint32_t rho_a = 0u, rho_b = 0u;
     if (slot_live) {
       tile_rows(tb + slot + k * slots, &row0, &nrows);
-      const uint32_t rho_a = nrho_a, rho_b = nrho_b;
+      rho_a = nrho_a;
+      rho_b = nrho_b;
       if (k + 1 < my_rounds) {  // prefetch the next round's row scales
         int nr0, nn;
         tile_rows(tb + slot + (k + 1) * slots, &nr0, &nn);
         nrho_a = r < nn ? rho_pair(p.row_scale[nr0 + r]) : 0u;
         nrho_b = r + 8 < nn ? rho_pair(p.row_scale[nr0 + r + 8]) : 0u;
       }
+    }
+    if constexpr (XM == 2) {
+      // every warp takes the round's spr steps together, live slot or not
+      for (int j = 0; j < spr; ++j) {
+        cp_async_wait<1>();  // this thread's copies for this step (window, ids) landed
+        __syncthreads();     // everyone's have; everyone is done with the previous step's buffer
+        issue_x(x_pol);      // the window of step + 2 into that buffer
+        const int c = kpart + j * wpt;
+        const bool valid = slot_live && c < p.chunks;
+        uint32_t c0[V * 4], c1[V * 4];
+        if (valid) {
+          const uint32_t st = ring_row + (uint32_t)(it & (kRing - 1)) * C::kStageBytes;
+#pragma unroll
+          for (int v = 0; v < V; ++v) {
+            asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(c0[4 * v]), "=r"(c0[4 * v + 1]), "=r"(c0[4 * v + 2]), "=r"(c0[4 * v + 3])
+                         : "r"(st + v * 256));
+            asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                         : "=r"(c1[4 * v]), "=r"(c1[4 * v + 1]), "=r"(c1[4 * v + 2]), "=r"(c1[4 * v + 3])
+                         : "r"(st + v * 256 + 128));
+          }
+          __syncwarp();
+          issue_ids();
+        }
+        cp_async_commit();  // one group per step and thread: the wait above counts on it
+        if (valid) {
+          const uint32_t xb = xs_s + xs_buf * xbuf_bytes;
+          uint32_t xsa_s[MT];
+#pragma unroll
+          for (int i = 0; i < MT; ++i) xsa_s[i] = xb + xsa[i];
+          gemv_chunk<D, R, IDW, REPL, MT, XM, false, SC>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, p.x, xoff, xsa_s,
+                                                     xv, c * kChunkBlocks * D + 4 * q,
+                                                     kpart * kChunkBlocks * D + 4 * q, p.K);
+          ++it;
+        }
+        if (++xs_buf == kXBufs) xs_buf = 0;
+      }
+    } else if (slot_live) {
       for (int j = 0; j < cpw; ++j, ++it) {
         cp_async_wait<kRing - 2>();
         __syncwarp();
@@ -398,11 +511,11 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
         const int c = kpart + j * wpt;
         const int col_base = c * kChunkBlocks * D + 4 * q;
         if (need_mask && c == p.chunks - 1) {
-          gemv_chunk<D, R, IDW, REPL, MT, XS, true, SC>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, p.x, xoff, xsa, xv,
-                                                    col_base, p.K);
+          gemv_chunk<D, R, IDW, REPL, MT, XM, true, SC>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, p.x, xoff, xsa, xv,
+                                                    col_base, col_base, p.K);
         } else {
-          gemv_chunk<D, R, IDW, REPL, MT, XS, false, SC>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, p.x, xoff, xsa, xv,
-                                                     col_base, p.K);
+          gemv_chunk<D, R, IDW, REPL, MT, XM, false, SC>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, p.x, xoff, xsa, xv,
+                                                     col_base, col_base, p.K);
         }
       }
     }
@@ -457,7 +570,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XS>::kT)
 template <int D, int R, int IDW, bool REPL, bool SC>
 __global__ void __launch_bounds__(kThreads) rvq_dequant_kernel(const __grid_constant__ GemvParams p, uint16_t* w,
                                                                long long ldw) {
-  using C = GemvCfg<D, R, IDW, REPL, 1, false>;
+  using C = GemvCfg<D, R, IDW, REPL, 1, 0>;
   using L = typename C::L;
   constexpr int V = C::V;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -621,12 +734,19 @@ int persistent_grid(Kern kern, int threads, int smem, int num_ctas, GemvParams& 
 
 using namespace wal;
 
-template <int D, int R, int IDW, bool REPL, int MT, bool XS, bool SC = false>
+template <int D, int R, int IDW, bool REPL, int MT, int XM, bool SC = false>
 static int run_gemv(GemvParams p, int num_ctas, cudaStream_t stream) {
-  using C = GemvCfg<D, R, IDW, REPL, MT, XS>;
-  auto kern = rvq_gemv_kernel<D, R, IDW, REPL, MT, XS, SC>;
+  using C = GemvCfg<D, R, IDW, REPL, MT, XM>;
+  auto kern = rvq_gemv_kernel<D, R, IDW, REPL, MT, XM, SC>;
   const int kpad = p.chunks * kChunkBlocks * D;
-  const int smem = C::smem(p.entries, p.M, kpad);
+  int smem = C::smem(p.entries, p.M, kpad, p.wpt);
+  if constexpr (XM == 2) {  // the window ring grows with wpt: fewer warps per tile until it fits
+    while (smem > 227 * 1024 && p.wpt > 1) {
+      p.wpt >>= 1;
+      p.wpt_shift -= 1;
+      smem = C::smem(p.entries, p.M, kpad, p.wpt);
+    }
+  }
   if (smem > 227 * 1024) return WAL_ERR_UNSUPPORTED;
   if (p.wpt > C::kW) return WAL_ERR_INVALID_ARGUMENT;
   int grid = 0;
@@ -654,7 +774,7 @@ static int run_gemv(GemvParams p, int num_ctas, cudaStream_t stream) {
 
 template <int D, int R, int IDW, bool REPL, bool SC = false>
 static int run_dequant(GemvParams p, uint16_t* w, long long ldw, cudaStream_t stream) {
-  using C = GemvCfg<D, R, IDW, REPL, 1, false>;
+  using C = GemvCfg<D, R, IDW, REPL, 1, 0>;
   auto kern = rvq_dequant_kernel<D, R, IDW, REPL, SC>;
   const int smem = C::cb_bytes(p.entries);
   if (smem > 227 * 1024) return WAL_ERR_UNSUPPORTED;
@@ -665,34 +785,35 @@ static int run_dequant(GemvParams p, uint16_t* w, long long ldw, cudaStream_t st
   return cudaGetLastError() == cudaSuccess ? WAL_OK : WAL_ERR_CUDA;
 }
 
-// mt: n-tiles of 8 tokens per launch (1, 2 or 4); xs: activations staged in
-// shared memory (never for 4 n-tiles: 32 rows of activations do not fit)
+// mt: n-tiles of 8 tokens per launch (1, 2 or 4); xm: activation mode
+// (1 staged whole, 2 window ring, 0 unstaged)
+template <int D, int R, int IDW, bool REPL, bool SC>
+static int run_mt(const GemvParams& p, int num_ctas, cudaStream_t stream, int mt, int xm) {
+  if (mt == 1)
+    return xm == 1 ? run_gemv<D, R, IDW, REPL, 1, 1, SC>(p, num_ctas, stream)
+                   : xm == 2 ? run_gemv<D, R, IDW, REPL, 1, 2, SC>(p, num_ctas, stream)
+                             : run_gemv<D, R, IDW, REPL, 1, 0, SC>(p, num_ctas, stream);
+  if (mt == 2)
+    return xm == 1 ? run_gemv<D, R, IDW, REPL, 2, 1, SC>(p, num_ctas, stream)
+                   : xm == 2 ? run_gemv<D, R, IDW, REPL, 2, 2, SC>(p, num_ctas, stream)
+                             : run_gemv<D, R, IDW, REPL, 2, 0, SC>(p, num_ctas, stream);
+  // 32 rows of whole activations never fit
+  return xm == 2 ? run_gemv<D, R, IDW, REPL, 4, 2, SC>(p, num_ctas, stream)
+                 : xm == 0 ? run_gemv<D, R, IDW, REPL, 4, 0, SC>(p, num_ctas, stream) : WAL_ERR_UNSUPPORTED;
+}
+
 template <int D, int R, int IDW>
-static int dispatch_gemv(const GemvParams& p, int num_ctas, cudaStream_t stream, bool repl, int mt, bool xs) {
+static int dispatch_gemv(const GemvParams& p, int num_ctas, cudaStream_t stream, bool repl, int mt, int xm) {
   if constexpr (IDW == 1 && R > 1) {
     if (p.stage_scales) {  // scaled multi-stage tables: fp32 replicated layout only
       if (!repl) return WAL_ERR_UNSUPPORTED;
-      if (mt == 1) return xs ? run_gemv<D, R, IDW, true, 1, true, true>(p, num_ctas, stream)
-                             : run_gemv<D, R, IDW, true, 1, false, true>(p, num_ctas, stream);
-      if (mt == 2) return xs ? run_gemv<D, R, IDW, true, 2, true, true>(p, num_ctas, stream)
-                             : run_gemv<D, R, IDW, true, 2, false, true>(p, num_ctas, stream);
-      return run_gemv<D, R, IDW, true, 4, false, true>(p, num_ctas, stream);
+      return run_mt<D, R, IDW, true, true>(p, num_ctas, stream, mt, xm);
     }
   }
   if constexpr (IDW == 1) {
-    if (repl) {
-      if (mt == 1) return xs ? run_gemv<D, R, IDW, true, 1, true>(p, num_ctas, stream)
-                             : run_gemv<D, R, IDW, true, 1, false>(p, num_ctas, stream);
-      if (mt == 2) return xs ? run_gemv<D, R, IDW, true, 2, true>(p, num_ctas, stream)
-                             : run_gemv<D, R, IDW, true, 2, false>(p, num_ctas, stream);
-      return run_gemv<D, R, IDW, true, 4, false>(p, num_ctas, stream);
-    }
+    if (repl) return run_mt<D, R, IDW, true, false>(p, num_ctas, stream, mt, xm);
   }
-  if (mt == 1) return xs ? run_gemv<D, R, IDW, false, 1, true>(p, num_ctas, stream)
-                         : run_gemv<D, R, IDW, false, 1, false>(p, num_ctas, stream);
-  if (mt == 2) return xs ? run_gemv<D, R, IDW, false, 2, true>(p, num_ctas, stream)
-                         : run_gemv<D, R, IDW, false, 2, false>(p, num_ctas, stream);
-  return run_gemv<D, R, IDW, false, 4, false>(p, num_ctas, stream);
+  return run_mt<D, R, IDW, false, false>(p, num_ctas, stream, mt, xm);
 }
 
 template <int D, int R, int IDW>
@@ -713,9 +834,9 @@ static int dispatch_dequant(const GemvParams& p, uint16_t* w, long long ldw, cud
 // translation unit (the build passes -DWAL_UNIT_D=8/16/32) so the kernel
 // instantiations build in parallel; the C entry points are in the unit built
 // with -DWAL_UNIT_API.
-int wal_gemv_dispatch_d8(const GemvParams&, int, cudaStream_t, int, int, bool, int, bool);
-int wal_gemv_dispatch_d16(const GemvParams&, int, cudaStream_t, int, int, bool, int, bool);
-int wal_gemv_dispatch_d32(const GemvParams&, int, cudaStream_t, int, int, bool, int, bool);
+int wal_gemv_dispatch_d8(const GemvParams&, int, cudaStream_t, int, int, bool, int, int);
+int wal_gemv_dispatch_d16(const GemvParams&, int, cudaStream_t, int, int, bool, int, int);
+int wal_gemv_dispatch_d32(const GemvParams&, int, cudaStream_t, int, int, bool, int, int);
 int wal_dequant_dispatch_d8(const GemvParams&, uint16_t*, long long, cudaStream_t, int, int, bool);
 int wal_dequant_dispatch_d16(const GemvParams&, uint16_t*, long long, cudaStream_t, int, int, bool);
 int wal_dequant_dispatch_d32(const GemvParams&, uint16_t*, long long, cudaStream_t, int, int, bool);
@@ -724,7 +845,7 @@ int wal_dequant_dispatch_d32(const GemvParams&, uint16_t*, long long, cudaStream
 #define WAL_CAT2(a, b) a##b
 #define WAL_CAT(a, b) WAL_CAT2(a, b)
 int WAL_CAT(wal_gemv_dispatch_d, WAL_UNIT_D)(const GemvParams& p, int num_ctas, cudaStream_t s, int R, int idw,
-                                             bool repl, int mt, bool xs) {
+                                             bool repl, int mt, int xs) {
   constexpr int D = WAL_UNIT_D;
   switch (R * 10 + idw) {
     case 11: return dispatch_gemv<D, 1, 1>(p, num_ctas, s, repl, mt, xs);
@@ -751,7 +872,7 @@ int WAL_CAT(wal_dequant_dispatch_d, WAL_UNIT_D)(const GemvParams& p, uint16_t* w
 
 #ifdef WAL_UNIT_API
 static int gemv_by_d(int d, const GemvParams& p, int num_ctas, cudaStream_t s, int R, int idw, bool repl, int mt,
-                     bool xs) {
+                     int xs) {
   if (d == 8) return wal_gemv_dispatch_d8(p, num_ctas, s, R, idw, repl, mt, xs);
   if (d == 16) return wal_gemv_dispatch_d16(p, num_ctas, s, R, idw, repl, mt, xs);
   if (d == 32) return wal_gemv_dispatch_d32(p, num_ctas, s, R, idw, repl, mt, xs);
@@ -853,8 +974,11 @@ static int gemv_common(const wal_rvq_layer* layer, const uint16_t* x, int64_t M,
   const size_t ysz = y_dtype == WAL_F32 ? 4 : 2;
   const int kpad = p.chunks * kChunkBlocks * d;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  for (int64_t m0 = 0; m0 < M; m0 += kMaxTokens) {
-    const int mm = (int)((M - m0) < kMaxTokens ? (M - m0) : kMaxTokens);
+  // slabs of up to 32 tokens; a slab whose n-tiles do not fit in shared memory
+  // (large multi-stage codebooks) runs as two slabs of half the tokens
+  int cap = kMaxTokens;
+  for (int64_t m0 = 0; m0 < M;) {
+    const int mm = (int)((M - m0) < cap ? (M - m0) : cap);
     p.x = x + m0 * ldx;
     if (push) {
       for (int r = 0; r < push->num_ranks; ++r) p.push_dst[r] = static_cast<uint2*>(push->dst[r]) + m0 * push->ld_dst;
@@ -863,11 +987,18 @@ static int gemv_common(const wal_rvq_layer* layer, const uint16_t* x, int64_t M,
     }
     p.M = mm;
     const int mt = mm <= 8 ? 1 : (mm <= 16 ? 2 : 4);
-    const bool xs = mt < 4 && (long long)mm * kpad * 2 <= kXSmemBudget;
-    int rs = gemv_by_d(d, p, num_ctas, s, R, idw, repl, mt, xs);
-    if (rs == WAL_ERR_UNSUPPORTED && xs)  // activations do not fit beside the codebook
-      rs = gemv_by_d(d, p, num_ctas, s, R, idw, repl, mt, false);
+    // whole activations when small, else the window ring, else (shared memory
+    // taken by a large codebook) unstaged reads
+    int xm = mt < 4 && (long long)mm * kpad * 2 <= kXSmemBudget ? 1 : 2;
+    int rs = gemv_by_d(d, p, num_ctas, s, R, idw, repl, mt, xm);
+    if (rs == WAL_ERR_UNSUPPORTED && xm == 1) rs = gemv_by_d(d, p, num_ctas, s, R, idw, repl, mt, xm = 2);
+    if (rs == WAL_ERR_UNSUPPORTED && xm == 2) rs = gemv_by_d(d, p, num_ctas, s, R, idw, repl, mt, 0);
+    if (rs == WAL_ERR_UNSUPPORTED && mt > 1) {
+      cap = mt == 4 ? 16 : 8;
+      continue;
+    }
     if (rs != WAL_OK) return rs;
+    m0 += mm;
   }
   return WAL_OK;
 }
