@@ -9,9 +9,11 @@
 //     `kpart` of a slot taking chunks kpart, kpart + wpt, ...;
 //   * activations: staged whole in shared memory when they fit; otherwise
 //     streamed through a three-deep window ring shared by the CTA: step j of a
-//     round needs the same wpt chunks' columns in every slot, so all warps step
-//     together (one CTA barrier per step) and each window of x is copied from
-//     L2 once per CTA instead of once per 16-row tile;
+//     round needs the same wpt chunks' columns in every slot, so four producer
+//     warps (warps 16..19) copy each window once per CTA instead of once per
+//     16-row tile, handing buffers to the 16 compute warps through hardware
+//     named barriers (full: producer arrives, compute warps wait; empty: the
+//     reverse), which lets compute warps drift up to two windows apart;
 //   * each warp walks its own flat list of (tile, chunk) items with a
 //     kRing-deep cp.async ring in shared memory, so id loads for later items
 //     are in flight while the current one is decoded (no spin-waits: the copy
@@ -54,6 +56,7 @@ struct GemvParams {
   int num_groups;
   int pdl;                               // launched with programmatic dependent launch
   int wpt_shift;                         // log2(wpt)
+  int auto_tpc;                          // tiles per CTA when wpt was chosen automatically, else 0
   int group_tile_start[kMaxGroups + 1];  // first tile of each group, plus the total
   int group_row_start[kMaxGroups + 1];   // first output row of each group, plus N
   // CTA split (host-computed for the launch's grid): group g owns CTAs
@@ -117,6 +120,9 @@ __device__ __forceinline__ void emit_out(const GemvParams& p, unsigned tag, int 
 __device__ __forceinline__ void named_barrier(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory");
 }
+__device__ __forceinline__ void named_barrier_arrive(int id, int nthreads) {
+  asm volatile("bar.arrive %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory");
+}
 
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 
@@ -144,13 +150,18 @@ __device__ __forceinline__ void cta_range(const GemvParams& p, int cta, int* gro
 // Activation modes: XM = 0 read from global memory per fragment (fallback),
 // 1 staged whole, 2 window ring.
 constexpr int kXBufs = 3;  // window ring depth
+// named barrier ids: 0 = __syncthreads, 1..8 = slot reductions (wpt >= 2),
+// window ring full / empty per buffer
+constexpr int kFullBar = 9;
+constexpr int kEmptyBar = kFullBar + kXBufs;
 
 template <int D, int R, int IDW, bool REPL, int MT, int XM>
 struct GemvCfg {
   using L = CbLayout<D, REPL>;
   // one CTA of 16 warps per SM shares one staged codebook
-  static constexpr int kW = 16;
-  static constexpr int kT = kW * 32;
+  static constexpr int kW = 16;                          // compute warps
+  static constexpr int kP = XM == 2 ? 4 : 0;              // window producer warps
+  static constexpr int kT = (kW + kP) * 32;
   static constexpr int V = R * IDW;               // 16-byte vectors per row-chunk
   static constexpr int NW = V * 4;                // 32-bit code words per row-chunk
   static constexpr int kStageBytes = V * 256;     // one chunk of one tile (16 rows)
@@ -168,7 +179,11 @@ struct GemvCfg {
     return 0;
   }
   __host__ __device__ static int ring_bytes() { return kW * kRing * kStageBytes; }
-  __host__ __device__ static int red_bytes() { return 2 * kW * 16 * MC * 4; }
+  // partial sums of a slot's warps: double-buffered by round parity, except
+  // with the window ring (whose smem is scarcer): one buffer and a second slot
+  // barrier after the reads
+  static constexpr int kRedBufs = XM == 2 ? 1 : 2;
+  __host__ __device__ static int red_bytes() { return kRedBufs * kW * 16 * MC * 4; }
   __host__ __device__ static int smem(int entries, int M, int kpad, int wpt) {
     return cb_bytes(entries) + x_bytes(M, kpad, wpt) + ring_bytes() + red_bytes();
   }
@@ -224,11 +239,12 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
   uint8_t* cb = smem;
   uint16_t* xs = reinterpret_cast<uint16_t*>(smem + C::cb_bytes(p.entries));
   uint8_t* ring = smem + C::cb_bytes(p.entries) + C::x_bytes(p.M, kpad, p.wpt);
-  float* red = reinterpret_cast<float*>(ring + C::ring_bytes());  // [2][kW][16][MC]
+  float* red = reinterpret_cast<float*>(ring + C::ring_bytes());  // [kRedBufs][kW][16][MC]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, q = lane & 3;
-  static_assert(kWarps == 16, "warp split assumes 16 warps");
+  static_assert(kWarps == 16, "warp split assumes 16 compute warps");
+  const bool producer = XM == 2 && warp >= kWarps;  // the window ring's copy warps
   const int wpt = p.wpt, wsh = p.wpt_shift;  // wpt = 1 << wsh
   const int ssh = 4 - wsh;                    // slots = 16 / wpt = 1 << ssh
   const int slots = 1 << ssh;
@@ -250,7 +266,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
   const int ntiles = te - tb;
   const int rounds = (ntiles + slots - 1) >> ssh;
   // tiles this warp owns: tb + slot + k * slots, k < my_rounds
-  const int my_rounds = slot < ntiles ? (ntiles - slot + slots - 1) >> ssh : 0;
+  const int my_rounds = !producer && slot < ntiles ? (ntiles - slot + slots - 1) >> ssh : 0;
   const int items = my_rounds * cpw;
   const long long tile_bytes = (long long)p.chunks * V * 256;
   uint8_t* wring = ring + warp * kRing * C::kStageBytes;
@@ -293,24 +309,21 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
   };
 
   // window ring (XM == 2): window w of a round covers chunks [w * wpt, (w + 1) * wpt);
-  // step s reads buffer s % kXBufs and the copies for step s + 2 go out during step s
+  // step s of the CTA reads buffer s % kXBufs
   const int spr = (p.chunks + wpt - 1) >> wsh;  // steps per round, equal for every warp
   const uint32_t xw_stride = (uint32_t)C::xw_stride(wpt);
   const uint32_t xbuf_bytes = (uint32_t)MC * xw_stride;
   const uint32_t xs_s = smem_u32(xs);
   const bool x16 = (((uintptr_t)p.x & 15) == 0) && ((p.ldx & 7) == 0);
-  int xi_w = 0;       // window of the next copy
-  uint32_t xi_b = 0;  // its buffer
-  int xi_left = 0;    // windows left to copy
-  auto issue_x = [&](uint64_t pol) {
-    if (xi_left <= 0) return;
-    --xi_left;
-    const int col0 = xi_w * wpt * kChunkBlocks * D;
-    const uint32_t dst0 = xs_s + xi_b * xbuf_bytes;
+  // copies of window w into buffer b by the producer warps' threads
+  auto copy_window = [&](int w, uint32_t b, uint64_t pol) {
+    constexpr int kPT = C::kP * 32;
+    const int col0 = w * wpt * kChunkBlocks * D;
+    const uint32_t dst0 = xs_s + b * xbuf_bytes;
     constexpr int kVecShift = D == 8 ? 4 : (D == 16 ? 5 : 6);  // log2(16-byte vectors per chunk row)
     const int vsh = wsh + kVecShift;
     const int nvec = p.M << vsh;
-    for (int v = threadIdx.x; v < nvec; v += kThreads) {
+    for (int v = (int)threadIdx.x - kWarps * 32; v < nvec; v += kPT) {
       const int m = v >> vsh, vec = v & ((1 << vsh) - 1);
       const int col = col0 + vec * 8;
       const int left = p.K - col;
@@ -324,8 +337,6 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
         cp_async_8_zfill(dst + 8, nb > 8 ? src + 4 : p.x, nb > 8 ? nb - 8 : 0u);
       }
     }
-    if (++xi_w == spr) xi_w = 0;
-    if (++xi_b == kXBufs) xi_b = 0;
   };
 
   // -- prologue: weights (static) first, activations after the dependency --
@@ -359,9 +370,6 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
       *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(xs) + (size_t)b * xbuf_bytes + (size_t)m * xw_stride +
                                 (size_t)w16 * 16) = make_uint4(0u, 0u, 0u, 0u);
     }
-    xi_left = rounds * spr;
-    issue_x(x_pol);  // steps 0 and 1
-    issue_x(x_pol);
   }
   if constexpr (XM == 1) {
     // rows m < M, columns [0, kpad): zero beyond K
@@ -432,6 +440,33 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
     nrho_b = r + 8 < nrows ? rho_pair(p.row_scale[row0 + r + 8]) : 0u;
   }
 
+  if constexpr (XM == 2) {
+    if (producer) {
+      // window s of the CTA (window s % spr of round s / spr) goes to buffer
+      // s % kXBufs once the compute warps are done with window s - kXBufs; the
+      // full barrier of window s - 1 is signalled when its copies have landed
+      const int T = rounds * spr;
+      int w = 0;
+      uint32_t b = 0;
+      for (int s = 0; s < T; ++s) {
+        if (s >= kXBufs) named_barrier(kEmptyBar + (int)b, kThreads);
+        copy_window(w, b, x_pol);
+        cp_async_commit();
+        if (s >= 1) {
+          cp_async_wait<1>();
+          named_barrier_arrive(kFullBar + (int)(b == 0 ? kXBufs - 1 : b - 1), kThreads);
+        }
+        if (++w == spr) w = 0;
+        if (++b == kXBufs) b = 0;
+      }
+      cp_async_wait<0>();
+      named_barrier_arrive(kFullBar + (int)(b == 0 ? kXBufs - 1 : b - 1), kThreads);
+      // complete the empty barriers of the last windows
+      for (int s = T > kXBufs ? T : kXBufs; s < T + kXBufs; ++s) named_barrier(kEmptyBar + s % kXBufs, kThreads);
+      return;
+    }
+  }
+
   int it = 0;
   uint32_t xs_buf = 0;  // window ring: buffer of the current step
   for (int k = 0; k < rounds; ++k) {
@@ -455,16 +490,15 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
       }
     }
     if constexpr (XM == 2) {
-      // every warp takes the round's spr steps together, live slot or not
+      // every compute warp takes the round's spr windows, live slot or not
       for (int j = 0; j < spr; ++j) {
-        cp_async_wait<1>();  // this thread's copies for this step (window, ids) landed
-        __syncthreads();     // everyone's have; everyone is done with the previous step's buffer
-        issue_x(x_pol);      // the window of step + 2 into that buffer
         const int c = kpart + j * wpt;
-        const bool valid = slot_live && c < p.chunks;
-        uint32_t c0[V * 4], c1[V * 4];
-        if (valid) {
+        named_barrier(kFullBar + (int)xs_buf, kThreads);  // this window's activations landed
+        if (slot_live && c < p.chunks) {
+          cp_async_wait<kRing - 2>();
+          __syncwarp();
           const uint32_t st = ring_row + (uint32_t)(it & (kRing - 1)) * C::kStageBytes;
+          uint32_t c0[V * 4], c1[V * 4];
 #pragma unroll
           for (int v = 0; v < V; ++v) {
             asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -475,10 +509,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
                          : "r"(st + v * 256 + 128));
           }
           __syncwarp();
-          issue_ids();
-        }
-        cp_async_commit();  // one group per step and thread: the wait above counts on it
-        if (valid) {
+          issue();
           const uint32_t xb = xs_s + xs_buf * xbuf_bytes;
           uint32_t xsa_s[MT];
 #pragma unroll
@@ -488,6 +519,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
                                                      kpart * kChunkBlocks * D + 4 * q, p.K);
           ++it;
         }
+        named_barrier_arrive(kEmptyBar + (int)xs_buf, kThreads);  // done with this buffer
         if (++xs_buf == kXBufs) xs_buf = 0;
       }
     } else if (slot_live) {
@@ -538,7 +570,8 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
       }
       continue;
     }
-    float* wred = red + ((int)(k & 1) * kWarps + warp) * 16 * MC;
+    const int rbuf = C::kRedBufs == 2 ? (k & 1) : 0;
+    float* wred = red + (rbuf * kWarps + warp) * 16 * MC;
 #pragma unroll
     for (int i = 0; i < MT; ++i) {
       float v4[4];
@@ -550,7 +583,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
       wred[(r + 8) * MC + i * 8 + 2 * q + 1] = v4[3];
     }
     named_barrier(1 + slot, wpt * 32);
-    const float* sred = red + ((int)(k & 1) * kWarps + slot * wpt) * 16 * MC;
+    const float* sred = red + (rbuf * kWarps + slot * wpt) * 16 * MC;
     const int tid = kpart * 32 + lane;
     for (int e = tid; e < 16 * MC; e += wpt * 32) {
       const int row = e / MC, m = e - row * MC;
@@ -561,6 +594,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
       if (p.bias) v += __bfloat162float(__ushort_as_bfloat16(p.bias[orow]));
       emit_out(p, tag, m, orow, v);
     }
+    if constexpr (C::kRedBufs == 1) named_barrier(1 + slot, wpt * 32);  // reads done before the next round's writes
   }
   cp_async_wait<0>();
 }
@@ -734,16 +768,38 @@ int persistent_grid(Kern kern, int threads, int smem, int num_ctas, GemvParams& 
 
 using namespace wal;
 
+// Warps per tile for a CTA with tpc tiles: rounds of 16/wpt tiles, each round
+// ceil(chunks/wpt) chunks, plus a small reduction cost per round growing with wpt.
+static int best_wpt(long long tpc, int chunks, int wmax) {
+  double best = 1e30;
+  int wpt = 1;
+  for (int w = 1; w <= wmax; w *= 2) {
+    const long long slots = 16 / w;
+    const long long rounds = (tpc + slots - 1) / slots;
+    const long long cpw = (chunks + w - 1) / w;
+    const double cost = (double)rounds * ((double)cpw + 0.25 * (w > 1 ? 1 + w / 4.0 : 0.0));
+    if (cost < best - 1e-9) {
+      best = cost;
+      wpt = w;
+    }
+  }
+  return wpt;
+}
+
+static int log2_pow2(int w) { return w == 1 ? 0 : w == 2 ? 1 : w == 4 ? 2 : w == 8 ? 3 : 4; }
+
 template <int D, int R, int IDW, bool REPL, int MT, int XM, bool SC = false>
 static int run_gemv(GemvParams p, int num_ctas, cudaStream_t stream) {
   using C = GemvCfg<D, R, IDW, REPL, MT, XM>;
   auto kern = rvq_gemv_kernel<D, R, IDW, REPL, MT, XM, SC>;
   const int kpad = p.chunks * kChunkBlocks * D;
   int smem = C::smem(p.entries, p.M, kpad, p.wpt);
-  if constexpr (XM == 2) {  // the window ring grows with wpt: fewer warps per tile until it fits
-    while (smem > 227 * 1024 && p.wpt > 1) {
-      p.wpt >>= 1;
-      p.wpt_shift -= 1;
+  if constexpr (XM == 2) {  // the window ring grows with wpt: choose among the splits that fit
+    int wmax = 16;
+    while (wmax > 1 && C::smem(p.entries, p.M, kpad, wmax) > 227 * 1024) wmax >>= 1;
+    if (p.wpt > wmax) {
+      p.wpt = p.auto_tpc > 0 ? best_wpt(p.auto_tpc, p.chunks, wmax) : wmax;
+      p.wpt_shift = log2_pow2(p.wpt);
       smem = C::smem(p.entries, p.M, kpad, p.wpt);
     }
   }
@@ -939,28 +995,18 @@ static int gemv_common(const wal_rvq_layer* layer, const uint16_t* x, int64_t M,
   st = make_params(layer, &p);
   if (st != WAL_OK) return st;
   int wpt = warps_per_tile;
+  p.auto_tpc = 0;
   if (wpt == 0) {
-    // per-warp work model: rounds of 16/wpt tiles, each round ceil(chunks/wpt)
-    // chunks, plus a small reduction cost per round that grows with wpt
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const long long grid = layer->num_tiles < sms ? layer->num_tiles : sms;
     const long long tpc = (layer->num_tiles + grid - 1) / grid;  // tiles per CTA (max)
-    double best = 1e30;
-    for (int w = 1; w <= 16; w *= 2) {
-      const long long slots = 16 / w;
-      const long long rounds = (tpc + slots - 1) / slots;
-      const long long cpw = (p.chunks + w - 1) / w;
-      const double cost = (double)rounds * ((double)cpw + 0.25 * (w > 1 ? 1 + w / 4.0 : 0.0));
-      if (cost < best - 1e-9) {
-        best = cost;
-        wpt = w;
-      }
-    }
+    wpt = best_wpt(tpc, p.chunks, 16);
+    p.auto_tpc = (int)tpc;
   }
   p.wpt = wpt;
-  p.wpt_shift = wpt == 1 ? 0 : wpt == 2 ? 1 : wpt == 4 ? 2 : wpt == 8 ? 3 : 4;
+  p.wpt_shift = log2_pow2(wpt);
   p.ldx = ldx;
   p.ldy = ldy;
   p.y_dtype = y_dtype;
