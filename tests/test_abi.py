@@ -178,3 +178,10 @@ def test_route_module_shape():
     inp = synthetic.route_inputs(40, 64, d=16, G=4, seed=15)
     mod = RouteCodebookLinear.from_routes(inp.route, inp.code, inp.codebooks, inp.row_scale, in_features=64)
     assert mod.num_entries == 1024 and mod.num_stages == 1 and mod.out_features == 40
+
+
+def test_profile_cases_cli_lists_its_cases():
+    from wal2026_b200 import profile_cases
+
+    assert set(profile_cases.CASES) == {"cfg1_gemv", "gemv_window", "idroute_mlp", "attention"}
+    assert profile_cases.main(["no_such_case"]) == 2

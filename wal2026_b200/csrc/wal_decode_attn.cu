@@ -4,17 +4,19 @@
 // of its output) in the decode step; no reference counterpart (the reference
 // runs Hugging Face attention).
 //
-// Split-K over positions: CTA (b, kv head, split) scores its position range
-// for all G = hq / hkv query heads that share the kv head.  The split's V rows
-// stream into shared memory (cp.async) while each thread scores one position
-// with its whole K row loaded at once (hd / 8 independent 16-byte loads), so
-// many rows are in flight per SM; the weighted sum of values then reads V from
-// shared memory.  Each CTA keeps (max, sum, un-normalised output) per head in
+// Split-K over positions: CTA (b, kv head, split) handles up to 128 positions
+// for all G = hq / hkv query heads that share the kv head.  The split's K and
+// V rows are copied to shared memory (cp.async, zero-filled past the end);
+// scores and the weighted values run on the tensor cores (mma.sync m16n8k16,
+// bf16 in, fp32 accumulate) with the G heads as the rows of the A tiles, each
+// warp owning 32 positions; the exp2 weights P are re-packed from the score
+// fragments into bf16 A fragments of the P.V product without leaving
+// registers.  Each CTA keeps (max, sum, un-normalised output) per head in
 // fp32 and writes them to a workspace slot.  The last CTA of each (b, kv head)
 // to finish (a counter in the workspace, returned to zero) merges the splits in
 // split order - deterministic - and writes the bf16 output row in the layout
 // the o-projection reads.  Softmax uses base-2 exponentials of scores
-// pre-multiplied by scale * log2(e).
+// multiplied by scale * log2(e).
 #include "../../include/wal_rvq.h"
 
 #include <cuda_bf16.h>
@@ -26,7 +28,7 @@
 namespace {
 
 constexpr int kThreads = 128;     // 4 warps
-constexpr int kMaxChunk = kThreads;  // positions per split: one K row per thread
+constexpr int kMaxChunk = kThreads;  // positions per split: 32 per warp
 constexpr int kTargetCtas = 148;   // one CTA per SM when the batch is small
 
 __device__ __forceinline__ float bf16f(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
@@ -46,159 +48,182 @@ struct AttnParams {
   unsigned* counter;  // [B * hkv]
 };
 
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t v;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(v) : "f"(hi), "f"(lo));
+  return v;
+}
+
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  // A rows 8..15 are zero (at most 8 query heads share a kv head)
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&m)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(m[0]), "=r"(m[1]), "=r"(m[2]), "=r"(m[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&m)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(m[0]), "=r"(m[1]), "=r"(m[2]), "=r"(m[3])
+               : "r"(addr));
+}
+
+// Tensor-core decode attention for one (sequence, kv head, split): the G query
+// heads are the rows of m16n8k16 tiles (rows >= G are zero), positions the
+// columns of the score tiles and the k dimension of the P.V tiles.  K and V
+// rows of the split are staged in shared memory with 16-byte piece c of row t
+// at piece c ^ (t & 7), so ldmatrix (K) and ldmatrix.trans (V) read eight rows
+// without bank conflicts.  Each warp owns 32 positions.
 template <int HD, int G>
 __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_constant__ AttnParams p) {
-  constexpr int E = HD / 32;   // head-dim elements per lane in the value pass
-  constexpr int P16 = HD / 8;  // 16-byte pieces per K/V row
+  constexpr int KT = HD / 16;   // k-tiles of the head dimension
+  constexpr int NT = HD / 8;    // n-tiles of the output
+  constexpr int P16 = HD / 8;   // 16-byte pieces per row
+  constexpr int PSH = HD == 128 ? 4 : 3;
   constexpr int NW = kThreads / 32;
-  // shared: q [G][HD] fp32 | scores [G][chunk] fp32 | V rows [chunk][HD] bf16 | warp outputs [NW][G][HD] fp32
-  //         | merge weights [nsplit][G] | merge sums [nsplit][G]
-  extern __shared__ __align__(16) float sm[];
-  __shared__ float red[NW][G];
-  __shared__ float stat[2][G];
+  constexpr int RB = HD * 2;    // row bytes
+  static_assert(NW * 32 == kMaxChunk, "one warp per 32 positions");
+  extern __shared__ __align__(128) uint8_t sm[];
+  __shared__ float red[NW][8];
+  __shared__ float stat[2][8];
   __shared__ int last;
   const int bh = blockIdx.x, split = blockIdx.y;
   const int b = bh / p.hkv, kvh = bh - b * p.hkv;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r = lane >> 2, qd = lane & 3;
   const int t0 = split * p.chunk;
   const int len = min(p.n - t0, p.chunk);  // >= 1: the plan leaves no empty split
-  float* qs = sm;
-  float* sc = qs + G * HD;
-  uint16_t* vs = reinterpret_cast<uint16_t*>(sc + G * p.chunk);
-  float* po = reinterpret_cast<float*>(vs + p.chunk * HD);
+  // shared: V rows | K rows, the K region reused after the scores for the
+  // warps' outputs [NW][G][HD] and the merge's split weights and sums
+  const uint32_t vs_s = (uint32_t)__cvta_generic_to_shared(sm);
+  const uint32_t ks_s = vs_s + kMaxChunk * RB;
+  float* po = reinterpret_cast<float*>(sm + kMaxChunk * RB);
   const uint16_t* kb = p.k + (((long long)b * p.hkv + kvh) * p.cache_len + t0) * HD;
   const uint16_t* vb = p.v + (((long long)b * p.hkv + kvh) * p.cache_len + t0) * HD;
 
   // the cache and q come from earlier kernels of the step
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
-  // this thread's K row: hd / 8 independent 16-byte loads in flight
-  uint4 kv[P16];
-  if (tid < len) {
-    const uint4* kr = reinterpret_cast<const uint4*>(kb + (long long)tid * HD);
-#pragma unroll
-    for (int j = 0; j < P16; ++j) kv[j] = __ldg(kr + j);
+  // K and V rows -> shared memory (rows >= len zero-filled)
+  for (int i = tid; i < kMaxChunk * P16; i += kThreads) {
+    const int t = i >> PSH, c = i & (P16 - 1);
+    const uint32_t off = (uint32_t)(t * RB + ((c ^ (t & 7)) << 4));
+    const bool in = t < len;
+    const uint32_t nb = in ? 16u : 0u;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(ks_s + off),
+                 "l"(in ? kb + (long long)t * HD + c * 8 : kb), "r"(nb));
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(vs_s + off),
+                 "l"(in ? vb + (long long)t * HD + c * 8 : vb), "r"(nb));
   }
-  // V rows of this split -> shared memory
-  const uint32_t vs_s = (uint32_t)__cvta_generic_to_shared(vs);
-  for (int i = tid; i < len * P16; i += kThreads)
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(vs_s + i * 16), "l"(vb + (long long)i * 8));
   asm volatile("cp.async.commit_group;\n" ::: "memory");
-  // the G query heads, pre-scaled
-  for (int i = tid; i < G * HD; i += kThreads)
-    qs[i] = bf16f(p.q[(long long)b * p.ld_q + (long long)kvh * G * HD + i]) * p.qscale;
-  __syncthreads();
-
-  // scores of this thread's position for the G heads
-  float m_part[G];
-  if (tid < len) {
-    float s[G];
+  // q fragments (A rows = heads): dims kt*16 + 2*qd (+1) and + 8
+  uint32_t qa[KT][2];
+  const uint16_t* qrow = p.q + (long long)b * p.ld_q + (long long)(kvh * G + (r < G ? r : 0)) * HD;
 #pragma unroll
-    for (int g = 0; g < G; ++g) s[g] = 0.f;
-#pragma unroll
-    for (int j = 0; j < P16; ++j) {
-      const uint32_t w[4] = {kv[j].x, kv[j].y, kv[j].z, kv[j].w};
-#pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float4 qa = *reinterpret_cast<const float4*>(qs + g * HD + j * 8);
-        const float4 qb = *reinterpret_cast<const float4*>(qs + g * HD + j * 8 + 4);
-        s[g] = fmaf(qa.x, __uint_as_float(w[0] << 16), s[g]);
-        s[g] = fmaf(qa.y, __uint_as_float(w[0] & 0xFFFF0000u), s[g]);
-        s[g] = fmaf(qa.z, __uint_as_float(w[1] << 16), s[g]);
-        s[g] = fmaf(qa.w, __uint_as_float(w[1] & 0xFFFF0000u), s[g]);
-        s[g] = fmaf(qb.x, __uint_as_float(w[2] << 16), s[g]);
-        s[g] = fmaf(qb.y, __uint_as_float(w[2] & 0xFFFF0000u), s[g]);
-        s[g] = fmaf(qb.z, __uint_as_float(w[3] << 16), s[g]);
-        s[g] = fmaf(qb.w, __uint_as_float(w[3] & 0xFFFF0000u), s[g]);
-      }
-    }
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      sc[g * p.chunk + tid] = s[g];
-      m_part[g] = s[g];
-    }
-  } else {
-#pragma unroll
-    for (int g = 0; g < G; ++g) m_part[g] = -INFINITY;
-  }
-  // split max per head
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float m = m_part[g];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) red[warp][g] = m;
-  }
-  __syncthreads();
-  float e_part[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float m = red[0][g];
-#pragma unroll
-    for (int w = 1; w < NW; ++w) m = fmaxf(m, red[w][g]);
-    if (tid == 0) stat[0][g] = m;
-    e_part[g] = 0.f;
-    if (tid < len) {
-      e_part[g] = exp2f(sc[g * p.chunk + tid] - m);
-      sc[g * p.chunk + tid] = e_part[g];
-    }
-  }
-  __syncthreads();  // red is reused below
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float l = e_part[g];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    if (lane == 0) red[warp][g] = l;
+  for (int kt = 0; kt < KT; ++kt) {
+    qa[kt][0] = r < G ? *reinterpret_cast<const uint32_t*>(qrow + kt * 16 + 2 * qd) : 0u;
+    qa[kt][1] = r < G ? *reinterpret_cast<const uint32_t*>(qrow + kt * 16 + 8 + 2 * qd) : 0u;
   }
   asm volatile("cp.async.wait_all;\n" ::: "memory");
   __syncthreads();
-  // weighted values from shared memory: warps own positions, lanes own E columns
-  float acc[G][E];
+
+  // scores of the warp's 32 positions (4 n-tiles of 8): lane holds head r, positions 2qd, 2qd + 1
+  const int wp0 = warp * 32;
+  float s[4][4];
 #pragma unroll
-  for (int g = 0; g < G; ++g)
+  for (int nt = 0; nt < 4; ++nt) {
+    s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+    const int row = wp0 + nt * 8 + (lane & 7);  // the row this lane addresses for ldmatrix
 #pragma unroll
-    for (int e = 0; e < E; ++e) acc[g][e] = 0.f;
-  for (int t = warp; t < len; t += NW) {
-    float vv[E];
-    const uint16_t* vr = vs + t * HD + lane * E;
-    if constexpr (E == 4) {
-      const uint2 raw = *reinterpret_cast<const uint2*>(vr);
-      vv[0] = __uint_as_float(raw.x << 16); vv[1] = __uint_as_float(raw.x & 0xFFFF0000u);
-      vv[2] = __uint_as_float(raw.y << 16); vv[3] = __uint_as_float(raw.y & 0xFFFF0000u);
-    } else {
-      const uint32_t raw = *reinterpret_cast<const uint32_t*>(vr);
-      vv[0] = __uint_as_float(raw << 16); vv[1] = __uint_as_float(raw & 0xFFFF0000u);
-    }
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float pg = sc[g * p.chunk + t];
-#pragma unroll
-      for (int e = 0; e < E; ++e) acc[g][e] = fmaf(pg, vv[e], acc[g][e]);
+    for (int kt = 0; kt < KT; kt += 2) {
+      uint32_t m[4];
+      const int c = 2 * kt + (lane >> 3);
+      ldsm_x4(ks_s + row * RB + ((c ^ (row & 7)) << 4), m);
+      mma16816(s[nt], qa[kt][0], qa[kt][1], m[0], m[1]);
+      mma16816(s[nt], qa[kt + 1][0], qa[kt + 1][1], m[2], m[3]);
     }
   }
+  // scale, mask, split max per head
+  float mx = -INFINITY;
 #pragma unroll
-  for (int g = 0; g < G; ++g)
+  for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-    for (int e = 0; e < E; ++e) po[(warp * G + g) * HD + lane * E + e] = acc[g][e];
+    for (int e = 0; e < 2; ++e) {
+      const int t = wp0 + nt * 8 + 2 * qd + e;
+      s[nt][e] = t < len ? s[nt][e] * p.qscale : -INFINITY;
+      mx = fmaxf(mx, s[nt][e]);
+    }
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+  if (qd == 0 && r < G) red[warp][r] = mx;
+  __syncthreads();
+  if (tid < G) {
+    float m = red[0][tid];
+#pragma unroll
+    for (int w = 1; w < NW; ++w) m = fmaxf(m, red[w][tid]);
+    stat[0][tid] = m;
+  }
+  __syncthreads();
+  const float M = r < G ? stat[0][r] : 0.f;
+  float l = 0.f;
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      s[nt][e] = exp2f(s[nt][e] - M);  // masked positions: exp2(-inf) = 0
+      l += s[nt][e];
+    }
+  l += __shfl_xor_sync(0xffffffffu, l, 1);
+  l += __shfl_xor_sync(0xffffffffu, l, 2);
+  __syncthreads();  // red is reused
+  if (qd == 0 && r < G) red[warp][r] = l;
+
+  // P.V: the warp's 32 positions are two k-tiles; P re-packed as bf16 A fragments
+  float o[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+#pragma unroll
+  for (int kk = 0; kk < 2; ++kk) {
+    const uint32_t a0 = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
+    const uint32_t a2 = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+    const int row = wp0 + kk * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+#pragma unroll
+    for (int np = 0; np < NT / 2; ++np) {
+      uint32_t m[4];
+      const int c = 2 * np + (lane >> 4);
+      ldsm_x4_t(vs_s + row * RB + ((c ^ (row & 7)) << 4), m);
+      mma16816(o[2 * np], a0, a2, m[0], m[1]);
+      mma16816(o[2 * np + 1], a0, a2, m[2], m[3]);
+    }
+  }
+  if (r < G) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+      *reinterpret_cast<float2*>(po + (warp * G + r) * HD + nt * 8 + 2 * qd) = make_float2(o[nt][0], o[nt][1]);
+  }
   __syncthreads();
   // this split's slot: the warps' outputs summed in warp order, then (max, sum)
   const long long slot = (long long)bh * p.nsplit + split;
   float4* dst = reinterpret_cast<float4*>(p.part + slot * G * HD);
   for (int i = tid; i < G * HD / 4; i += kThreads) {
-    float4 a = reinterpret_cast<const float4*>(po)[i];
+    float4 acc = reinterpret_cast<const float4*>(po)[i];
 #pragma unroll
     for (int w = 1; w < NW; ++w) {
       const float4 c = reinterpret_cast<const float4*>(po + w * G * HD)[i];
-      a.x += c.x; a.y += c.y; a.z += c.z; a.w += c.w;
+      acc.x += c.x; acc.y += c.y; acc.z += c.z; acc.w += c.w;
     }
-    dst[i] = a;
+    dst[i] = acc;
   }
   if (tid < G) {
-    float l = red[0][tid];
+    float ls = red[0][tid];
 #pragma unroll
-    for (int w = 1; w < NW; ++w) l += red[w][tid];
-    p.stats[slot * G + tid] = make_float2(stat[0][tid], l);
+    for (int w = 1; w < NW; ++w) ls += red[w][tid];
+    p.stats[slot * G + tid] = make_float2(stat[0][tid], ls);
   }
   // the last split of this (b, kv head) to finish merges
   __threadfence();
@@ -288,7 +313,8 @@ size_t stats_bytes(long long B, int hkv, int nsplit, int G) {
 template <int HD, int G>
 int launch(const AttnParams& p, long long B, void* stream) {
   auto kern = decode_attn_kernel<HD, G>;
-  const int smem = (G * HD + G * p.chunk + 4 * G * HD + 2 * G * p.nsplit) * 4 + p.chunk * HD * 2;
+  const int k_region = kMaxChunk * HD * 2, out_region = (4 * G * HD + 2 * G * p.nsplit) * 4;
+  const int smem = kMaxChunk * HD * 2 + (k_region > out_region ? k_region : out_region);
   if (smem > 48 * 1024 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return WAL_ERR_CUDA;
   cudaLaunchConfig_t cfg = {};
