@@ -31,8 +31,6 @@ constexpr int kThreads = 128;     // 4 warps
 constexpr int kMaxChunk = kThreads;  // positions per split: 32 per warp
 constexpr int kTargetCtas = 148;   // one CTA per SM when the batch is small
 
-__device__ __forceinline__ float bf16f(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
-
 struct AttnParams {
   const uint16_t* q;
   long long ld_q;
