@@ -316,18 +316,24 @@ WAL_API int wal_decode_attention(const uint16_t* q, int64_t ld_q, const uint16_t
                          void* workspace, size_t workspace_bytes, void* stream);
 
 /*
- * wal_decode_attention without a caller-provided workspace and without any
- * allocation: scratch is a file-scope device array of 4 MiB per device
- * (merge counters in a fixed 16 KiB region at its front, zero from module
- * load and returned to zero by every call; partial outputs and stats after
- * them).  Returns WAL_ERR_BUFFER_TOO_SMALL when B * hkv > 4096 or the
- * partials need more than the remaining 4 MiB - 16 KiB (the bytes
- * wal_decode_attention_workspace reports minus B * hkv * 4, rounded to 256).
- * The first call on each device looks up the array's address
- * (cudaGetSymbolAddress) and must come before any stream capture that
- * records a later call.  All calls on one device share the array: calls that
- * overlap in time (other streams, other host threads) race.  Results are
- * bit-identical to wal_decode_attention.  No reference counterpart.
+ * Decode attention that allocates nothing, for callers that cannot call
+ * cudaMalloc: a plugin run by a host engine that owns all device memory and
+ * hands it inputs and outputs but no workspace, or a serving loop that must
+ * not stall on the device-wide synchronisation a cudaMalloc/cudaFree pair
+ * brings.  Arguments and results (bit-identical) are those of
+ * wal_decode_attention without the workspace: the scratch is a 4 MiB array
+ * compiled into this library, which every GPU that loads the library keeps
+ * until the process exits.  Limit: B * hkv <= 4096 and the split partials
+ * within 4 MiB - 16 KiB (the bytes wal_decode_attention_workspace reports
+ * minus B * hkv * 4, rounded up to 256; Llama-3-8B heads at 2048 positions
+ * fit up to batch 15); larger calls return WAL_ERR_BUFFER_TOO_SMALL and
+ * launch nothing.  Each call clears the merge counters it uses with an
+ * asynchronous memset on the stream before its kernel.  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress, that
+ * device current); make that first call before any stream capture.  Every
+ * call on a device uses the same array, so calls that can overlap on the GPU
+ * (other streams, other host threads) race and corrupt each other's results.
+ * No counterpart in the reference.
  */
 WAL_API int wal_decode_attention_static(const uint16_t* q, int64_t ld_q, const uint16_t* k_cache,
                          const uint16_t* v_cache, int64_t B, int32_t hq, int32_t hkv, int32_t hd,

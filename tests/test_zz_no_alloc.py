@@ -1,7 +1,13 @@
-"""wal_decode_attention_static (scratch in a static device array, no allocation) against
-wal_decode_attention with a caller workspace: same bits, on consecutive calls of different shapes.
+"""The allocation-free decode attention entry point against the workspace one.
 
-Collected last so that it also runs after every other test in the process has used the GPU.
+wal_decode_attention_static serves callers that cannot call cudaMalloc (an
+engine plugin given no workspace, a serving loop that must not stall on the
+synchronisation an allocation brings): its scratch is an array compiled into
+the library.  Through the C ABI it must give the same bits as
+wal_decode_attention on consecutive calls whose shapes change (so each call
+finds the array as the previous one left it), and refuse shapes beyond the
+array.  The file sorts last so a run that stops at the first failure has run
+every other test; it also passes alone in a fresh process.
 """
 from __future__ import annotations
 

@@ -293,9 +293,12 @@ void plan(long long B, int hkv, long long n, int* nsplit, int* chunk) {
   *chunk = (int)c;
 }
 
-// Scratch of wal_decode_attention_static, zero-filled at module load: the
-// merge counters occupy a fixed region at the front (so they are zero for any
-// shape, each call returning them to zero), partial outputs and stats follow.
+// Scratch of wal_decode_attention_static, for callers that cannot allocate
+// device memory: 4 MiB that every GPU loading this library keeps until the
+// process exits.  The merge counters occupy a fixed region at the front (each
+// call clears the ones it uses); partial outputs and stats follow.  Host code
+// must not pass this name to a kernel: it reaches the device address through
+// cudaGetSymbolAddress, once per device.
 constexpr size_t kStaticScratchBytes = 4u << 20;  // 4 MiB
 constexpr size_t kStaticCounters = 4096;         // max B * hkv
 constexpr size_t kStaticDataOffset = kStaticCounters * sizeof(unsigned);
@@ -439,6 +442,11 @@ int wal_decode_attention_static(const uint16_t* q, int64_t ld_q, const uint16_t*
   p.counter = reinterpret_cast<unsigned*>(ws);
   p.part = reinterpret_cast<float*>(ws + kStaticDataOffset);
   p.stats = reinterpret_cast<float2*>(ws + kStaticDataOffset + part_bytes(B, hkv, p.nsplit, G, hd));
+  // the array keeps whatever the last call left: clear the counters this call
+  // uses (the partials and stats are written before they are read)
+  if (cudaMemsetAsync(p.counter, 0, (size_t)B * hkv * sizeof(unsigned), static_cast<cudaStream_t>(stream)) !=
+      cudaSuccess)
+    return WAL_ERR_CUDA;
   return run(p, B, stream);
 }
 
