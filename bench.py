@@ -56,9 +56,10 @@ N_OUT, K_IN, D, G = 14336, 4096, 16, 16
 METRIC = "RVQ gather-GEMV GB/s (% of 8 TB/s HBM); 8B decode tok/s at 1/2/4/8 B200"
 UNIT = "GB/s"
 NOMINAL_HBM_GBS = 8000.0
-# DRAM bytes per launch of rvq_gemv_kernel on this workload (one cfg1 instance, M = 1), from the
-# ncu capture summarised in profiles/rvq_gemv_cfg1_m1.md: dram__bytes_read.sum + dram__bytes_write.sum.
-NCU_TRAFFIC_BYTES = 7553536
+# DRAM bytes per launch of rvq_gemv_kernel on this workload (one cfg1 instance, M = 1):
+# dram__bytes_read.sum + dram__bytes_write.sum from an ncu capture of
+# `python -m wal2026_b200.profile_cases cfg1_gemv`.
+NCU_TRAFFIC_BYTES = 7534336
 
 
 def algorithmic_bytes(M: int) -> int:
