@@ -107,18 +107,21 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   // the cache and q come from earlier kernels of the step
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
-  // K and V rows -> shared memory (rows >= len zero-filled)
-  for (int i = tid; i < kMaxChunk * P16; i += kThreads) {
-    const int t = i >> PSH, c = i & (P16 - 1);
-    const uint32_t off = (uint32_t)(t * RB + ((c ^ (t & 7)) << 4));
-    const bool in = t < len;
-    const uint32_t nb = in ? 16u : 0u;
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(ks_s + off),
-                 "l"(in ? kb + (long long)t * HD + c * 8 : kb), "r"(nb));
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(vs_s + off),
-                 "l"(in ? vb + (long long)t * HD + c * 8 : vb), "r"(nb));
+  // K rows, then V rows -> shared memory (rows >= len zero-filled), as two
+  // copy groups: the scores and the softmax need only K, so they overlap V
+#pragma unroll
+  for (int kv = 0; kv < 2; ++kv) {
+    const uint32_t base = kv == 0 ? ks_s : vs_s;
+    const uint16_t* src = kv == 0 ? kb : vb;
+    for (int i = tid; i < kMaxChunk * P16; i += kThreads) {
+      const int t = i >> PSH, c = i & (P16 - 1);
+      const uint32_t off = (uint32_t)(t * RB + ((c ^ (t & 7)) << 4));
+      const bool in = t < len;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(base + off),
+                   "l"(in ? src + (long long)t * HD + c * 8 : src), "r"(in ? 16u : 0u));
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
   }
-  asm volatile("cp.async.commit_group;\n" ::: "memory");
   // q fragments (A rows = heads): dims kt*16 + 2*qd (+1) and + 8
   uint32_t qa[KT][2];
   const uint16_t* qrow = p.q + (long long)b * p.ld_q + (long long)(kvh * G + (r < G ? r : 0)) * HD;
@@ -127,7 +130,7 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     qa[kt][0] = r < G ? *reinterpret_cast<const uint32_t*>(qrow + kt * 16 + 2 * qd) : 0u;
     qa[kt][1] = r < G ? *reinterpret_cast<const uint32_t*>(qrow + kt * 16 + 8 + 2 * qd) : 0u;
   }
-  asm volatile("cp.async.wait_all;\n" ::: "memory");
+  asm volatile("cp.async.wait_group 1;\n" ::: "memory");  // K landed
   __syncthreads();
 
   // scores of the warp's 32 positions (4 n-tiles of 8): lane holds head r, positions 2qd, 2qd + 1
@@ -178,7 +181,8 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
     }
   l += __shfl_xor_sync(0xffffffffu, l, 1);
   l += __shfl_xor_sync(0xffffffffu, l, 2);
-  __syncthreads();  // red is reused
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");  // V landed
+  __syncthreads();  // red is reused; V visible to every warp
   if (qd == 0 && r < G) red[warp][r] = l;
 
   // P.V: the warp's 32 positions are two k-tiles; P re-packed as bf16 A fragments
