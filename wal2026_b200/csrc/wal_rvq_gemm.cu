@@ -2,7 +2,8 @@
 // tcgen05.mma (5th-generation tensor cores, fp32 accumulators in TMEM).
 //
 // One CTA computes a 512 (tokens) x 128 (output rows) tile of y over all of K
-// in stages of 64 columns, with warp specialisation:
+// in stages of 64 columns (a CTA whose tokens end early loads and multiplies
+// only the 128-token tiles that hold tokens), with warp specialisation:
 //   warp 0      TMA producer: the activation tile [512 x 64] bf16 per stage
 //               (two 256-row boxes), cp.async.bulk.tensor into a
 //               128-byte-swizzled K-major buffer (no multicast), completion
@@ -12,10 +13,11 @@
 //               each decoded weight tile) into four TMEM accumulators and
 //               commits to empty[stage] (the stage's buffers are free again)
 //               and, after the last stage, to acc_full;
-//   warps 2..9  decoders: for every stage decode the 128 x 64 weight tile
+//   warps 2..17 decoders: for every stage decode the 128 x 64 weight tile
 //               exactly (same arithmetic as the decode GEMV: fp32 stage sum,
-//               two bf16 roundings; two threads per row, ids prefetched two
-//               stages ahead) straight into the swizzled K-major B buffer,
+//               two bf16 roundings; four threads per row, two blocks each,
+//               ids prefetched two stages ahead) straight into the swizzled
+//               K-major B buffer,
 //               fence it for the async proxy and arrive on full_b; then the
 //               epilogue: TMEM -> registers (tcgen05.ld 32x32b), bias,
 //               bf16/fp32 store of y.
@@ -41,7 +43,9 @@ constexpr int kBN = 128;   // output rows per CTA (MMA N)
 constexpr int kBK = 64;
 constexpr int kStages = 2;
 constexpr int kTmaRows = 256;  // TMA box height: two boxes per activation stage
-constexpr int kDecodeWarps = 8;
+constexpr int kDecodeWarps = 16;
+constexpr int kRowParts = kDecodeWarps * 32 / 128;  // decoder threads per weight row
+constexpr int kPartBlocks = 8 / kRowParts;          // d = 8 blocks per thread per 64-column stage
 constexpr int kThreads = (2 + kDecodeWarps) * 32;
 constexpr int kABytes = kBM * kBK * 2;  // 64 KB
 constexpr int kBBytes = kBN * kBK * 2;  // 16 KB
@@ -152,14 +156,14 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Decode the weights of one output row for half of a 64-column stage (blocks
-// u0 .. u0+3 of the stage, d = 8) and store them, 16 bytes per block, into the
-// swizzled B buffer.  ids[st] holds the four 1-byte ids of those blocks.
+// Decode the weights of one output row for blocks u0 .. u0 + kPartBlocks - 1
+// of a 64-column stage (d = 8) and store them, 16 bytes per block, into the
+// swizzled B buffer.  ids[st] holds the 1-byte ids of those blocks.
 template <int R>
-__device__ __forceinline__ void decode_stage_half(uint32_t bsm_row, int nsw, const uint32_t (&ids)[R], int u0,
+__device__ __forceinline__ void decode_stage_part(uint32_t bsm_row, int nsw, const uint32_t (&ids)[R], int u0,
                                                   uint32_t cb_lane, uint32_t rho2, int k_left) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
+  for (int j = 0; j < kPartBlocks; ++j) {
     const int u = u0 + j;
     uint4 o = make_uint4(0u, 0u, 0u, 0u);
     if (u * 8 < k_left) {
@@ -222,6 +226,10 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_kernel(const __grid_cons
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * kBM;
   const int n0 = blockIdx.y * kBN;
+  // 128-token MMA tiles holding real tokens (the last CTA of a small M needs
+  // fewer than four) and the 256-row activation boxes they read
+  const int mtiles = min(kBM / kUM, (p.M - m0 + kUM - 1) / kUM);
+  const int boxes = (mtiles * kUM + kTmaRows - 1) / kTmaRows;
   const int kblocks = (p.K + kBK - 1) / kBK;
 
   // row group of this N tile (the host guarantees a tile never straddles groups)
@@ -279,9 +287,8 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_kernel(const __grid_cons
           break;
         }
         if (abort_flag) break;
-        mbar_expect_tx(full_a + 8 * s, kABytes);
-#pragma unroll
-        for (int h = 0; h < kBM / kTmaRows; ++h)
+        mbar_expect_tx(full_a + 8 * s, boxes * (kTmaRows * 128));
+        for (int h = 0; h < boxes; ++h)
           tma_load_2d(a_sm + s * kABytes + h * (kTmaRows * 128), &xmap, kb * kBK, m0 + h * kTmaRows, full_a + 8 * s);
         ++issued;
       }
@@ -305,6 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_kernel(const __grid_cons
           const uint64_t bd = smem_desc_sw128(b_sm + s * kBBytes + ks * 32);
 #pragma unroll
           for (int mt = 0; mt < kBM / kUM; ++mt) {
+            if (mt >= mtiles) break;
             const uint64_t ad = smem_desc_sw128(a_sm + s * kABytes + mt * (kUM * 128) + ks * 32);
             umma_bf16(tmem + (uint32_t)(mt * kBN), ad, bd, (kb > 0 || ks > 0) ? 1u : 0u);
           }
@@ -315,8 +323,8 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_kernel(const __grid_cons
     }
   } else {
     // ---------------- decoders, then epilogue -----------------------------
-    const int t = threadIdx.x - 64;  // 0..255: row t & 127 of the tile, column half t >> 7 of each stage
-    const int row = t & (kBN - 1), half = t >> 7;
+    const int t = threadIdx.x - 64;  // row t & 127 of the tile, blocks part * kPartBlocks.. of each stage
+    const int row = t & (kBN - 1), part = t >> 7;
     const int n = n0 + row;
     const bool row_ok = n < g_row1;
     const uint32_t rho2 = row_ok ? rho_pair(p.row_scale[n]) : 0u;
@@ -324,18 +332,22 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_kernel(const __grid_cons
     const long long tile = (long long)g_tile0 + local / 16;
     const int rr = local % 16;
     const long long tile_bytes = (long long)p.chunks * R * 256;
-    const uint8_t* idrow = p.packed + tile * tile_bytes + rr * 16 + half * 4;
+    const uint8_t* idrow = p.packed + tile * tile_bytes + rr * 16 + part * kPartBlocks;
     const uint32_t bsm_row0 = b_sm + (row >> 3) * 1024 + (row & 7) * 128;
     const uint32_t cb_lane = cb_sm + (uint32_t)(lane & 7) * 16;
     const int nsw = row & 7;
     // stage kb covers blocks 8kb..8kb+7 = bytes 8*(kb&1) of chunk kb/2; this
-    // thread's four blocks are 4 more bytes in.  Ids run two stages ahead.
+    // thread's blocks are kPartBlocks bytes per part further in.  Ids run two
+    // stages ahead.
+    static_assert(kPartBlocks == 2 || kPartBlocks == 4, "ids are loaded as 2 or 4 bytes");
     auto load_ids = [&](int kb, uint32_t (&dst)[R]) {
 #pragma unroll
-      for (int st = 0; st < R; ++st)
-        dst[st] = (row_ok && kb < kblocks)
-                      ? *reinterpret_cast<const uint32_t*>(idrow + ((long long)(kb >> 1) * R + st) * 256 + 8 * (kb & 1))
-                      : 0u;
+      for (int st = 0; st < R; ++st) {
+        const uint8_t* a = idrow + ((long long)(kb >> 1) * R + st) * 256 + 8 * (kb & 1);
+        dst[st] = !(row_ok && kb < kblocks) ? 0u
+                  : kPartBlocks == 4        ? *reinterpret_cast<const uint32_t*>(a)
+                                            : (uint32_t)*reinterpret_cast<const uint16_t*>(a);
+      }
     };
     uint32_t ids0[R], ids1[R], ids2[R];
     load_ids(0, ids0);
@@ -349,7 +361,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_kernel(const __grid_cons
       }
       if (abort_flag) break;
       const int k_left = row_ok ? p.K - kb * kBK : 0;
-      decode_stage_half<R>(bsm_row0 + s * kBBytes, nsw, ids0, half * 4, cb_lane, rho2, k_left);
+      decode_stage_part<R>(bsm_row0 + s * kBBytes, nsw, ids0, part * kPartBlocks, cb_lane, rho2, k_left);
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) mbar_arrive(full_b + 8 * s);
@@ -366,9 +378,11 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_kernel(const __grid_cons
     if (ok) {
       const int quarter = warp & 3;
       const bool vec_ok = (p.ldy % 8) == 0 && ((uintptr_t)p.y & 15) == 0;
-      // two warps share a lane quarter; each takes two of the four accumulators
-      for (int mi = 0; mi < 2; ++mi) {
-      const int mt = 2 * ((warp - 2) >> 2) + mi;
+      // kDecodeWarps / 4 warps share a lane quarter and split the four accumulators
+      constexpr int kAccPerWarp = 16 / kDecodeWarps;
+      for (int mi = 0; mi < kAccPerWarp; ++mi) {
+      const int mt = kAccPerWarp * ((warp - 2) >> 2) + mi;
+      if (mt >= mtiles) continue;  // this accumulator holds no tokens (warp-uniform)
       const int m = m0 + mt * kUM + quarter * 32 + lane;
       for (int c0 = 0; c0 < kBN; c0 += 16) {
         uint32_t v[16];
