@@ -214,7 +214,7 @@ def gemm_f32(mod: PackedGroupedBlockRVQLinear, x: torch.Tensor) -> torch.Tensor:
 
 @pytest.mark.parametrize("M,N,K,R,bias", [(256, 512, 256, 2, False), (300, 1000, 520, 2, True), (128, 256, 1024, 1, False),
                                           (517, 768, 2048, 2, True), (1100, 640, 384, 2, False),
-                                          (2048, 384, 136, 1, True)])
+                                          (2048, 384, 136, 1, True), (200, 384, 1536, 2, True)])
 def test_prefill_gemm_matches_oracle(M, N, K, R, bias):
     enc = single_group(synthetic.rvq_encoding(N, K, d=8, R=R, seed=M + N))
     b = synthetic.bias_vector(N, seed=3) if bias else None
