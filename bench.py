@@ -505,8 +505,10 @@ def run_ours(args) -> None:
     decode = run_decode(args, rank, world, dev) if args.decode else None
     decode70 = run_decode(args, rank, world, dev, "70b") if args.decode_70b else None
     peaks = measured_peaks()
-    prefill = run_prefill(args, dev, peaks) if (args.prefill and world == 1) else None
+    # the ID-route leg runs before the prefill leg, whose sustained tensor work
+    # leaves the GPU at its power cap for a while afterwards
     idroute = run_idroute(args, dev, peaks) if (args.idroute and world == 1) else None
+    prefill = run_prefill(args, dev, peaks) if (args.prefill and world == 1) else None
     peak = peaks.get("hbm_gbs")
     peak_src = "measured" if peak else "fallback"
     peak = float(peak or 6650.0)
