@@ -12,6 +12,8 @@ seconds and holds a few hundred MB on the device at most.
   idroute_mlp  ID-route linear 4096 -> 14336 (1536 routes), M = 1 GEMV
   attention    decode attention, Llama-3-8B heads (32 q / 8 kv, head dim 128),
                batch 8 over 2048 cached positions
+  prefill_gate_up  tcgen05 prefill GEMM, Llama-3-8B gate/up projection
+               (2 x 14336 rows x 4096, d = 8, R = 2), 2048 tokens
 """
 from __future__ import annotations
 
@@ -68,7 +70,21 @@ def attention() -> None:
         decode_attention(q, k, v, n, out, ws)
 
 
-CASES = {"cfg1_gemv": cfg1_gemv, "gemv_window": gemv_window, "idroute_mlp": idroute_mlp, "attention": attention}
+def prefill_gate_up() -> None:
+    mod = PackedGroupedBlockRVQLinear.random([14336, 14336], 4096, generator=_gen(8), device=DEV)
+    x = torch.randn(2048, 4096, device=DEV, generator=_gen(9)).to(torch.bfloat16)
+    y = torch.empty(2048, 28672, device=DEV, dtype=torch.bfloat16)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    for _ in range(3):
+        if not mod.gemm_into(x, y, status):
+            raise RuntimeError("the prefill GEMM does not cover this layer")
+    torch.cuda.synchronize()
+    if int(status.item()) != 0:
+        raise RuntimeError("prefill GEMM reported a pipeline timeout")
+
+
+CASES = {"cfg1_gemv": cfg1_gemv, "gemv_window": gemv_window, "idroute_mlp": idroute_mlp, "attention": attention,
+         "prefill_gate_up": prefill_gate_up}
 
 
 def main(argv: list[str]) -> int:
