@@ -38,7 +38,7 @@ HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parents[1]))
 
 from wal2026_b200 import synthetic  # noqa: E402
-from wal2026_b200.block_vq import GroupedBlockRVQEncoding, single_group  # noqa: E402
+from wal2026_b200.block_vq import BlockRVQEncoding, GroupedBlockRVQEncoding, single_group  # noqa: E402
 
 
 def sha(t: torch.Tensor | np.ndarray) -> str:
@@ -63,7 +63,8 @@ def to_reference(enc: GroupedBlockRVQEncoding, ref_block_vq):
                                                 original_shape=enc.original_shape)
 
 
-def run_case(name, enc, Ms, x_seed, bias, ref_runtime, ref_block_vq, *, full: bool, y_rows: int | None = None):
+def run_case(name, enc, Ms, x_seed, bias, ref_runtime, ref_block_vq, *, full: bool, y_rows: int | None = None,
+             extra: dict | None = None):
     ref_enc = to_reference(enc, ref_block_vq)
     mod = ref_runtime.PackedGroupedBlockRVQLinear(ref_enc, bias, matmul_strategy="per_group")
     with torch.no_grad():
@@ -86,6 +87,8 @@ def run_case(name, enc, Ms, x_seed, bias, ref_runtime, ref_block_vq, *, full: bo
                 out[f"g{gi}_scales"] = g.stage_scales.numpy()
     if bias is not None:
         out["bias_bits"] = bits(bias)
+    for key, value in (extra or {}).items():
+        out[key] = np.array(value)
     for M in Ms:
         x = synthetic.activations(M, enc.original_shape[1], seed=x_seed)
         with torch.no_grad():
@@ -165,6 +168,17 @@ def main() -> None:
              scaled(synthetic.grouped_encoding([32, 16], 96, d=16, R=3, seed=20),
                     [[1.0, 0.5, 0.333251953125], [0.9, 1.1, 0.7]]), [3], 20, None, ref_runtime, ref_block_vq,
              full=True)
+    # product splits, encoded by the reference's own encoder (src/block_vq.py:340-531): split 0
+    # (columns 0..3 of every 8-column block) has two stages, split 1 one; each stage's codebook is
+    # stored full width with zeros outside its split, so the fused path sums three stages
+    torch.manual_seed(23)
+    weight = torch.randn(48, 128) * 0.02
+    ref_enc = ref_block_vq.encode_block_residual_vq(weight, block_size=8, codebook_size=256, num_stages=2,
+                                                    product_splits=2, stages_per_split=(2, 1), kmeans_iters=4)
+    ours = BlockRVQEncoding(**{f.name: getattr(ref_enc, f.name) for f in dataclasses.fields(BlockRVQEncoding)})
+    run_case("small_product_splits", single_group(ours), [1, 6], 23, synthetic.bias_vector(48, seed=23),
+             ref_runtime, ref_block_vq, full=True, extra={"product_splits": 2, "stages_per_split": [2, 1],
+                                                          "stage_value_dims": list(ref_enc.stage_value_dims)})
     # an encoding map written by the reference's own saver (src/encoding_io.py:77-85)
     from src import encoding_io as ref_io  # type: ignore
 

@@ -10,7 +10,8 @@ import torch
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
 SMALL_CASES = ["small_r2_d8", "small_r1_ragged", "small_r3_d16", "small_grouped", "small_route",
-               "small_d32", "small_r4_wide", "small_scaled_r2", "small_scaled_r1", "small_scaled_grouped"]
+               "small_d32", "small_r4_wide", "small_scaled_r2", "small_scaled_r1", "small_scaled_grouped",
+               "small_product_splits"]
 
 
 def load(name: str) -> dict:
@@ -61,6 +62,10 @@ def encoding_from_fixture(fx: dict):
         enc = make_plain_encoding(ids, books, rho, in_features=K, block_size=d)
         if g["stage_scales"] is not None:
             enc = dataclasses.replace(enc, stage_scales=torch.from_numpy(np.ascontiguousarray(g["stage_scales"])))
+        if "product_splits" in fx:  # the reference encoder's split metadata (codebooks are full width)
+            enc = dataclasses.replace(enc, product_splits=int(fx["product_splits"]),
+                                      stages_per_split=tuple(int(v) for v in fx["stages_per_split"]),
+                                      stage_value_dims=tuple(int(v) for v in fx["stage_value_dims"]))
         n = int(ids[0].shape[0])
         groups.append(enc)
         slices.append((row0, row0 + n))

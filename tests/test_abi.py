@@ -185,3 +185,11 @@ def test_profile_cases_cli_lists_its_cases():
 
     assert set(profile_cases.CASES) == {"cfg1_gemv", "gemv_window", "idroute_mlp", "attention", "prefill_gate_up"}
     assert profile_cases.main(["no_such_case"]) == 2
+
+
+def test_product_split_encoding_is_accepted():
+    """Reference-encoded product splits: full-width codebooks summed like any other stages."""
+    fx = goldens.load("small_product_splits")
+    mod = PackedGroupedBlockRVQLinear(goldens.encoding_from_fixture(fx))
+    g = mod.groups[0]  # split metadata lives on the row group, as in the reference's PackedBlockRVQGroup
+    assert g.product_splits == 2 and g.stages_per_split == (2, 1) and mod.num_stages == 3
