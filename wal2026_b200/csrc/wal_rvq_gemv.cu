@@ -197,11 +197,9 @@ __device__ __forceinline__ void gemv_chunk(float (&acc)[GemvCfg<D, R, IDW, REPL,
                                            uint32_t rho_b, const LaneSel& ls, const uint16_t* x, const uint32_t (&xoff)[MT],
                                            const uint32_t (&xsa)[MT], const bool (&xv)[MT], int col_base, int xcol, int K) {
   using C = GemvCfg<D, R, IDW, REPL, MT, XM>;
-  static_for<0, D>([&](auto ktc) {
+  // activations of k-tile kt, then the MMAs of the decoded fragments ra (row r), rb (row r + 8)
+  auto consume = [&](auto ktc, const uint32_t (&ra)[2], const uint32_t (&rb)[2]) {
     constexpr int kt = decltype(ktc)::value;
-    uint32_t ra[2], rb[2];
-    decode_row<D, R, IDW, REPL, kt, C::NW, SC>(ra, c0, cb, cbl, rho_a, ls);
-    decode_row<D, R, IDW, REPL, kt, C::NW, SC>(rb, c1, cb, cbl, rho_b, ls);
     const int col = col_base + kt * 16;  // lane's first physical column (includes 4q)
     const bool in_k = !MASK || col < K;
     uint2 xf[MT];
@@ -222,7 +220,36 @@ __device__ __forceinline__ void gemv_chunk(float (&acc)[GemvCfg<D, R, IDW, REPL,
     // (independent MMA chains); four n-tiles are four chains already
 #pragma unroll
     for (int i = 0; i < MT; ++i) mma_bf16_16816(acc[kt % C::kAcc][i], a, xf[i].x, xf[i].y);
-  });
+  };
+  if constexpr (R == 1 && !SC) {
+    // one-stage tables: one gather per row and k-tile; issue the gathers of
+    // four k-tiles before using any, so their shared-memory latency overlaps
+    constexpr int kGroup = 4;
+    static_for<0, D / kGroup>([&](auto gc) {
+      constexpr int g0 = decltype(gc)::value * kGroup;
+      uint2 pa[kGroup], pb[kGroup];
+      static_for<0, kGroup>([&](auto jc) {
+        constexpr int j = decltype(jc)::value, kt = g0 + j;
+        constexpr int half_off = (D == 32) ? (kt & 1) * CbLayout<D, REPL>::kHalfStride : 0;
+        pa[j] = lds64<half_off>(piece_addr<D, R, IDW, REPL, kt, C::NW, 0>(c0, cb, ls, cbl));
+        pb[j] = lds64<half_off>(piece_addr<D, R, IDW, REPL, kt, C::NW, 0>(c1, cb, ls, cbl));
+      });
+      static_for<0, kGroup>([&](auto jc) {
+        constexpr int j = decltype(jc)::value;
+        const uint32_t ra[2] = {mul_bf16x2_rn(pa[j].x, rho_a), mul_bf16x2_rn(pa[j].y, rho_a)};
+        const uint32_t rb[2] = {mul_bf16x2_rn(pb[j].x, rho_b), mul_bf16x2_rn(pb[j].y, rho_b)};
+        consume(std::integral_constant<int, g0 + j>{}, ra, rb);
+      });
+    });
+  } else {
+    static_for<0, D>([&](auto ktc) {
+      constexpr int kt = decltype(ktc)::value;
+      uint32_t ra[2], rb[2];
+      decode_row<D, R, IDW, REPL, kt, C::NW, SC>(ra, c0, cb, cbl, rho_a, ls);
+      decode_row<D, R, IDW, REPL, kt, C::NW, SC>(rb, c1, cb, cbl, rho_b, ls);
+      consume(ktc, ra, rb);
+    });
+  }
 }
 
 template <int D, int R, int IDW, bool REPL, int MT, int XM, bool SC>
