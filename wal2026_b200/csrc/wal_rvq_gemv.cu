@@ -223,8 +223,8 @@ __device__ __forceinline__ void gemv_chunk(float (&acc)[GemvCfg<D, R, IDW, REPL,
   };
   if constexpr (R == 1 && !SC) {
     // one-stage tables: one gather per row and k-tile; issue the gathers of
-    // four k-tiles before using any, so their shared-memory latency overlaps
-    constexpr int kGroup = 4;
+    // eight k-tiles before using any, so their shared-memory latency overlaps
+    constexpr int kGroup = 8;
     static_for<0, D / kGroup>([&](auto gc) {
       constexpr int g0 = decltype(gc)::value * kGroup;
       uint2 pa[kGroup], pb[kGroup];
