@@ -59,7 +59,7 @@ NOMINAL_HBM_GBS = 8000.0
 # DRAM bytes per launch of rvq_gemv_kernel on this workload (one cfg1 instance, M = 1):
 # dram__bytes_read.sum + dram__bytes_write.sum from an ncu capture of
 # `python -m wal2026_b200.profile_cases cfg1_gemv`.
-NCU_TRAFFIC_BYTES = 7534336
+NCU_TRAFFIC_BYTES = 7532288
 
 
 def algorithmic_bytes(M: int) -> int:
