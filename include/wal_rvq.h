@@ -302,12 +302,17 @@ WAL_API int wal_silu_mul(const uint16_t* gu, int64_t ld_gu, int64_t M, int64_t I
  * contiguous, 8-byte aligned); k_cache/v_cache: bf16 [B, hkv, cache_len, hd]
  * contiguous, 16-byte aligned; out: bf16 rows ld_out apart.  hd in {64, 128},
  * G in {1, 2, 4, 8}.
- * workspace: device scratch of at least wal_decode_attention_workspace(...)
- * bytes, 256-byte aligned and zero-filled before its first use (the kernel
- * leaves its counters at zero again); calls sharing one workspace must not
- * overlap in time.  Split-K over positions with an exact (log-sum-exp)
- * merge in split order: deterministic.  No reference counterpart (the
- * reference runs Hugging Face attention).
+ * workspace: device scratch of at least wal_decode_attention_workspace(B, hq,
+ * hkv, hd, max_n) bytes for calls with n <= max_n positions (the size covers
+ * the largest split count of any such n), 256-byte aligned and zero-filled
+ * before its first use.  Its merge counters sit at a fixed offset at the
+ * front and every call leaves them at zero, so one workspace serves a whole
+ * decode loop whose n grows; calls sharing one workspace must not overlap in
+ * time.  Split-K over positions with an exact (log-sum-exp) merge in split
+ * order: deterministic.  The merge keeps 8 * G bytes per split in shared
+ * memory: a call whose splits (about n / 128 at large n) do not fit in 227 KB
+ * returns WAL_ERR_SHAPE (hd = 128, G = 8: n <= 366,592 positions).  No
+ * reference counterpart (the reference runs Hugging Face attention).
  */
 WAL_API size_t wal_decode_attention_workspace(int64_t B, int32_t hq, int32_t hkv, int32_t hd, int64_t n);
 WAL_API int wal_decode_attention(const uint16_t* q, int64_t ld_q, const uint16_t* k_cache,
@@ -323,11 +328,10 @@ WAL_API int wal_decode_attention(const uint16_t* q, int64_t ld_q, const uint16_t
  * brings.  Arguments and results (bit-identical) are those of
  * wal_decode_attention without the workspace: the scratch is a 4 MiB array
  * compiled into this library, which every GPU that loads the library keeps
- * until the process exits.  Limit: B * hkv <= 4096 and the split partials
- * within 4 MiB - 16 KiB (the bytes wal_decode_attention_workspace reports
- * minus B * hkv * 4, rounded up to 256; Llama-3-8B heads at 2048 positions
- * fit up to batch 15); larger calls return WAL_ERR_BUFFER_TOO_SMALL and
- * launch nothing.  Each call clears the merge counters it uses with an
+ * until the process exits.  Limit: B * hkv <= 4096 and the call's split
+ * partials and statistics (B * hkv * nsplit * G * (hd + 2) * 4 bytes) within
+ * 4 MiB - 16 KiB (Llama-3-8B heads at 2048 positions fit up to batch 15);
+ * larger calls return WAL_ERR_BUFFER_TOO_SMALL and launch nothing.  Each call clears the merge counters it uses with an
  * asynchronous memset on the stream before its kernel.  The first call on a
  * device looks up the array's device address (cudaGetSymbolAddress, that
  * device current); make that first call before any stream capture.  Every

@@ -193,3 +193,13 @@ def test_product_split_encoding_is_accepted():
     mod = PackedGroupedBlockRVQLinear(goldens.encoding_from_fixture(fx))
     g = mod.groups[0]  # split metadata lives on the row group, as in the reference's PackedBlockRVQGroup
     assert g.product_splits == 2 and g.stages_per_split == (2, 1) and mod.num_stages == 3
+
+
+def test_attention_workspace_covers_every_shorter_call():
+    # the size for max_n must cover each n <= max_n (the split count itself is
+    # not monotone in n), so the reported size never decreases as n grows
+    lib = _abi.load()
+    for B, hkv, hq in ((1, 8, 32), (2, 8, 64), (3, 2, 8), (16, 8, 32)):
+        sizes = [int(lib.wal_decode_attention_workspace(B, hq, hkv, 128, n)) for n in range(1, 5000)]
+        assert all(a <= b for a, b in zip(sizes, sizes[1:])), (B, hkv)
+        assert sizes[0] > 0

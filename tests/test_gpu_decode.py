@@ -112,6 +112,25 @@ def test_decode_attention_matches_reference_math(B, hq, hkv, hd, L, n):
     assert torch.equal(out, again)
 
 
+@pytest.mark.parametrize("B,hq,hkv,hd,L", [(1, 32, 8, 128, 1024), (2, 8, 2, 64, 700)])
+def test_decode_attention_reuses_one_workspace_while_n_grows(B, hq, hkv, hd, L):
+    # a decode loop sizes one workspace for its longest context and reuses it as
+    # n grows; the split count is not monotone in n (for B = 1, hkv = 8 it drops
+    # from 19 to 17 at n = 609), so each call must find its counters at zero
+    g = _gen(B * 31 + L)
+    q = torch.randn(B, hq * hd, device=DEV, generator=g).to(torch.bfloat16)
+    kc = torch.randn(B, hkv, L, hd, device=DEV, generator=g).to(torch.bfloat16)
+    vc = torch.randn(B, hkv, L, hd, device=DEV, generator=g).to(torch.bfloat16)
+    ws = decode_attention_workspace(B, hq, hkv, hd, L, DEV)
+    for n in list(range(600, 621)) + list(range(L - 8, L + 1)):
+        got = torch.full((B, hq * hd), float("nan"), device=DEV, dtype=torch.bfloat16)
+        decode_attention(q, kc, vc, n, got, ws)
+        want = torch.empty_like(got)
+        decode_attention(q, kc, vc, n, want, decode_attention_workspace(B, hq, hkv, hd, n, DEV))
+        torch.cuda.synchronize()
+        assert torch.equal(got, want), n
+
+
 def _layer(N, K, seed=0):
     return PackedGroupedBlockRVQLinear.random([N], K, generator=_gen(seed), device=DEV)
 

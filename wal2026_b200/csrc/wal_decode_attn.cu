@@ -284,13 +284,21 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   }
 }
 
-void plan(long long B, int hkv, long long n, int* nsplit, int* chunk) {
+// Split count before rounding the chunk to a multiple of 4: about one CTA per
+// SM, at most kMaxChunk and at least 32 positions per split.  Every term is
+// non-decreasing in n, so this is an upper bound of plan()'s split count for
+// every n' <= n (the chunk rounding in plan() only lowers it).
+long long split_bound(long long B, int hkv, long long n) {
   long long s = (kTargetCtas + B * hkv - 1) / (B * hkv);
   const long long min_split = (n + kMaxChunk - 1) / kMaxChunk;
   if (s < min_split) s = min_split;
   const long long max_split = (n + 31) / 32;  // at least 32 positions per split
   if (s > max_split) s = max_split;
-  if (s < 1) s = 1;
+  return s < 1 ? 1 : s;
+}
+
+void plan(long long B, int hkv, long long n, int* nsplit, int* chunk) {
+  long long s = split_bound(B, hkv, n);
   long long c = ((n + s - 1) / s + 3) & ~3LL;  // multiple of 4 keeps the shared-memory regions 16-byte aligned
   s = (n + c - 1) / c;
   *nsplit = (int)s;
@@ -314,12 +322,24 @@ size_t part_bytes(long long B, int hkv, int nsplit, int G, int hd) {
 size_t stats_bytes(long long B, int hkv, int nsplit, int G) {
   return ((size_t)B * hkv * nsplit * G * sizeof(float2) + 255) & ~(size_t)255;
 }
+// The merge counters sit at the front of a workspace, at an offset that does
+// not depend on n: calls of growing n that reuse one workspace find them at
+// zero where the previous call left them.
+size_t counter_bytes(long long B, int hkv) { return ((size_t)B * hkv * sizeof(unsigned) + 255) & ~(size_t)255; }
+
+// Dynamic shared memory of one CTA: the V rows, then the K rows, which the
+// output buffer and the merge's per-split weights (2 floats per head and
+// split) reuse once K has been read.
+size_t smem_bytes(int hd, int G, long long nsplit) {
+  const size_t k_region = (size_t)kMaxChunk * hd * 2, out_region = ((size_t)4 * G * hd + (size_t)2 * G * nsplit) * 4;
+  return (size_t)kMaxChunk * hd * 2 + (k_region > out_region ? k_region : out_region);
+}
+constexpr size_t kMaxSmem = 227u * 1024u;  // opt-in dynamic shared memory per CTA on sm_100
 
 template <int HD, int G>
 int launch(const AttnParams& p, long long B, void* stream) {
   auto kern = decode_attn_kernel<HD, G>;
-  const int k_region = kMaxChunk * HD * 2, out_region = (4 * G * HD + 2 * G * p.nsplit) * 4;
-  const int smem = kMaxChunk * HD * 2 + (k_region > out_region ? k_region : out_region);
+  const int smem = (int)smem_bytes(HD, G, p.nsplit);
   if (smem > 48 * 1024 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return WAL_ERR_CUDA;
   cudaLaunchConfig_t cfg = {};
@@ -353,10 +373,10 @@ extern "C" {
 
 size_t wal_decode_attention_workspace(int64_t B, int32_t hq, int32_t hkv, int32_t hd, int64_t n) {
   if (B <= 0 || hq <= 0 || hkv <= 0 || hd <= 0 || n <= 0 || hq % hkv) return 0;
-  int nsplit = 0, chunk = 0;
-  plan(B, hkv, n, &nsplit, &chunk);
+  // sized for the largest split count of any call with up to n positions
+  const int nsplit = (int)split_bound(B, hkv, n);
   const int G = hq / hkv;
-  return part_bytes(B, hkv, nsplit, G, hd) + stats_bytes(B, hkv, nsplit, G) + (size_t)B * hkv * sizeof(unsigned);
+  return counter_bytes(B, hkv) + part_bytes(B, hkv, nsplit, G, hd) + stats_bytes(B, hkv, nsplit, G);
 }
 
 }  // extern "C"
@@ -385,6 +405,7 @@ int prepare(const uint16_t* q, int64_t ld_q, const uint16_t* k_cache, const uint
   p->hkv = hkv;
   p->hd = hd;
   plan(B, hkv, n, &p->nsplit, &p->chunk);
+  if (smem_bytes(hd, hq / hkv, p->nsplit) > kMaxSmem) return WAL_ERR_SHAPE;  // merge weights of too many splits
   p->qscale = scale * 1.4426950408889634f;  // log2(e)
   p->out = out;
   p->ld_out = ld_out;
@@ -415,9 +436,10 @@ int wal_decode_attention(const uint16_t* q, int64_t ld_q, const uint16_t* k_cach
   if (workspace_bytes < wal_decode_attention_workspace(B, hq, hkv, hd, n)) return WAL_ERR_BUFFER_TOO_SMALL;
   const int G = hq / hkv;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  p.part = reinterpret_cast<float*>(ws);
-  p.stats = reinterpret_cast<float2*>(ws + part_bytes(B, hkv, p.nsplit, G, hd));
-  p.counter = reinterpret_cast<unsigned*>(ws + part_bytes(B, hkv, p.nsplit, G, hd) + stats_bytes(B, hkv, p.nsplit, G));
+  const size_t cb = counter_bytes(B, hkv);
+  p.counter = reinterpret_cast<unsigned*>(ws);
+  p.part = reinterpret_cast<float*>(ws + cb);
+  p.stats = reinterpret_cast<float2*>(ws + cb + part_bytes(B, hkv, p.nsplit, G, hd));
   return run(p, B, stream);
 }
 
