@@ -203,3 +203,19 @@ def test_attention_workspace_covers_every_shorter_call():
         sizes = [int(lib.wal_decode_attention_workspace(B, hq, hkv, 128, n)) for n in range(1, 5000)]
         assert all(a <= b for a, b in zip(sizes, sizes[1:])), (B, hkv)
         assert sizes[0] > 0
+
+
+def _documented_struct(name: str) -> list[tuple[str, str]]:
+    """(field, ctypes type text) pairs of a ctypes struct in INTEGRATION.md's binding snippet."""
+    text = (HEADER.parents[1] / "INTEGRATION.md").read_text()
+    m = re.search(rf"class {name}\(ctypes\.Structure\):\s*_fields_ = \[(.*?)\][^\n]*\n", text, re.S)
+    assert m, f"{name} not found in INTEGRATION.md"
+    return re.findall(r'\("(\w+)",\s*([\w.]+(?:\([\w.]+\))?)\)', m.group(1))
+
+
+def test_documented_binding_structs_match_the_library_structs():
+    # a maintainer copies INTEGRATION.md's ctypes structs; a missing or reordered
+    # field would shift every later pointer the library reads
+    for doc_name, lib_struct in (("_Geom", _abi.Geometry), ("_Layer", _abi.Layer)):
+        doc = [(f, eval(t, {"ctypes": ctypes, "_Geom": _abi.Geometry})) for f, t in _documented_struct(doc_name)]
+        assert doc == list(lib_struct._fields_), (doc_name, doc, lib_struct._fields_)
