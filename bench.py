@@ -18,19 +18,25 @@ Arms:
 Multi-GPU (torchrun): every rank runs its own instances (weak scaling, no
 collective on the data path); the time is the max over ranks.
 
-Also reported in the same JSON line (BASELINE's second metric and config 3):
+Also reported in the same JSON line (BASELINE's second metric and configs 0, 2, 3, 4):
+  gemv_configs (N = 1) config 0 (Block-RVQ 2048 x 2048, d=8, R=2) at M = 1/4/16
+              over 256 distinct instances, and config 1 at M = 8/16, GB/s of
+              algorithmic bytes with a roofline against the measured HBM copy;
   decode_8b   Llama-3-8B-shaped stack (random init, every projection Block-RVQ
               d=8, R=2, 256 entries; dense bf16 lm_head), one CUDA graph per
               decode step at a 2048-token context, tensor-parallel over all
               N GPUs (NVLink push exchange after the row-parallel linears),
-              next to the same stack with dense bf16 cuBLAS projections;
+              next to the same stack with dense bf16 cuBLAS projections (same
+              push exchange; at N > 1 also with an NCCL all-reduce); at N > 1
+              the logits of one sharded step against the unsharded stack;
+  decode_1b   config 2: the Llama-3.2-1B-shaped stack at batch 1/16 on a
+              512-token context, same arms;
+  decode_70b  config 4: the Llama-3-70B-shaped stack at batch 1/16/64 on a
+              4096-token context, same arms; configurations that do not fit
+              a GPU's memory at this N are listed as skipped;
   prefill_8b  (N = 1) the stack's 128 projection GEMMs at M = 2048 tokens on
               the tcgen05 decode-to-shared-memory GEMM, TFLOP/s against the
               measured bf16 peak, next to cuBLAS on the same shapes;
-  decode_70b  (--decode-70b 1) config 4: the Llama-3-70B-shaped stack at
-              batch 1/16/64 on a 4096-token context, tensor-parallel over all
-              N GPUs; configurations that do not fit a GPU's memory at this
-              N are listed as skipped;
   idroute_gemv (N = 1) the ID-route linear (reference PackedIDRouteLinear:
               an int16 id per weight into fp16 route sums) on the 8B MLP
               shape, GB/s against the measured HBM bandwidth.
@@ -240,6 +246,48 @@ def _decode_bytes_per_rank(shape, kind: str, batch: int, context: int, world: in
     return int(weights + embed + kv + draw + 4e9)
 
 
+DECODE_LEGS = {
+    # which: (model name, batches argument, context argument)
+    "1b": ("Llama-3.2-1B", "decode1b_batches", "context1b"),
+    "8b": ("Llama-3-8B", "decode_batches", "context"),
+    "70b": ("Llama-3-70B", "decode70_batches", "context70"),
+}
+
+
+def tp_logits_error(st, shape, which: str, rank: int, world: int, dev: torch.device, context: int) -> float | None:
+    """Relative max error of one tensor-parallel decode step's logits against the unsharded stack (rank 0).
+
+    Every rank holds a shard of the same seeded model and a slice of the same
+    cache, so the sharded step (push exchange) must reproduce the single-GPU
+    step up to the order of the fp32 partial sums.
+    """
+    import torch.distributed as dist
+
+    from wal2026_b200.llama import rvq_llama
+
+    batch = 1
+    gen = torch.Generator(device=dev).manual_seed(17)
+    tokens = torch.randint(0, shape.vocab, (batch,), device=dev, generator=gen)
+    st.allocate_cache(batch, context + 1, consistent=True, seed=19)
+    cos, sin = st.rope_tables(context)
+    st.enable_push_exchange(batch)
+    logits = st.decode_step_fused(tokens, context, cos, sin, exchange="push").float()
+    torch.cuda.synchronize()
+    st.k_cache, st.v_cache = [], []
+    torch.cuda.empty_cache()
+    err = None
+    if rank == 0:
+        full = rvq_llama(shape, device=dev, seed=0)
+        full.allocate_cache(batch, context + 1, consistent=True, seed=19)
+        ref = full.decode_step_fused(tokens, context, cos, sin).float()
+        torch.cuda.synchronize()
+        err = float((logits - ref).abs().max() / ref.abs().max())
+        del full, ref
+        torch.cuda.empty_cache()
+    dist.barrier()
+    return err
+
+
 def run_decode(args, rank: int, world: int, dev: torch.device, which: str = "8b") -> dict:
     """Llama-shaped decode tok/s, tensor-parallel over every rank (all ranks call this together)."""
     import torch.distributed as dist
@@ -248,22 +296,28 @@ def run_decode(args, rank: int, world: int, dev: torch.device, which: str = "8b"
 
     shape = SHAPES[which]
     tp = TPContext(rank, world, dist.group.WORLD if world > 1 else None)
-    if which == "8b":
-        batches, context = [int(b) for b in args.decode_batches.split(",") if b], args.context
-    else:
-        batches, context = [int(b) for b in args.decode70_batches.split(",") if b], args.context70
+    name, batches_arg, context_arg = DECODE_LEGS[which]
+    batches = [int(b) for b in getattr(args, batches_arg).split(",") if b]
+    context = int(getattr(args, context_arg))
     total = torch.cuda.get_device_properties(dev).total_memory
-    name = {"8b": "Llama-3-8B", "70b": "Llama-3-70B"}[which]
+    exch = "nvlink push (tagged words)" if world > 1 else "none"
     out = {"model": f"{name} shape ({shape.layers} layers, hidden {shape.hidden}, MLP {shape.mlp}, "
                     f"{shape.heads} q / {shape.kv_heads} kv heads, vocab {shape.vocab}), random init; "
                     "q/k/v/o/gate/up/down Block-RVQ d=8 R=2 256 entries; lm_head dense bf16",
-           "context": context, "tp": world, "exchange": "nvlink push (tagged words)" if world > 1 else "none",
+           "context": context, "tp": world, "exchange": exch,
            "graph": "one CUDA graph per decode step", "steps": args.decode_steps}
-    for kind, ctor, exchange in (("rvq", rvq_llama, "push"), ("dense_bf16_cublas", dense_llama, "nccl")):
+    # the dense comparator runs the same push exchange as the RVQ stack (a
+    # separate push of the cuBLAS output) and, under tensor parallelism, also
+    # the NCCL all-reduce, so the speed-up compares linears, not exchanges
+    arms = [("rvq", rvq_llama, "push"), ("dense_bf16_cublas", dense_llama, "push")]
+    if world > 1:
+        arms.append(("dense_bf16_cublas_nccl", dense_llama, "nccl"))
+    for kind, ctor, exchange in arms:
         if kind.startswith("dense") and not args.dense:
             continue
-        fits = [b for b in batches if _decode_bytes_per_rank(shape, kind, b, context, world) < 0.85 * total]
-        res = {str(b): {"skipped": f"needs ~{_decode_bytes_per_rank(shape, kind, b, context, world) / 1e9:.0f} GB "
+        dkind = "dense" if kind.startswith("dense") else "rvq"
+        fits = [b for b in batches if _decode_bytes_per_rank(shape, dkind, b, context, world) < 0.85 * total]
+        res = {str(b): {"skipped": f"needs ~{_decode_bytes_per_rank(shape, dkind, b, context, world) / 1e9:.0f} GB "
                                    f"per GPU at tp={world}"} for b in batches if b not in fits}
         if fits:
             st = ctor(shape, device=dev, seed=0, tp=tp)
@@ -275,6 +329,9 @@ def run_decode(args, rank: int, world: int, dev: torch.device, which: str = "8b"
                 torch.cuda.empty_cache()
             if kind == "rvq":
                 out["rvq_projection_bytes_per_rank"] = st.linear_bytes()
+                if world > 1 and args.tp_check:
+                    err = tp_logits_error(st, shape, which, rank, world, dev, context)
+                    out["tp_logits_max_rel_err_vs_unsharded"] = None if err is None else round(err, 6)
             st.close()
             del st
             torch.cuda.empty_cache()
@@ -283,6 +340,63 @@ def run_decode(args, rank: int, world: int, dev: torch.device, which: str = "8b"
         out["rvq_speedup_vs_dense"] = {
             b: round(out["rvq"][b]["tok_s"] / out["dense_bf16_cublas"][b]["tok_s"], 3)
             for b in out["rvq"] if "tok_s" in out["rvq"][b] and "tok_s" in out["dense_bf16_cublas"][b]}
+    return out
+
+
+def _gemv_line(mods, M: int, K: int, reps: int, bytes_per: int, peak: float, dev: torch.device) -> dict:
+    """GB/s of one GEMV shape over distinct instances (inputs larger than L2), graph replay, CUDA events."""
+    x = torch.randn(M, K, device=dev).to(torch.bfloat16)
+    y = torch.empty(M, mods[0].out_features, device=dev, dtype=torch.bfloat16)
+    for m in mods:
+        m.gemv_into(x, y)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for m in mods:
+            m.gemv_into(x, y)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * len(mods))
+    gbs = bytes_per / (us * 1e-6) / 1e9
+    del g
+    return {"M": M, "us_per_gemv": round(us, 3), "gbs": round(gbs, 1),
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "algorithmic_bytes_per_launch": bytes_per},
+            "gpu_launches": reps * len(mods)}
+
+
+def run_gemv_configs(args, dev: torch.device, peaks: dict, cfg1_mods) -> dict:
+    """cfg0 (2048 x 2048, d=8, R=2) at M = 1/4/16 and cfg1 at M = 8/16 (the headline is cfg1 at M = 1)."""
+    from wal2026_b200.runtime import PackedGroupedBlockRVQLinear
+
+    peak = float(peaks.get("hbm_gbs") or 6650.0)
+    out = {"peak_source": "measured hbm_gbs" if peaks.get("hbm_gbs") else "fallback"}
+    N, K, d, R = 2048, 2048, 8, 2
+    gen = torch.Generator(device=dev).manual_seed(23)
+    mods = [PackedGroupedBlockRVQLinear.random([N], K, block_size=d, num_stages=R, generator=gen, device=dev)
+            for _ in range(args.cfg0_instances)]
+    lines = []
+    for M in (1, 4, 16):
+        nbytes = N * (K // d) * R + R * 256 * d * 2 + 2 * N + 2 * M * K + 2 * M * N
+        lines.append(_gemv_line(mods, M, K, 20, nbytes, peak, dev))
+    out["cfg0"] = {"workload": f"Block-RVQ linear {K}->{N}, d={d}, R={R}, 256 entries (cfg0 distributions), "
+                               f"{len(mods)} distinct instances ({len(mods) * N * K * R // d / 1e6:.0f} MB of ids, "
+                               "larger than L2) per graph", "lines": lines}
+    del mods
+    lines = []
+    for M in (8, 16):
+        lines.append(_gemv_line(cfg1_mods, M, K_IN, 20, algorithmic_bytes(M), peak, dev))
+    out["cfg1"] = {"workload": f"cfg1 route-codebook linear {K_IN}->{N_OUT}, {len(cfg1_mods)} instances per graph",
+                   "lines": lines}
+    torch.cuda.empty_cache()
     return out
 
 
@@ -502,9 +616,11 @@ def run_ours(args) -> None:
                  "rvq_speedup": round(dms / (per_launch_s * 1e3), 3)}
         del ws
 
-    decode = run_decode(args, rank, world, dev) if args.decode else None
-    decode70 = run_decode(args, rank, world, dev, "70b") if args.decode_70b else None
     peaks = measured_peaks()
+    gemv_cfgs = run_gemv_configs(args, dev, peaks, mods) if (args.gemv_configs and world == 1) else None
+    decode = run_decode(args, rank, world, dev) if args.decode else None
+    decode1b = run_decode(args, rank, world, dev, "1b") if args.decode_1b else None
+    decode70 = run_decode(args, rank, world, dev, "70b") if args.decode_70b else None
     # the ID-route leg runs before the prefill leg, whose sustained tensor work
     # leaves the GPU at its power cap for a while afterwards
     idroute = run_idroute(args, dev, peaks) if (args.idroute and world == 1) else None
@@ -538,7 +654,9 @@ def run_ours(args) -> None:
             "clocks": clocks,
             "cpu_baseline": cpu,
             "dense_bf16_cublas": dense,
+            "gemv_configs": gemv_cfgs,
             "decode_8b": decode,
+            "decode_1b": decode1b,
             "decode_70b": decode70,
             "prefill_8b": prefill,
             "idroute_gemv": idroute,
@@ -567,7 +685,14 @@ def main() -> None:
     ap.add_argument("--decode-batches", default="1,8,32")
     ap.add_argument("--decode-steps", type=int, default=20)
     ap.add_argument("--context", type=int, default=2048)
-    ap.add_argument("--decode-70b", type=int, default=0, help="also time the 70B-shaped decode step (config 4)")
+    ap.add_argument("--decode-70b", type=int, default=1, help="also time the 70B-shaped decode step (config 4)")
+    ap.add_argument("--decode-1b", type=int, default=1, help="also time the 1B-shaped decode step (config 2)")
+    ap.add_argument("--decode1b-batches", default="1,16")
+    ap.add_argument("--context1b", type=int, default=512)
+    ap.add_argument("--tp-check", type=int, default=1,
+                    help="at N > 1, compare one tensor-parallel decode step's logits with the unsharded stack")
+    ap.add_argument("--gemv-configs", type=int, default=1, help="also time cfg0 M=1/4/16 and cfg1 M=8/16 (N = 1)")
+    ap.add_argument("--cfg0-instances", type=int, default=256)
     ap.add_argument("--decode70-batches", default="1,16,64")
     ap.add_argument("--context70", type=int, default=4096)
     ap.add_argument("--prefill", type=int, default=1, help="also time the 8B-shaped prefill GEMMs (N = 1)")

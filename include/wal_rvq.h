@@ -272,6 +272,17 @@ WAL_API int wal_tp_reduce_rmsnorm(const void* recv, int32_t num_ranks, int64_t r
                           int64_t M, int64_t N, int* status, void* stream);
 
 /*
+ * Sending half of the exchange for an output another kernel produced (a dense
+ * library GEMM, say): y (WAL_F32 or WAL_BF16, rows < M, N columns, row stride
+ * ldy) is stored into dst[p] of every rank p as {value, tag} words, two words
+ * per 16-byte store, tag = *epoch + 1; wal_tp_reduce_rmsnorm receives it
+ * exactly like the words of wal_rvq_gemv_push.  N, ldy and push->ld_dst even;
+ * every dst[p] 16-byte aligned.
+ */
+WAL_API int wal_tp_push_rows(const void* y, int64_t ldy, int y_dtype, int64_t M, int64_t N, const wal_tp_push* push,
+                     void* stream);
+
+/*
  * Local form: h <- bf16(h + bf16(partial)) when partial (fp32, rows ldp apart)
  * is not NULL, then x_out <- bf16(h * rsqrt(mean(h^2) + eps) * norm_weight).
  */

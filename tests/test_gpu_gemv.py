@@ -244,3 +244,42 @@ def test_prefill_falls_back_for_uncovered_formats():
     assert not mod.gemm_into(x, y)
     ref = orc.forward_f32(bits_of(x), orc.groups_from_encoding(enc), 256)
     assert_close(mod(x).float().cpu().numpy(), ref, tol=8e-3)
+
+
+def _sampled_groups(enc, rows: np.ndarray) -> list[dict]:
+    """Oracle group dicts holding only the given (sorted, global) output rows of each group."""
+    out = []
+    for g, (r0, r1) in zip(orc.groups_from_encoding(enc), enc.row_slices):
+        sel = rows[(rows >= r0) & (rows < r1)] - r0
+        if sel.size == 0:
+            continue
+        out.append({"stage_ids": [a[sel] for a in g["stage_ids"]], "codebooks": g["codebooks"],
+                    "row_scale": np.asarray(g["row_scale"]).reshape(-1)[sel], "stage_scales": None})
+    return out
+
+
+@pytest.mark.parametrize("rows,K", [([4096, 1024, 1024], 4096), ([4096], 4096), ([14336, 14336], 4096),
+                                    ([4096], 14336)], ids=["qkv", "o", "gate_up", "down"])
+def test_prefill_gemm_at_8b_layer_shapes(rows, K):
+    # the Llama-3-8B projections the prefill benchmark times, at M = 2048 tokens;
+    # the C oracle checks a spread sample of output rows (every 128-row tile
+    # boundary case included) so the CPU side stays a few seconds
+    from oracle import c_oracle
+
+    M = 2048
+    enc = synthetic.grouped_encoding(rows, K, d=8, R=2, seed=K + len(rows))
+    N = sum(rows)
+    mod = PackedGroupedBlockRVQLinear(enc).cuda()
+    x = synthetic.activations(M, K, seed=K)
+    y = gemm_f32(mod, x).cpu().numpy()
+    rng = np.random.default_rng(N + K)
+    edges = [0, 1, 127, 128, 255, N - 129, N - 128, N - 1] + [r for r in np.cumsum(rows)[:-1]]
+    sample = np.unique(np.concatenate([rng.choice(N, 200, replace=False), np.array(edges)]))
+    ref = c_oracle.forward(bits_of(x), _sampled_groups(enc, sample), K)
+    assert_close(y[:, sample], ref)
+    yb = torch.empty((M, N), device="cuda", dtype=torch.bfloat16)
+    status = torch.zeros(1, device="cuda", dtype=torch.int32)
+    assert mod.gemm_into(x.cuda(), yb, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert_bf16_within_ulp(bits_of(yb)[:, sample], orc.f32_to_bf16_bits(ref))

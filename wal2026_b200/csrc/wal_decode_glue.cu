@@ -277,6 +277,52 @@ int grid_for(long long work, int block) {
   return (int)(g < 1 ? 1 : g);
 }
 
+// Sending half of the exchange for an output that some other kernel already
+// produced (e.g. a dense library GEMM): every pair of adjacent fp32 values of
+// rows < M becomes one 16-byte store {v0, tag, v1, tag} into every rank's
+// receive rows (as NCCL's LL protocol, each 8-byte {value, tag} half arrives
+// whole).  tag = *epoch + 1, read after the grid dependency.
+struct PushRowsParams {
+  const void* y;
+  long long ldy;
+  int y_dtype;
+  int M;
+  long long N;  // even
+  int num_ranks;
+  uint4* dst[WAL_MAX_RANKS];
+  long long ld_dst;  // words, even
+  const unsigned* epoch;
+};
+
+__global__ void __launch_bounds__(256) push_rows_kernel(const __grid_constant__ PushRowsParams p) {
+  dependency_wait();
+  const unsigned tag = *reinterpret_cast<const volatile unsigned*>(p.epoch) + 1u;
+  const long long pairs_per_row = p.N / 2, total = pairs_per_row * p.M;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int m = (int)(i / pairs_per_row);
+    const long long c = (i - (long long)m * pairs_per_row) * 2;
+    float v0, v1;
+    if (p.y_dtype == WAL_F32) {
+      const float2 v = *reinterpret_cast<const float2*>(static_cast<const float*>(p.y) + m * p.ldy + c);
+      v0 = v.x;
+      v1 = v.y;
+    } else {
+      const uint32_t b = *reinterpret_cast<const uint32_t*>(static_cast<const uint16_t*>(p.y) + m * p.ldy + c);
+      v0 = __uint_as_float(b << 16);
+      v1 = __uint_as_float(b & 0xffff0000u);
+    }
+    const long long w = (m * p.ld_dst + c) / 2;
+#pragma unroll
+    for (int r = 0; r < WAL_MAX_RANKS; ++r)
+      if (r < p.num_ranks)
+        asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};\n" ::"l"(p.dst[r] + w),
+                     "r"(__float_as_uint(v0)), "r"(tag), "r"(__float_as_uint(v1)), "r"(tag)
+                     : "memory");
+  }
+  dependents_launch();
+}
+
 }  // namespace
 
 extern "C" {
@@ -369,6 +415,32 @@ int wal_silu_mul(const uint16_t* gu, int64_t ld_gu, int64_t M, int64_t I, uint16
   if (M <= 0 || I <= 0 || ld_gu < 2 * I || ld_out < I || M > 0x7fffffff) return WAL_ERR_SHAPE;
   return launch_pdl(silu_mul_kernel, grid_for(M * I, 256), 256, 0, stream, gu, (long long)ld_gu, (int)M,
                     (long long)I, out, (long long)ld_out);
+}
+
+int wal_tp_push_rows(const void* y, int64_t ldy, int y_dtype, int64_t M, int64_t N, const wal_tp_push* push,
+                     void* stream) {
+  if (!y || !push || !push->epoch) return WAL_ERR_INVALID_ARGUMENT;
+  if (push->num_ranks < 1 || push->num_ranks > WAL_MAX_RANKS || push->rank < 0 || push->rank >= push->num_ranks)
+    return WAL_ERR_INVALID_ARGUMENT;
+  if (y_dtype != WAL_F32 && y_dtype != WAL_BF16) return WAL_ERR_UNSUPPORTED;
+  if (M <= 0 || N <= 0 || M > 0x7fffffff || ldy < N || push->ld_dst < N) return WAL_ERR_SHAPE;
+  if ((N % 2) || (ldy % 2) || (push->ld_dst % 2)) return WAL_ERR_ALIGNMENT;
+  if ((uintptr_t)y & (y_dtype == WAL_F32 ? 7 : 3)) return WAL_ERR_ALIGNMENT;
+  PushRowsParams p = {};
+  p.y = y;
+  p.ldy = ldy;
+  p.y_dtype = y_dtype;
+  p.M = (int)M;
+  p.N = N;
+  p.num_ranks = push->num_ranks;
+  for (int r = 0; r < push->num_ranks; ++r) {
+    if (!push->dst[r]) return WAL_ERR_INVALID_ARGUMENT;
+    if ((uintptr_t)push->dst[r] & 15) return WAL_ERR_ALIGNMENT;
+    p.dst[r] = static_cast<uint4*>(push->dst[r]);
+  }
+  p.ld_dst = push->ld_dst;
+  p.epoch = push->epoch;
+  return launch_pdl(push_rows_kernel, grid_for(M * (N / 2), 256), 256, 0, stream, p);
 }
 
 int wal_peer_region_create(size_t bytes, void** dev_ptr, void* handle_out) {

@@ -160,6 +160,7 @@ class _DecodeBuffers:
         self.gu = torch.empty(batch, 2 * l0.mlp, device=dev, dtype=bf)
         self.act = torch.empty(batch, l0.mlp, device=dev, dtype=bf)
         self.y32 = torch.empty(batch, s.hidden, device=dev, dtype=torch.float32)
+        self.ybf = torch.empty(batch, s.hidden, device=dev, dtype=bf)  # a dense linear's output before a push
         cache_len = stack.k_cache[0].shape[2] if stack.k_cache else 1
         self.attn_ws = decode_attention_workspace(batch, l0.hq, l0.hkv, hd, cache_len, dev)
         self.cache_len = cache_len
@@ -262,8 +263,13 @@ class LlamaStack(nn.Module):
         """h += (sum over ranks of) lin(a); x = RMSNorm(h) * norm_w."""
         eps = self.shape.eps
         if exchange == "push" and self.tp.size > 1:
-            self.exchange.push_gemv(lin, a, slot % self.exchange.SLOTS)
-            self.exchange.reduce_residual_norm(slot % self.exchange.SLOTS, bufs.h, norm_w, eps, bufs.x)
+            slot %= self.exchange.SLOTS
+            if isinstance(lin, PackedGroupedBlockRVQLinear):
+                self.exchange.push_gemv(lin, a, slot)  # the GEMV's epilogue stores the tagged words
+            else:
+                torch.matmul(a, lin.weight.t(), out=bufs.ybf)
+                self.exchange.push_rows(bufs.ybf, slot)
+            self.exchange.reduce_residual_norm(slot, bufs.h, norm_w, eps, bufs.x)
             return
         if isinstance(lin, PackedGroupedBlockRVQLinear):
             lin.gemv_into(a, bufs.y32)

@@ -217,6 +217,14 @@ class PeerExchange:
                                          _abi.stream_handle(x2.device))
         _abi.check(st, "wal_rvq_gemv_push")
 
+    def push_rows(self, y: Tensor, slot: int) -> None:
+        """Send an already computed output (fp32 or bf16 [M, width], e.g. a dense GEMM's) into `slot` on every rank."""
+        if y.shape[0] > self.max_rows or y.shape[1] != self.width or y.stride(1) != 1:
+            raise ValueError("pushed rows do not match the exchange's slot")
+        st = self._lib.wal_tp_push_rows(y.data_ptr(), y.stride(0), _abi.DTYPE_CODE[y.dtype], y.shape[0], y.shape[1],
+                                        ctypes.byref(self._pushes[slot]), _abi.stream_handle(y.device))
+        _abi.check(st, "wal_tp_push_rows")
+
     def reduce_residual_norm(self, slot: int, h: Tensor, norm_w: Tensor, eps: float, x_out: Tensor) -> None:
         """h += sum of the slot's partials (rank order); x_out = RMSNorm(h) * norm_w."""
         M, N = h.shape
