@@ -52,6 +52,18 @@ typedef enum wal_status {
 
 typedef enum wal_dtype { WAL_BF16 = 0, WAL_F32 = 1, WAL_F16 = 2 } wal_dtype;
 
+/* How the stage values become a weight (wal_rvq_layer.sum_mode).
+ * WAL_SUM_EXACT: the reference's per_group reconstruction (src/runtime.py:379-414):
+ *   w = T( T( sum_s fp32(C_s[id]) ) * T(rho) ), the stage sum in fp32 from +0.0.
+ * WAL_SUM_FAST: the reference's reconstruct_weight_fast (src/runtime.py:431-448,
+ *   :568-598), used by its *_fast and hot strategies: every stage table is
+ *   rounded to T once (times T(stage scale), rounded, when scales exist) and
+ *   the stages are added in T, in order: w = T( T(T(C_0[id]) + T(C_1[id])) * T(rho) ).
+ * T is the weight type: bf16 for bf16 activations, fp16 for fp16 ones, fp32
+ * for fp32 ones (where both modes differ only in the sign of zero sums). */
+#define WAL_SUM_EXACT 0
+#define WAL_SUM_FAST 1
+
 /* Rows per packed tile and blocks per packed chunk (layout constants). */
 #define WAL_TILE_ROWS 16
 #define WAL_CHUNK_BLOCKS 16
@@ -81,6 +93,7 @@ typedef struct wal_rvq_layer {
   const float* stage_scales;  /* fp32 [num_groups][R] per-stage scales or NULL: each */
                               /* stage value is RN(fp32(c) * scale) before the sum   */
                               /* (reference src/block_vq.py:264-268)                 */
+  int32_t sum_mode;           /* WAL_SUM_EXACT or WAL_SUM_FAST                       */
 } wal_rvq_layer;
 
 /* Human-readable text for a status code (static storage). */
@@ -141,6 +154,18 @@ WAL_API int wal_rvq_gemv(const wal_rvq_layer* layer, const uint16_t* x, int64_t 
                  void* y, int64_t ldy, int y_dtype, void* stream);
 
 /*
+ * Decode GEMV with the activation type explicit: x_dtype WAL_BF16 or WAL_F16
+ * (weights decoded and multiplied in that type, as the reference's forward in
+ * x.dtype does, src/runtime.py:1501-1507 with reconstruct_weight(x.dtype));
+ * y_dtype WAL_BF16, WAL_F16 or WAL_F32.  x_dtype WAL_F32 runs fp32 weights
+ * (w = fp32(sum) * fp32(rho)) with fp32 fused multiply-adds on the CUDA
+ * cores and needs y_dtype WAL_F32.  warps_per_tile and num_ctas as in
+ * wal_rvq_gemv_ex (0 = library default).
+ */
+WAL_API int wal_rvq_gemv_typed(const wal_rvq_layer* layer, const void* x, int x_dtype, int64_t M, int64_t ldx,
+                       void* y, int64_t ldy, int y_dtype, int warps_per_tile, int num_ctas, void* stream);
+
+/*
  * Prefill GEMM (large M): y[M, N] = x[M, K] @ w^T (+ bias) on the tcgen05
  * tensor cores.  Weight tiles are decoded exactly (same arithmetic as the
  * GEMV) into shared memory per 64-column stage; x tiles arrive by TMA.
@@ -153,6 +178,17 @@ WAL_API int wal_rvq_gemv(const wal_rvq_layer* layer, const uint16_t* x, int64_t 
  */
 WAL_API int wal_rvq_gemm(const wal_rvq_layer* layer, const uint16_t* x, int64_t M, int64_t ldx,
                  void* y, int64_t ldy, int y_dtype, int* status, void* stream);
+
+/*
+ * Prefill GEMM with the activation type explicit: x_dtype WAL_BF16 or
+ * WAL_F16 (weights decoded in that type, MMA operands of that type, fp32
+ * accumulation); y_dtype WAL_BF16, WAL_F16 or WAL_F32.  Supports the
+ * configurations of wal_rvq_gemm in both sum modes, plus one-stage tables with
+ * a stage scale and fast-mode tables with stage scales; otherwise (and for
+ * x_dtype WAL_F32) returns WAL_ERR_UNSUPPORTED.
+ */
+WAL_API int wal_rvq_gemm_typed(const wal_rvq_layer* layer, const void* x, int x_dtype, int64_t M, int64_t ldx,
+                       void* y, int64_t ldy, int y_dtype, int* status, void* stream);
 
 /*
  * Same as wal_rvq_gemv with an explicit split of each 16-row tile's blocks
@@ -169,6 +205,14 @@ WAL_API int wal_rvq_gemv_ex(const wal_rvq_layer* layer, const uint16_t* x, int64
  * (PackedGroupedBlockRVQLinear.reconstruct_weight(torch.bfloat16)).
  */
 WAL_API int wal_rvq_dequant(const wal_rvq_layer* layer, uint16_t* w, int64_t ldw, void* stream);
+
+/*
+ * The weight [N, K] in w_dtype (WAL_BF16, WAL_F16 or WAL_F32), bit-identical
+ * to reference src/runtime.py:1234-1236 reconstruct_weight(out_dtype) for
+ * WAL_SUM_EXACT and to reconstruct_weight_fast(out_dtype) (:1238-1240) for
+ * WAL_SUM_FAST.
+ */
+WAL_API int wal_rvq_dequant_typed(const wal_rvq_layer* layer, void* w, int64_t ldw, int w_dtype, void* stream);
 
 /*
  * Read the packed stream back into per-stage id matrices on the device:

@@ -85,6 +85,58 @@ def reconstruct_group_bits(
     return f32_to_bf16_bits(w_bf * rho_bf)
 
 
+def _round_to(a: np.ndarray, dtype: str) -> np.ndarray:
+    """Round float32 values to the weight type, returned as float32 values of that type."""
+    a = np.asarray(a, dtype=np.float32)
+    if dtype == "bf16":
+        return bf16_bits_to_f32(f32_to_bf16_bits(a))
+    if dtype == "f16":
+        return a.astype(np.float16).astype(np.float32)
+    return a
+
+
+def reconstruct_group_typed(stage_ids: list[np.ndarray], codebooks: list[np.ndarray], row_scale: np.ndarray,
+                            in_features: int, dtype: str = "bf16", mode: str = "exact",
+                            stage_scales: np.ndarray | None = None) -> np.ndarray:
+    """Weight values (float32 array holding ``dtype`` values) of one group.
+
+    ``mode="exact"`` restates ``reconstruct_weight(out_dtype)`` (reference
+    ``src/runtime.py:379-414``): fp32 stage sum from +0.0 (stage scales applied
+    in fp32), rounded to ``dtype``, times the ``dtype``-rounded row scale with
+    one more rounding (fp32 keeps the fp32 product).
+    ``mode="fast"`` restates ``reconstruct_weight_fast`` (``src/runtime.py:431-448``,
+    ``:568-598``): every stage table converted to ``dtype`` (times the
+    ``dtype``-rounded stage scale, rounded), the gathered stages added in
+    ``dtype`` in order starting from the first stage's value, then the row
+    scale multiply rounded to ``dtype``.  Sums and products of two bf16 or fp16
+    values are formed in float32 and rounded once, which equals the rounded
+    exact result for these types.
+    """
+    rho = _round_to(np.asarray(row_scale, dtype=np.float16).astype(np.float32).reshape(-1, 1), dtype)
+    if mode == "exact":
+        acc = stage_sum_f32(stage_ids, codebooks, stage_scales)
+        w = acc.reshape(acc.shape[0], -1)[:, :in_features]
+        return _round_to(_round_to(w, dtype) * rho, dtype)
+    if mode != "fast":
+        raise ValueError(f"unknown mode {mode!r}")
+    acc = None
+    for s, (ids, book) in enumerate(zip(stage_ids, codebooks)):
+        table = _round_to(np.asarray(book, dtype=np.float16).astype(np.float32), dtype)
+        if stage_scales is not None:
+            sc = _round_to(np.float32(np.asarray(stage_scales, dtype=np.float32).reshape(-1)[s]), dtype)
+            table = _round_to(table * sc, dtype)
+        v = table[np.asarray(ids).astype(np.int64)]
+        acc = v if acc is None else _round_to(acc + v, dtype)
+    w = acc.reshape(acc.shape[0], -1)[:, :in_features]
+    return _round_to(w * rho, dtype)
+
+
+def reconstruct_typed(groups: list[dict], in_features: int, dtype: str = "bf16", mode: str = "exact") -> np.ndarray:
+    """Concatenated group weights in ``dtype`` for either reconstruction mode (float32 values)."""
+    return np.concatenate([reconstruct_group_typed(g["stage_ids"], g["codebooks"], g["row_scale"], in_features, dtype,
+                                                   mode, g.get("stage_scales")) for g in groups], axis=0)
+
+
 def reconstruct_bits(groups: list[dict], in_features: int) -> np.ndarray:
     """Concatenate per-group weights (``PackedGroupedBlockRVQLinear.reconstruct_weight``, ``src/runtime.py:1234-1236``).
 

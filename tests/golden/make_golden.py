@@ -132,16 +132,139 @@ def run_idroute_case(name, inp, Ms, x_seed, bias, ref_runtime):
     print(f"wrote {name}.npz  w16_sha256={out['w16_sha256']}")
 
 
+def run_stage_drop_case(name, enc, k, Ms, x_seed, ref_runtime, ref_block_vq):
+    """Reference variable-stage decoding (src/runtime.py:352-377, :568-598): effective_stages_per_split = k
+    under the full_weight_fast strategy, which sums only the active stages (in bf16)."""
+    ref_enc = to_reference(enc, ref_block_vq)
+    mod = ref_runtime.PackedGroupedBlockRVQLinear(ref_enc, None, matmul_strategy="full_weight_fast")
+    n = ref_runtime.set_global_effective_stages(mod, k)
+    active = [list(g._compute_active_stage_indices()) for g in mod.groups]
+    with torch.no_grad():
+        w_full = mod.reconstruct_weight(torch.bfloat16)
+        w_fast = mod.reconstruct_weight_fast(torch.bfloat16)
+    out = {"name": np.array(name), "k": np.array(k), "groups_updated": np.array(n),
+           "N": np.array(enc.original_shape[0]), "K": np.array(enc.original_shape[1]),
+           "w_bits": bits(w_full), "w_fast_bits": bits(w_fast), "stages_per_split": np.array(
+               [list(g.stages_per_split) for g in enc.groups])}
+    for gi, (g, act) in enumerate(zip(enc.groups, active)):
+        out[f"g{gi}_active"] = np.array(act)
+        for s, (ids, book) in enumerate(zip(g.stage_ids, g.codebooks)):
+            out[f"g{gi}_ids{s}"] = ids.numpy()
+            out[f"g{gi}_book{s}"] = book.numpy()
+        out[f"g{gi}_rho"] = g.row_scale.numpy()
+    for M in Ms:
+        x = synthetic.activations(M, enc.original_shape[1], seed=x_seed)
+        with torch.no_grad():
+            y = mod(x)
+        out[f"x{M}_bits"] = bits(x)
+        out[f"y{M}_fast32"] = (x.double() @ w_fast.double().T).float().numpy()
+        out[f"y{M}_fast_bf16"] = bits(y)
+    np.savez_compressed(HERE / f"{name}.npz", **out)
+    print(f"wrote {name}.npz  active={active}")
+
+
+def f16_bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def run_dtype_case(name, enc, Ms, x_seed, bias, ref_runtime, ref_block_vq):
+    """The reference forward in float16 and float32 (src/runtime.py:1501-1507 builds the weight with
+    reconstruct_weight(x.dtype), :379-414) and its fast reconstruction (:568-598) in every dtype."""
+    ref_enc = to_reference(enc, ref_block_vq)
+    exact = ref_runtime.PackedGroupedBlockRVQLinear(ref_enc, bias, matmul_strategy="per_group")
+    fast = ref_runtime.PackedGroupedBlockRVQLinear(ref_enc, bias, matmul_strategy="full_weight_fast")
+    with torch.no_grad():
+        w16 = exact.reconstruct_weight(torch.float16)
+        w32 = exact.reconstruct_weight(torch.float32)
+        wf16 = fast.reconstruct_weight_fast(torch.float16)
+        wfb = fast.reconstruct_weight_fast(torch.bfloat16)
+        wf32 = fast.reconstruct_weight_fast(torch.float32)
+    out = {"name": np.array(name), "N": np.array(enc.original_shape[0]), "K": np.array(enc.original_shape[1]),
+           "w16_bits": f16_bits(w16), "w32": w32.numpy(), "wfast16_bits": f16_bits(wf16),
+           "wfast_bf16_bits": bits(wfb), "wfast32": wf32.numpy()}
+    for gi, g in enumerate(enc.groups):
+        for s, (ids, book) in enumerate(zip(g.stage_ids, g.codebooks)):
+            out[f"g{gi}_ids{s}"] = ids.numpy()
+            out[f"g{gi}_book{s}"] = book.numpy()
+        out[f"g{gi}_rho"] = g.row_scale.numpy()
+        if g.stage_scales is not None:
+            out[f"g{gi}_scales"] = g.stage_scales.numpy()
+    if bias is not None:
+        out["bias_bits"] = bits(bias)
+    bdouble = None if bias is None else bias.double()[None, :]
+    for M in Ms:
+        xb = synthetic.activations(M, enc.original_shape[1], seed=x_seed)
+        x16, x32 = xb.to(torch.float16), xb.to(torch.float32)
+        with torch.no_grad():
+            y16 = exact(x16)
+            y32 = exact(x32)
+            yfb = fast(xb)
+        out[f"x{M}_bits"] = bits(xb)  # x16 and x32 are exact conversions of these bf16 values
+        out[f"y{M}_f16_bits"] = f16_bits(y16)
+        out[f"y{M}_f32"] = y32.numpy()
+        r16 = x16.double() @ w16.double().T
+        r32 = x32.double() @ w32.double().T
+        rfb = xb.double() @ wfb.double().T
+        if bdouble is not None:
+            r16, r32, rfb = r16 + bdouble, r32 + bdouble, rfb + bdouble
+        out[f"y{M}_f16_ref32"] = r16.float().numpy()
+        out[f"y{M}_f32_ref64"] = r32.numpy()
+        out[f"y{M}_fast_bf16_bits"] = bits(yfb)
+        out[f"y{M}_fast_ref32"] = rfb.float().numpy()
+    np.savez_compressed(HERE / f"{name}.npz", **out)
+    print(f"wrote {name}.npz")
+
+
+def dtype_cases(ref_runtime, ref_block_vq) -> None:
+    def scaled(enc, scales_per_group):
+        groups = tuple(dataclasses.replace(g, stage_scales=torch.tensor(sc, dtype=torch.float16))
+                       for g, sc in zip(enc.groups, scales_per_group))
+        return dataclasses.replace(enc, groups=groups)
+
+    run_dtype_case("dtype_r2_d8", single_group(synthetic.rvq_encoding(48, 192, d=8, R=2, seed=41)), [1, 6], 41,
+                   synthetic.bias_vector(48, seed=41), ref_runtime, ref_block_vq)
+    run_dtype_case("dtype_scaled_grouped",
+                   scaled(synthetic.grouped_encoding([32, 16], 128, d=16, R=3, seed=42),
+                          [[1.0, 0.5, 0.333251953125], [0.9, 1.1, 0.7]]), [3], 42, None, ref_runtime, ref_block_vq)
+    run_dtype_case("dtype_route", single_group(synthetic.route_inputs(40, 96, d=16, G=4, seed=43).encoding()), [2],
+                   43, synthetic.bias_vector(40, seed=43), ref_runtime, ref_block_vq)
+    run_dtype_case("dtype_scaled_r1", scaled(single_group(synthetic.rvq_encoding(32, 64, d=8, R=1, seed=44)),
+                                             [[1.2001953125]]), [2], 44, None, ref_runtime, ref_block_vq)
+
+
+def stage_drop_cases(ref_runtime, ref_block_vq) -> None:
+    run_stage_drop_case("stage_drop_r3", single_group(synthetic.rvq_encoding(64, 192, d=8, R=3, seed=31)), 2,
+                        [1, 5], 31, ref_runtime, ref_block_vq)
+    run_stage_drop_case("stage_drop_r3_k1", synthetic.grouped_encoding([32, 48], 128, d=16, R=3, seed=32), 1,
+                        [3], 32, ref_runtime, ref_block_vq)
+    # product splits (2 splits x 2 stages, split-major), encoded by the reference's own encoder;
+    # keeping one stage per split leaves stages 0 and 2
+    torch.manual_seed(33)
+    weight = torch.randn(48, 128) * 0.02
+    ref_enc = ref_block_vq.encode_block_residual_vq(weight, block_size=8, codebook_size=256, num_stages=2,
+                                                    product_splits=2, stages_per_split=(2, 2), kmeans_iters=4)
+    ours = BlockRVQEncoding(**{f.name: getattr(ref_enc, f.name) for f in dataclasses.fields(BlockRVQEncoding)})
+    run_stage_drop_case("stage_drop_splits", single_group(ours), 1, [2], 33, ref_runtime, ref_block_vq)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
     ap.add_argument("--skip-full", action="store_true")
+    ap.add_argument("--only", default="", help="comma-separated groups to (re)generate: stage_drop, dtype")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     from src import block_vq as ref_block_vq  # type: ignore
     from src import runtime as ref_runtime  # type: ignore
 
     torch.set_num_threads(max(1, torch.get_num_threads()))
+    only = {v for v in args.only.split(",") if v}
+    if only:
+        if "stage_drop" in only:
+            stage_drop_cases(ref_runtime, ref_block_vq)
+        if "dtype" in only:
+            dtype_cases(ref_runtime, ref_block_vq)
+        return
     small = [
         ("small_r2_d8", single_group(synthetic.rvq_encoding(37, 64, d=8, R=2, seed=11)), [1, 3], 11, True),
         ("small_r1_ragged", single_group(synthetic.rvq_encoding(48, 100, d=8, R=1, C=200, seed=12)), [5], 12, False),
@@ -193,6 +316,8 @@ def main() -> None:
                      synthetic.bias_vector(40, seed=21).to(torch.float16), ref_runtime)
     run_idroute_case("idroute_medium", synthetic.idroute_inputs(256, 1024, routes=1536, seed=22), [3, 16], 22,
                      None, ref_runtime)
+    stage_drop_cases(ref_runtime, ref_block_vq)
+    dtype_cases(ref_runtime, ref_block_vq)
     if args.skip_full:
         return
     run_case("cfg0", synthetic.cfg0_encoding(0), [1, 4, 16], 0, None, ref_runtime, ref_block_vq, full=False)

@@ -31,6 +31,9 @@ WAL_BF16 = 0
 WAL_F32 = 1
 WAL_F16 = 2
 
+WAL_SUM_EXACT = 0
+WAL_SUM_FAST = 1
+
 DTYPE_CODE = {torch.bfloat16: WAL_BF16, torch.float32: WAL_F32, torch.float16: WAL_F16}
 
 # every function the header declares, with its ctypes signature
@@ -61,6 +64,7 @@ class Layer(ctypes.Structure):
         ("bias", ctypes.c_void_p),
         ("group_rows", ctypes.POINTER(ctypes.c_int64)),
         ("stage_scales", ctypes.c_void_p),
+        ("sum_mode", ctypes.c_int32),
     ]
 
 
@@ -100,6 +104,9 @@ SIGNATURES: dict[str, tuple] = {
                               ctypes.POINTER(ctypes.c_int32)]),
     "wal_route_pack": (_c_int, [_GP, _vp, _vp, _vp, ctypes.c_size_t, ctypes.POINTER(ctypes.c_int32)]),
     "wal_rvq_gemv": (_c_int, [_LP, _vp, _c_i64, _c_i64, _vp, _c_i64, _c_int, _vp]),
+    "wal_rvq_gemv_typed": (_c_int, [_LP, _vp, _c_int, _c_i64, _c_i64, _vp, _c_i64, _c_int, _c_int, _c_int, _vp]),
+    "wal_rvq_dequant_typed": (_c_int, [_LP, _vp, _c_i64, _c_int, _vp]),
+    "wal_rvq_gemm_typed": (_c_int, [_LP, _vp, _c_int, _c_i64, _c_i64, _vp, _c_i64, _c_int, _vp, _vp]),
     "wal_rvq_gemv_ex": (_c_int, [_LP, _vp, _c_i64, _c_i64, _vp, _c_i64, _c_int, _c_int, _c_int, _vp]),
     "wal_rvq_gemm": (_c_int, [_LP, _vp, _c_i64, _c_i64, _vp, _c_i64, _c_int, _vp, _vp]),
     "wal_rvq_dequant": (_c_int, [_LP, _vp, _c_i64, _vp]),

@@ -40,13 +40,14 @@ def _stale() -> bool:
 
 
 # translation units: (source, extra defines).  The GEMV source is compiled once
-# per block size so the template instantiations build in parallel.
+# per block size and weight type so the template instantiations build in
+# parallel, plus once for its C entry points.
 def units() -> list[tuple[Path, list[str]]]:
     out = []
     for src in sources():
         if src.name == "wal_rvq_gemv.cu":
             out.append((src, ["-DWAL_UNIT_API"]))
-            out += [(src, [f"-DWAL_UNIT_D={d}"]) for d in (8, 16, 32)]
+            out += [(src, [f"-DWAL_UNIT_D={d}", f"-DWAL_UNIT_T={t}"]) for t in (0, 1) for d in (8, 16, 32)]
         else:
             out.append((src, []))
     return out
@@ -61,7 +62,7 @@ def _run(cmd: list[str], verbose: bool) -> str:
     return res.stdout + res.stderr
 
 
-def build(verbose: bool = False, extra: list[str] | None = None) -> Path:
+def build(verbose: bool = False, extra: list[str] | None = None, force: bool = False) -> Path:
     from concurrent.futures import ThreadPoolExecutor
 
     objdir = PKG / "_build"
@@ -69,14 +70,29 @@ def build(verbose: bool = False, extra: list[str] | None = None) -> Path:
     common = [_nvcc(), *(extra or []), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
               "-Xcompiler", "-fvisibility=hidden", f"-I{INCLUDE}"]
     jobs = []
-    for i, (src, defs) in enumerate(units()):
-        obj = objdir / f"{src.stem}_{i}.o"
-        jobs.append((common + defs + ["-c", str(src), "-o", str(obj)], obj))
-    with ThreadPoolExecutor(max_workers=max(1, min(len(jobs), os.cpu_count() or 1))) as ex:
-        logs = list(ex.map(lambda j: _run(j[0], verbose), jobs))
+    headers = list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(INCLUDE.glob("*.h"))
+    for src, defs in units():
+        tag = "_".join(d.split("=")[-1] if "=" in d else d[2:].lower() for d in defs)
+        obj = objdir / (f"{src.stem}_{tag}.o" if tag else f"{src.stem}.o")
+        cmd = common + defs + ["-c", str(src), "-o", str(obj)]
+        stamp = obj.with_suffix(".cmd")
+        # an object is reused when it is newer than its source and every header
+        # and was built by the same command line
+        fresh = (not force and obj.exists() and stamp.exists() and stamp.read_text() == " ".join(cmd)
+                 and all(p.stat().st_mtime <= obj.stat().st_mtime for p in [src, *headers]))
+        jobs.append((cmd, obj, stamp, fresh))
+    todo = [j for j in jobs if not j[3]]
+
+    def compile_one(job):
+        out = _run(job[0], verbose)
+        job[2].write_text(" ".join(job[0]))
+        return out
+
+    with ThreadPoolExecutor(max_workers=max(1, min(len(todo) or 1, os.cpu_count() or 1))) as ex:
+        logs = list(ex.map(compile_one, todo))
     if verbose:
         print("".join(logs), file=sys.stderr)
-    link = [_nvcc(), *ARCH, "-shared", "-o", str(LIB) + ".tmp", *[str(o) for _, o in jobs], "-lcuda"]
+    link = [_nvcc(), *ARCH, "-shared", "-o", str(LIB) + ".tmp", *[str(j[1]) for j in jobs], "-lcuda"]
     _run(link, verbose)
     os.replace(str(LIB) + ".tmp", LIB)
     return LIB
@@ -89,4 +105,4 @@ def ensure_built() -> Path:
 
 
 if __name__ == "__main__":
-    print(build(verbose="-v" in sys.argv))
+    print(build(verbose="-v" in sys.argv, force="--force" in sys.argv))

@@ -11,6 +11,19 @@
 // values); for two or more stages the table holds the raw fp16 values and the
 // sum is formed with the mixed-precision add (fp16 operand converted exactly).
 //
+// Numerics modes (template parameter NUM = NM | (F16 ? 4 : 0)):
+//   NM = kExact        the sum above (reference per_group reconstruct_weight);
+//   NM = kExactScaled  the same with per-stage fp32 scales, multi-stage tables
+//                      staged as fp32 products RN(fp32(c) * scale);
+//   NM = kFast         reference reconstruct_weight_fast (src/runtime.py:568-598):
+//                      every stage table rounded to the weight type once
+//                      (times the weight-type stage scale, rounded), the
+//                      stages added in the weight type in order, then one
+//                      multiply by the row scale: w = T(T(T(c_0) + T(c_1)) * T(rho)).
+//   F16                weights, activations and MMA operands in fp16 instead of
+//                      bf16 (the reference's forward in x.dtype: .to(float16)
+//                      replaces .to(bfloat16) in every rounding above).
+//
 // Fragment convention (mma.sync m16n8k16, bf16 in, fp32 accumulate): lane
 // (r = lane/4, q = lane%4) owns, for rows r and r+8 of a 16-row tile, the four
 // consecutive physical columns 16*kt + 4q .. 4q+3 of k-tile kt.  Physical
@@ -105,6 +118,76 @@ __device__ __forceinline__ void add_f32x2(float& a0, float& a1, float b0, float 
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+constexpr int kExact = 0, kExactScaled = 1, kFast = 2;
+__host__ __device__ constexpr int num_mode(int nm, bool f16) { return nm | (f16 ? 4 : 0); }
+
+// Packed pair arithmetic in the weight type (bf16 or fp16), round-to-nearest.
+template <bool F16>
+struct WT {
+  static __device__ __forceinline__ uint32_t cvt2(float lo, float hi) {
+    uint32_t d;
+    if constexpr (F16) {
+      asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    } else {
+      asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    }
+    return d;
+  }
+  static __device__ __forceinline__ uint32_t mul2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    if constexpr (F16) {
+      asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    } else {
+      asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    }
+    return d;
+  }
+  static __device__ __forceinline__ uint32_t add2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    if constexpr (F16) {
+      asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    } else {
+      asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    }
+    return d;
+  }
+  // fp16 row scale -> both halves T(fp32(rho)) (for fp16 the value itself)
+  static __device__ __forceinline__ uint32_t rho2(uint16_t rho_bits) {
+    if constexpr (F16) {
+      return (uint32_t)rho_bits | ((uint32_t)rho_bits << 16);
+    } else {
+      return rho_pair(rho_bits);
+    }
+  }
+  // fp16 pair -> T pair of the plain conversion (sign of zero kept): the
+  // reference's codebook.to(dtype)
+  static __device__ __forceinline__ uint32_t from_f16x2(uint32_t h2) {
+    if constexpr (F16) {
+      return h2;
+    } else {
+      const __half2 h = *reinterpret_cast<const __half2*>(&h2);
+      return cvt2(__half2float(__low2half(h)), __half2float(__high2half(h)));
+    }
+  }
+  static __device__ __forceinline__ void mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    if constexpr (F16) {
+      asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+          "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+          : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+          : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    } else {
+      mma_bf16_16816(d, a, b0, b1);
+    }
+  }
+};
+
+// fp16 stage-scale bits of the fast mode: T(scale) as a pair.  The packed
+// scales are fp32 values converted exactly from the reference's fp16 buffer.
+template <bool F16>
+__device__ __forceinline__ uint32_t scale2(float sc) {
+  return WT<F16>::cvt2(sc, sc);
 }
 
 // ---------------------------------------------------------------------------
@@ -205,15 +288,41 @@ __device__ __forceinline__ void cp_async_8_zfill(uint32_t saddr, const void* gpt
 
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::); }
 
-// One-stage tables with a stage scale: the staged bf16 value is
-// bf16_rn(+0.0f + RN(fp32(c) * scale)).  Applied in place after the plain
+// One-stage tables with a stage scale: the staged value is
+// T(+0.0f + RN(fp32(c) * scale)).  Applied in place after the plain
 // staging copied the raw fp16 entries (called instead of the unscaled
 // pre-rounding).
+template <bool F16 = false>
 __device__ __forceinline__ uint32_t preround_pair_scaled(uint32_t h2, float sc) {
   const __half2 h = *reinterpret_cast<const __half2*>(&h2);
   const float lo = __fadd_rn(0.0f, __fmul_rn(__half2float(__low2half(h)), sc));
   const float hi = __fadd_rn(0.0f, __fmul_rn(__half2float(__high2half(h)), sc));
-  return pack_bf16x2_rn(lo, hi);
+  return WT<F16>::cvt2(lo, hi);
+}
+
+// First rounding of a one-stage table in the weight type: T(+0.0f + fp32(c)).
+template <bool F16>
+__device__ __forceinline__ uint32_t preround_pair_t(uint32_t h2) {
+  float lo = 0.0f, hi = 0.0f;
+  add2_f32_f16x2(lo, hi, h2);
+  return WT<F16>::cvt2(lo, hi);
+}
+
+// In-place transform of one staged 32-bit word (two fp16 entries) of stage s.
+//   exact, one stage:          first rounding (optionally after the fp32 stage scale)
+//   fast, any stage count:     T(c), times T(scale_s) rounded when scales exist
+//   exact, several stages:     raw fp16 (summed in fp32 by the decode)
+template <int R, int NM, bool F16>
+__device__ __forceinline__ uint32_t staged_word(uint32_t h2, const float* scales, int s) {
+  if constexpr (NM == kFast) {
+    uint32_t v = WT<F16>::from_f16x2(h2);
+    if (scales) v = WT<F16>::mul2(v, scale2<F16>(scales[s]));
+    return v;
+  } else if constexpr (R == 1) {
+    return scales ? preround_pair_scaled<F16>(h2, scales[0]) : preround_pair_t<F16>(h2);
+  } else {
+    return h2;
+  }
 }
 
 // Stage R codebooks of one group (fp16 [R][entries][D] in global memory) into
@@ -221,10 +330,10 @@ __device__ __forceinline__ uint32_t preround_pair_scaled(uint32_t h2, float sc) 
 //   stage_codebooks_issue  - every 16-byte run of an entry is fetched with
 //                            cp.async into its copy-0 position (not committed);
 //   stage_codebooks_finish - after the caller's cp.async wait + __syncthreads,
-//                            copy 0 is expanded into the other copies and
-//                            one-stage tables are pre-rounded to bf16 in place
-//                            (first rounding).  Follow it with __syncthreads().
-// `sb` is the byte stride between stages in shared memory.
+//                            the words are converted in place (staged_word:
+//                            pre-rounding of one-stage tables, fast-mode
+//                            tables) and copy 0 is expanded into the other
+//                            copies.  Follow it with __syncthreads().
 template <int D, int R, bool REPL>
 __device__ void stage_codebooks_issue(uint8_t* cb, const uint16_t* __restrict__ books, int entries) {
   using L = CbLayout<D, REPL>;
@@ -242,31 +351,21 @@ __device__ void stage_codebooks_issue(uint8_t* cb, const uint16_t* __restrict__ 
   }
 }
 
-template <int D, int R, bool REPL>
-__device__ void stage_codebooks_finish(uint8_t* cb, int entries, const float* scale = nullptr) {
+template <int D, int R, bool REPL, int NM = kExact, bool F16 = false>
+__device__ void stage_codebooks_finish(uint8_t* cb, int entries, const float* scales = nullptr) {
   using L = CbLayout<D, REPL>;
-  const float sc = scale ? *scale : 1.0f;  // one-stage tables only
+  constexpr bool kConvert = NM == kFast || R == 1;
   if constexpr (!REPL) {
-    if constexpr (R == 1) {  // plain one-stage table: first rounding in place
-      if (scale) {
+    if constexpr (kConvert) {
+#pragma unroll
+      for (int s = 0; s < R; ++s) {
         for (int e = threadIdx.x; e < entries; e += blockDim.x) {
 #pragma unroll
           for (int j = 0; j < L::kPieces; ++j) {
-            uint2* pv = reinterpret_cast<uint2*>(cb + L::piece_offset(0, e, j, 0, entries));
+            uint2* pv = reinterpret_cast<uint2*>(cb + L::piece_offset(s, e, j, 0, entries));
             uint2 v = *pv;
-            v.x = preround_pair_scaled(v.x, sc);
-            v.y = preround_pair_scaled(v.y, sc);
-            *pv = v;
-          }
-        }
-      } else {
-        for (int e = threadIdx.x; e < entries; e += blockDim.x) {
-#pragma unroll
-          for (int j = 0; j < L::kPieces; ++j) {
-            uint2* pv = reinterpret_cast<uint2*>(cb + L::piece_offset(0, e, j, 0, entries));
-            uint2 v = *pv;
-            v.x = preround_pair(v.x);
-            v.y = preround_pair(v.y);
+            v.x = staged_word<R, NM, F16>(v.x, scales, s);
+            v.y = staged_word<R, NM, F16>(v.y, scales, s);
             *pv = v;
           }
         }
@@ -287,18 +386,11 @@ __device__ void stage_codebooks_finish(uint8_t* cb, int entries, const float* sc
         for (int run = 0; run < kRuns; ++run) {
           const int off = D == 32 ? (run >> 1) * 128 + (run & 1) * 16 : run * 16;
           v[run] = *reinterpret_cast<const uint4*>(base + off);
-          if (R == 1) {
-            if (scale) {  // uniform branch: every thread takes the same side
-              v[run].x = preround_pair_scaled(v[run].x, sc);
-              v[run].y = preround_pair_scaled(v[run].y, sc);
-              v[run].z = preround_pair_scaled(v[run].z, sc);
-              v[run].w = preround_pair_scaled(v[run].w, sc);
-            } else {
-              v[run].x = preround_pair(v[run].x);
-              v[run].y = preround_pair(v[run].y);
-              v[run].z = preround_pair(v[run].z);
-              v[run].w = preround_pair(v[run].w);
-            }
+          if constexpr (kConvert) {
+            v[run].x = staged_word<R, NM, F16>(v[run].x, scales, s);
+            v[run].y = staged_word<R, NM, F16>(v[run].y, scales, s);
+            v[run].z = staged_word<R, NM, F16>(v[run].z, scales, s);
+            v[run].w = staged_word<R, NM, F16>(v[run].w, scales, s);
             *reinterpret_cast<uint4*>(base + off) = v[run];
           }
         }
@@ -365,17 +457,19 @@ __device__ void stage_codebooks_scaled(uint8_t* cb, const uint16_t* __restrict__
 }
 
 // One-call staging for kernels without other prologue work.
-template <int D, int R, bool REPL, bool SC = false>
+template <int D, int R, bool REPL, int NUM = 0>
 __device__ void stage_codebooks(uint8_t* cb, const uint16_t* __restrict__ books, int entries,
                                 const float* scales = nullptr) {
-  if constexpr (SC && REPL && R > 1) {
+  constexpr int NM = NUM & 3;
+  constexpr bool F16 = (NUM & 4) != 0;
+  if constexpr (NM == kExactScaled && REPL && R > 1) {
     stage_codebooks_scaled<D, R>(cb, books, scales, entries);
     return;
   }
   stage_codebooks_issue<D, R, REPL>(cb, books, entries);
   cp_async_wait_all();
   __syncthreads();
-  stage_codebooks_finish<D, R, REPL>(cb, entries, scales);
+  stage_codebooks_finish<D, R, REPL, NM, F16>(cb, entries, scales);
 }
 
 // ---------------------------------------------------------------------------
@@ -471,16 +565,19 @@ __device__ __forceinline__ uint32_t piece_addr(const uint32_t (&codes)[NW], uint
   }
 }
 
-// Decode the lane's two bf16x2 words of one row for k-tile KT:
+// Decode the lane's two weight-type words of one row for k-tile KT:
 // out[0] = columns 4q, 4q+1; out[1] = columns 4q+2, 4q+3 (both already
-// multiplied by the row scale with the second rounding).
+// multiplied by the row scale with the final rounding).
 // cb = shared codebook base, cbl = cb + this lane's offset (plain layouts).
-template <int D, int R, int IDW, bool REPL, int KT, int NW, bool SC = false>
+template <int D, int R, int IDW, bool REPL, int KT, int NW, int NUM = 0>
 __device__ __forceinline__ void decode_row(uint32_t (&out)[2], const uint32_t (&codes)[NW], uint32_t cb, uint32_t cbl,
                                            uint32_t rho2, const LaneSel& ls) {
   using L = CbLayout<D, REPL>;
+  constexpr int NM = NUM & 3;
+  constexpr bool F16 = (NUM & 4) != 0;
+  using T = WT<F16>;
   constexpr int half_off = (D == 32) ? (KT & 1) * L::kHalfStride : 0;
-  if constexpr (SC && REPL && R > 1) {  // scaled fp32 tables (LaneSel built with f32 = true)
+  if constexpr (NM == kExactScaled && REPL && R > 1) {  // scaled fp32 tables (LaneSel built with f32 = true)
     float4 t = lds128<L::stage_offset(0) + half_off>(cb + id_addr256<D, KT, 0, NW>(codes, ls));
 #pragma unroll
     for (int s = 1; s < R; ++s) {
@@ -491,12 +588,23 @@ __device__ __forceinline__ void decode_row(uint32_t (&out)[2], const uint32_t (&
       add_f32x2(t.x, t.y, u.x, u.y);
       add_f32x2(t.z, t.w, u.z, u.w);
     }
-    out[0] = mul_bf16x2_rn(pack_bf16x2_rn(t.x, t.y), rho2);
-    out[1] = mul_bf16x2_rn(pack_bf16x2_rn(t.z, t.w), rho2);
-  } else if (R == 1) {
-    const uint2 p = lds64<half_off>(piece_addr<D, R, IDW, REPL, KT, NW, 0>(codes, cb, ls, cbl));
-    out[0] = mul_bf16x2_rn(p.x, rho2);
-    out[1] = mul_bf16x2_rn(p.y, rho2);
+    out[0] = T::mul2(T::cvt2(t.x, t.y), rho2);
+    out[1] = T::mul2(T::cvt2(t.z, t.w), rho2);
+  } else if constexpr (R == 1 || NM == kFast) {
+    // tables already in the weight type: one stage is the (pre-rounded) value,
+    // the fast mode adds the stages in the weight type, in order
+    uint2 acc = lds64<L::stage_offset(0) + half_off>(piece_addr<D, R, IDW, REPL, KT, NW, 0>(codes, cb, ls, cbl));
+#pragma unroll
+    for (int s = 1; s < R; ++s) {
+      uint2 p;
+      if (s == 1) p = lds64<L::stage_offset(1) + half_off>(piece_addr<D, R, IDW, REPL, KT, NW, 1>(codes, cb, ls, cbl));
+      if (s == 2) p = lds64<L::stage_offset(2) + half_off>(piece_addr<D, R, IDW, REPL, KT, NW, 2>(codes, cb, ls, cbl));
+      if (s == 3) p = lds64<L::stage_offset(3) + half_off>(piece_addr<D, R, IDW, REPL, KT, NW, 3>(codes, cb, ls, cbl));
+      acc.x = T::add2(acc.x, p.x);
+      acc.y = T::add2(acc.y, p.y);
+    }
+    out[0] = T::mul2(acc.x, rho2);
+    out[1] = T::mul2(acc.y, rho2);
   } else {
     float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
@@ -509,8 +617,8 @@ __device__ __forceinline__ void decode_row(uint32_t (&out)[2], const uint32_t (&
       add2_f32_f16x2(s0, s1, p.x);
       add2_f32_f16x2(s2, s3, p.y);
     }
-    out[0] = mul_bf16x2_rn(pack_bf16x2_rn(s0, s1), rho2);
-    out[1] = mul_bf16x2_rn(pack_bf16x2_rn(s2, s3), rho2);
+    out[0] = T::mul2(T::cvt2(s0, s1), rho2);
+    out[1] = T::mul2(T::cvt2(s2, s3), rho2);
   }
 }
 

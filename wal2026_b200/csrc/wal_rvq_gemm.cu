@@ -57,6 +57,7 @@ constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s per wait, then giv
 struct GemmParams {
   const uint8_t* packed;
   const uint16_t* codebooks;
+  const float* stage_scales;  // fp32 [groups][R] (fast mode, or one stage) or null
   const uint16_t* row_scale;
   const uint16_t* bias;
   void* y;
@@ -127,15 +128,20 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
   return d;
 }
 
-// Instruction descriptor: kind::f16, A = B = bf16, D = f32, both K-major, M = 128, N = kBN.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) |
-                            ((uint32_t)(kUM >> 4) << 24);
+// Instruction descriptor: kind::f16, D = f32, A and B both bf16 (format 1) or
+// both fp16 (format 0), both K-major, M = 128, N = kBN.
+template <bool F16>
+__host__ __device__ constexpr uint32_t idesc() {
+  return (1u << 4) | (F16 ? 0u : (1u << 7) | (1u << 10)) | ((uint32_t)(kBN >> 3) << 17) |
+         ((uint32_t)(kUM >> 4) << 24);
+}
 
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+template <bool F16>
+__device__ __forceinline__ void umma_16bit(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n}\n"
-      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(accumulate), "r"(0u)
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc<F16>()), "r"(accumulate), "r"(0u)
       : "memory");
 }
 
@@ -158,10 +164,13 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
 
 // Decode the weights of one output row for blocks u0 .. u0 + kPartBlocks - 1
 // of a 64-column stage (d = 8) and store them, 16 bytes per block, into the
-// swizzled B buffer.  ids[st] holds the 1-byte ids of those blocks.
-template <int R>
+// swizzled B buffer.  ids[st] holds the 1-byte ids of those blocks.  Tables
+// of one stage and of the fast mode already hold weight-type values.
+template <int R, int NUM>
 __device__ __forceinline__ void decode_stage_part(uint32_t bsm_row, int nsw, const uint32_t (&ids)[R], int u0,
                                                   uint32_t cb_lane, uint32_t rho2, int k_left) {
+  using T = WT<(NUM & 4) != 0>;
+  constexpr bool kTyped = R == 1 || (NUM & 3) == kFast;
 #pragma unroll
   for (int j = 0; j < kPartBlocks; ++j) {
     const int u = u0 + j;
@@ -178,8 +187,15 @@ __device__ __forceinline__ void decode_stage_part(uint32_t bsm_row, int nsw, con
         asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
                      : "=r"(c.x), "=r"(c.y), "=r"(c.z), "=r"(c.w)
                      : "r"(cb_lane + (uint32_t)(st * 256 + id) * (kCbCopies * 16)));
-        if (R == 1) {  // one stage: the staged table is already bf16 (first rounding done)
-          w[0] = c.x; w[1] = c.y; w[2] = c.z; w[3] = c.w;
+        if (kTyped) {
+          if (st == 0) {
+            w[0] = c.x; w[1] = c.y; w[2] = c.z; w[3] = c.w;
+          } else {
+            w[0] = T::add2(w[0], c.x);
+            w[1] = T::add2(w[1], c.y);
+            w[2] = T::add2(w[2], c.z);
+            w[3] = T::add2(w[3], c.w);
+          }
         } else {
           add2_f32_f16x2(s[0], s[1], c.x);
           add2_f32_f16x2(s[2], s[3], c.y);
@@ -187,16 +203,16 @@ __device__ __forceinline__ void decode_stage_part(uint32_t bsm_row, int nsw, con
           add2_f32_f16x2(s[6], s[7], c.w);
         }
       }
-      if (R > 1) {
-        w[0] = pack_bf16x2_rn(s[0], s[1]);
-        w[1] = pack_bf16x2_rn(s[2], s[3]);
-        w[2] = pack_bf16x2_rn(s[4], s[5]);
-        w[3] = pack_bf16x2_rn(s[6], s[7]);
+      if (!kTyped) {
+        w[0] = T::cvt2(s[0], s[1]);
+        w[1] = T::cvt2(s[2], s[3]);
+        w[2] = T::cvt2(s[4], s[5]);
+        w[3] = T::cvt2(s[6], s[7]);
       }
-      o.x = mul_bf16x2_rn(w[0], rho2);
-      o.y = mul_bf16x2_rn(w[1], rho2);
-      o.z = mul_bf16x2_rn(w[2], rho2);
-      o.w = mul_bf16x2_rn(w[3], rho2);
+      o.x = T::mul2(w[0], rho2);
+      o.y = T::mul2(w[1], rho2);
+      o.z = T::mul2(w[2], rho2);
+      o.w = T::mul2(w[3], rho2);
     }
     const uint32_t addr = bsm_row + ((u ^ nsw) << 4);
     asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(o.x), "r"(o.y), "r"(o.z), "r"(o.w)
@@ -204,9 +220,12 @@ __device__ __forceinline__ void decode_stage_part(uint32_t bsm_row, int nsw, con
   }
 }
 
-template <int R>
+template <int R, int NUM>
 __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_kernel(const __grid_constant__ CUtensorMap xmap,
                                                                const __grid_constant__ GemmParams p) {
+  constexpr int NM = NUM & 3;
+  constexpr bool F16 = (NUM & 4) != 0;
+  using T = WT<F16>;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned region: [A stages][B stages][codebooks][barriers][tmem slot]
   const uint32_t raw = smem_u32(smem_raw);
@@ -254,18 +273,18 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_kernel(const __grid_cons
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  // codebooks of this group: plain [R][256][8] (one-stage tables pre-rounded to bf16)
+  // codebooks of this group: [R][256][8] x 8 copies (one-stage and fast-mode
+  // tables converted to the weight type, exactly as the GEMV stages them)
   {
     const uint16_t* books = p.codebooks + (size_t)g * R * p.entries * 8;
+    const float* scales = p.stage_scales ? p.stage_scales + (size_t)g * R : nullptr;
     for (int i = threadIdx.x; i < R * p.entries; i += kThreads) {
       const int st = i / p.entries, e = i - st * p.entries;
       uint4 v = *reinterpret_cast<const uint4*>(books + (size_t)i * 8);
-      if (R == 1) {
-        v.x = preround_pair(v.x);
-        v.y = preround_pair(v.y);
-        v.z = preround_pair(v.z);
-        v.w = preround_pair(v.w);
-      }
+      v.x = staged_word<R, NM, F16>(v.x, scales, st);
+      v.y = staged_word<R, NM, F16>(v.y, scales, st);
+      v.z = staged_word<R, NM, F16>(v.z, scales, st);
+      v.w = staged_word<R, NM, F16>(v.w, scales, st);
 #pragma unroll
       for (int c = 0; c < kCbCopies; ++c)
         *reinterpret_cast<uint4*>(cb + ((st * 256 + e) * kCbCopies + c) * 16) = v;
@@ -314,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_kernel(const __grid_cons
           for (int mt = 0; mt < kBM / kUM; ++mt) {
             if (mt >= mtiles) break;
             const uint64_t ad = smem_desc_sw128(a_sm + s * kABytes + mt * (kUM * 128) + ks * 32);
-            umma_bf16(tmem + (uint32_t)(mt * kBN), ad, bd, (kb > 0 || ks > 0) ? 1u : 0u);
+            umma_16bit<F16>(tmem + (uint32_t)(mt * kBN), ad, bd, (kb > 0 || ks > 0) ? 1u : 0u);
           }
         }
         umma_commit(empty + 8 * s);
@@ -327,7 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_kernel(const __grid_cons
     const int row = t & (kBN - 1), part = t >> 7;
     const int n = n0 + row;
     const bool row_ok = n < g_row1;
-    const uint32_t rho2 = row_ok ? rho_pair(p.row_scale[n]) : 0u;
+    const uint32_t rho2 = row_ok ? T::rho2(p.row_scale[n]) : 0u;
     const int local = n - g_row0;
     const long long tile = (long long)g_tile0 + local / 16;
     const int rr = local % 16;
@@ -361,7 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_kernel(const __grid_cons
       }
       if (abort_flag) break;
       const int k_left = row_ok ? p.K - kb * kBK : 0;
-      decode_stage_part<R>(bsm_row0 + s * kBBytes, nsw, ids0, part * kPartBlocks, cb_lane, rho2, k_left);
+      decode_stage_part<R, NUM>(bsm_row0 + s * kBBytes, nsw, ids0, part * kPartBlocks, cb_lane, rho2, k_left);
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) mbar_arrive(full_b + 8 * s);
@@ -405,17 +424,20 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_kernel(const __grid_cons
             for (int j = 0; j < 16; ++j)
               if (col0 + j < g_row1) yr[j] = f[j];
           }
-        } else {
-          __nv_bfloat16* yr = static_cast<__nv_bfloat16*>(p.y) + (long long)m * p.ldy + col0;
+        } else {  // 16-bit output: bf16 or fp16, one rounding of the fp32 sum
+          const bool yf16 = p.y_dtype == WAL_F16;
+          uint16_t* yr = static_cast<uint16_t*>(p.y) + (long long)m * p.ldy + col0;
           if (full) {
             uint32_t w[8];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) w[j] = pack_bf16x2_rn(f[2 * j], f[2 * j + 1]);
+            for (int j = 0; j < 8; ++j)
+              w[j] = yf16 ? WT<true>::cvt2(f[2 * j], f[2 * j + 1]) : WT<false>::cvt2(f[2 * j], f[2 * j + 1]);
             *reinterpret_cast<uint4*>(yr) = make_uint4(w[0], w[1], w[2], w[3]);
             *reinterpret_cast<uint4*>(yr + 8) = make_uint4(w[4], w[5], w[6], w[7]);
           } else {
             for (int j = 0; j < 16; ++j)
-              if (col0 + j < g_row1) yr[j] = __float2bfloat16_rn(f[j]);
+              if (col0 + j < g_row1)
+                yr[j] = yf16 ? __half_as_ushort(__float2half_rn(f[j])) : __bfloat16_as_ushort(__float2bfloat16_rn(f[j]));
           }
         }
       }
@@ -453,25 +475,40 @@ EncodeTiledFn encode_fn() {
 }  // namespace gemm
 }  // namespace wal
 
+using namespace wal;
 using namespace wal::gemm;
 
-extern "C" int wal_rvq_gemm(const wal_rvq_layer* layer, const uint16_t* x, int64_t M, int64_t ldx, void* y,
-                            int64_t ldy, int y_dtype, int* status, void* stream) {
+template <int R, int NUM>
+static int launch_gemm(const CUtensorMap& map, const GemmParams& p, dim3 grid, int smem, cudaStream_t s) {
+  if (cudaFuncSetAttribute(rvq_gemm_kernel<R, NUM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+      cudaSuccess)
+    return WAL_ERR_CUDA;
+  rvq_gemm_kernel<R, NUM><<<grid, kThreads, smem, s>>>(map, p);
+  return cudaGetLastError() == cudaSuccess ? WAL_OK : WAL_ERR_CUDA;
+}
+
+extern "C" int wal_rvq_gemm_typed(const wal_rvq_layer* layer, const void* x, int x_dtype, int64_t M, int64_t ldx,
+                                  void* y, int64_t ldy, int y_dtype, int* status, void* stream) {
   if (!layer || !x || !y) return WAL_ERR_INVALID_ARGUMENT;
   const wal_rvq_geometry& g = layer->geom;
   if (M <= 0 || g.out_features <= 0 || g.in_features <= 0 || layer->num_tiles <= 0) return WAL_ERR_SHAPE;
+  if (x_dtype != WAL_BF16 && x_dtype != WAL_F16) return WAL_ERR_UNSUPPORTED;  // fp32: the GEMV path
+  if (layer->sum_mode != WAL_SUM_EXACT && layer->sum_mode != WAL_SUM_FAST) return WAL_ERR_INVALID_ARGUMENT;
+  const bool fast = layer->sum_mode == WAL_SUM_FAST, f16 = x_dtype == WAL_F16;
   if (g.block_size != 8 || g.num_stages < 1 || g.num_stages > 2 || g.num_entries > 256) return WAL_ERR_UNSUPPORTED;
   if (g.num_groups < 1 || g.num_groups > 64) return WAL_ERR_UNSUPPORTED;
   if (!layer->packed_ids || !layer->codebooks || !layer->row_scale) return WAL_ERR_INVALID_ARGUMENT;
-  if (layer->stage_scales) return WAL_ERR_UNSUPPORTED;  // scaled stages: the GEMV path handles them
+  // exact multi-stage sums with fp32 stage scales: the GEMV path handles them
+  if (layer->stage_scales && g.num_stages > 1 && !fast) return WAL_ERR_UNSUPPORTED;
   if (ldx < g.in_features || ldy < g.out_features) return WAL_ERR_SHAPE;
   if ((ldx % 8) || ((uintptr_t)x & 15) || ((uintptr_t)layer->codebooks & 15) || ((uintptr_t)layer->packed_ids & 15))
     return WAL_ERR_ALIGNMENT;
-  if (y_dtype != WAL_BF16 && y_dtype != WAL_F32) return WAL_ERR_INVALID_ARGUMENT;
+  if (y_dtype != WAL_BF16 && y_dtype != WAL_F32 && y_dtype != WAL_F16) return WAL_ERR_INVALID_ARGUMENT;
   if (M > (int64_t)1 << 30 || g.in_features > (1 << 30)) return WAL_ERR_SHAPE;
   GemmParams p{};
   p.packed = static_cast<const uint8_t*>(layer->packed_ids);
   p.codebooks = layer->codebooks;
+  p.stage_scales = layer->stage_scales;
   p.row_scale = layer->row_scale;
   p.bias = layer->bias;
   p.y = y;
@@ -507,22 +544,29 @@ extern "C" int wal_rvq_gemm(const wal_rvq_layer* layer, const uint16_t* x, int64
   const cuuint64_t strides[1] = {(cuuint64_t)ldx * 2};
   const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kTmaRows};  // 64 x 256: two loads per stage
   const cuuint32_t estr[2] = {1, 1};
-  if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(x), dims, strides, box, estr,
-          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+  if (enc(&map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x),
+          dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return WAL_ERR_CUDA;
   const int R = g.num_stages;
   const int smem = smem_bytes(R);
   const dim3 grid((unsigned)((M + kBM - 1) / kBM), (unsigned)((g.out_features + kBN - 1) / kBN));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (R == 1) {
-    if (cudaFuncSetAttribute(rvq_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-      return WAL_ERR_CUDA;
-    rvq_gemm_kernel<1><<<grid, kThreads, smem, s>>>(map, p);
-  } else {
-    if (cudaFuncSetAttribute(rvq_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-      return WAL_ERR_CUDA;
-    rvq_gemm_kernel<2><<<grid, kThreads, smem, s>>>(map, p);
+  const int nm = fast ? kFast : kExact;
+  switch (R * 100 + nm * 10 + (f16 ? 1 : 0)) {
+    case 100 + kExact * 10: return launch_gemm<1, num_mode(kExact, false)>(map, p, grid, smem, s);
+    case 100 + kExact * 10 + 1: return launch_gemm<1, num_mode(kExact, true)>(map, p, grid, smem, s);
+    case 100 + kFast * 10: return launch_gemm<1, num_mode(kFast, false)>(map, p, grid, smem, s);
+    case 100 + kFast * 10 + 1: return launch_gemm<1, num_mode(kFast, true)>(map, p, grid, smem, s);
+    case 200 + kExact * 10: return launch_gemm<2, num_mode(kExact, false)>(map, p, grid, smem, s);
+    case 200 + kExact * 10 + 1: return launch_gemm<2, num_mode(kExact, true)>(map, p, grid, smem, s);
+    case 200 + kFast * 10: return launch_gemm<2, num_mode(kFast, false)>(map, p, grid, smem, s);
+    case 200 + kFast * 10 + 1: return launch_gemm<2, num_mode(kFast, true)>(map, p, grid, smem, s);
+    default: return WAL_ERR_UNSUPPORTED;
   }
-  return cudaGetLastError() == cudaSuccess ? WAL_OK : WAL_ERR_CUDA;
+}
+
+extern "C" int wal_rvq_gemm(const wal_rvq_layer* layer, const uint16_t* x, int64_t M, int64_t ldx, void* y,
+                            int64_t ldy, int y_dtype, int* status, void* stream) {
+  return wal_rvq_gemm_typed(layer, x, WAL_BF16, M, ldx, y, ldy, y_dtype, status, stream);
 }

@@ -191,12 +191,13 @@ struct GemvCfg {
 
 // col_base: the lane's first global column of the chunk (unstaged activations,
 // masking); xcol: the same column inside the staged buffer.
-template <int D, int R, int IDW, bool REPL, int MT, int XM, bool MASK, bool SC>
+template <int D, int R, int IDW, bool REPL, int MT, int XM, bool MASK, int NUM>
 __device__ __forceinline__ void gemv_chunk(float (&acc)[GemvCfg<D, R, IDW, REPL, MT, XM>::kAcc][MT][4], const uint32_t (&c0)[R * IDW * 4],
                                            const uint32_t (&c1)[R * IDW * 4], uint32_t cb, uint32_t cbl, uint32_t rho_a,
                                            uint32_t rho_b, const LaneSel& ls, const uint16_t* x, const uint32_t (&xoff)[MT],
                                            const uint32_t (&xsa)[MT], const bool (&xv)[MT], int col_base, int xcol, int K) {
   using C = GemvCfg<D, R, IDW, REPL, MT, XM>;
+  using T = WT<(NUM & 4) != 0>;
   // activations of k-tile kt, then the MMAs of the decoded fragments ra (row r), rb (row r + 8)
   auto consume = [&](auto ktc, const uint32_t (&ra)[2], const uint32_t (&rb)[2]) {
     constexpr int kt = decltype(ktc)::value;
@@ -219,9 +220,9 @@ __device__ __forceinline__ void gemv_chunk(float (&acc)[GemvCfg<D, R, IDW, REPL,
     // with one or two n-tiles, even and odd k-tiles feed separate accumulators
     // (independent MMA chains); four n-tiles are four chains already
 #pragma unroll
-    for (int i = 0; i < MT; ++i) mma_bf16_16816(acc[kt % C::kAcc][i], a, xf[i].x, xf[i].y);
+    for (int i = 0; i < MT; ++i) T::mma(acc[kt % C::kAcc][i], a, xf[i].x, xf[i].y);
   };
-  if constexpr (R == 1 && !SC) {
+  if constexpr (R == 1) {
     // one-stage tables: one gather per row and k-tile; issue the gathers of
     // eight k-tiles before using any, so their shared-memory latency overlaps
     constexpr int kGroup = 8;
@@ -236,8 +237,8 @@ __device__ __forceinline__ void gemv_chunk(float (&acc)[GemvCfg<D, R, IDW, REPL,
       });
       static_for<0, kGroup>([&](auto jc) {
         constexpr int j = decltype(jc)::value;
-        const uint32_t ra[2] = {mul_bf16x2_rn(pa[j].x, rho_a), mul_bf16x2_rn(pa[j].y, rho_a)};
-        const uint32_t rb[2] = {mul_bf16x2_rn(pb[j].x, rho_b), mul_bf16x2_rn(pb[j].y, rho_b)};
+        const uint32_t ra[2] = {T::mul2(pa[j].x, rho_a), T::mul2(pa[j].y, rho_a)};
+        const uint32_t rb[2] = {T::mul2(pb[j].x, rho_b), T::mul2(pb[j].y, rho_b)};
         consume(std::integral_constant<int, g0 + j>{}, ra, rb);
       });
     });
@@ -245,16 +246,19 @@ __device__ __forceinline__ void gemv_chunk(float (&acc)[GemvCfg<D, R, IDW, REPL,
     static_for<0, D>([&](auto ktc) {
       constexpr int kt = decltype(ktc)::value;
       uint32_t ra[2], rb[2];
-      decode_row<D, R, IDW, REPL, kt, C::NW, SC>(ra, c0, cb, cbl, rho_a, ls);
-      decode_row<D, R, IDW, REPL, kt, C::NW, SC>(rb, c1, cb, cbl, rho_b, ls);
+      decode_row<D, R, IDW, REPL, kt, C::NW, NUM>(ra, c0, cb, cbl, rho_a, ls);
+      decode_row<D, R, IDW, REPL, kt, C::NW, NUM>(rb, c1, cb, cbl, rho_b, ls);
       consume(ktc, ra, rb);
     });
   }
 }
 
-template <int D, int R, int IDW, bool REPL, int MT, int XM, bool SC>
+template <int D, int R, int IDW, bool REPL, int MT, int XM, int NUM>
 __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
     rvq_gemv_kernel(const __grid_constant__ GemvParams p) {
+  constexpr int NM = NUM & 3;
+  constexpr bool F16 = (NUM & 4) != 0;
+  using T = WT<F16>;
   using C = GemvCfg<D, R, IDW, REPL, MT, XM>;
   constexpr int kWarps = C::kW;
   constexpr int kThreads = C::kT;
@@ -276,7 +280,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
   const int ssh = 4 - wsh;                    // slots = 16 / wpt = 1 << ssh
   const int slots = 1 << ssh;
   const int slot = warp >> wsh, kpart = warp & (wpt - 1);
-  constexpr bool kF32 = SC && REPL && R > 1;  // scaled fp32 tables
+  constexpr bool kF32 = NM == kExactScaled && REPL && R > 1;  // scaled fp32 tables
   const LaneSel ls(r, q, kF32);
 
   int group, tb, te;
@@ -384,7 +388,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
   } else {
     cp_async_wait<kRing - 1>();  // codebooks landed
     __syncthreads();
-    stage_codebooks_finish<D, R, REPL>(cb, p.entries, gscales);
+    stage_codebooks_finish<D, R, REPL, NM, F16>(cb, p.entries, gscales);
   }
   if (p.pdl) grid_dependency_wait();  // x (and y) belong to the previous kernel in the stream
   const uint64_t x_pol = l2_policy_evict_last();
@@ -463,8 +467,8 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
   if (my_rounds > 0) {
     int row0, nrows;
     tile_rows(tb + slot, &row0, &nrows);
-    nrho_a = r < nrows ? rho_pair(p.row_scale[row0 + r]) : 0u;
-    nrho_b = r + 8 < nrows ? rho_pair(p.row_scale[row0 + r + 8]) : 0u;
+    nrho_a = r < nrows ? T::rho2(p.row_scale[row0 + r]) : 0u;
+    nrho_b = r + 8 < nrows ? T::rho2(p.row_scale[row0 + r + 8]) : 0u;
   }
 
   if constexpr (XM == 2) {
@@ -512,8 +516,8 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
       if (k + 1 < my_rounds) {  // prefetch the next round's row scales
         int nr0, nn;
         tile_rows(tb + slot + (k + 1) * slots, &nr0, &nn);
-        nrho_a = r < nn ? rho_pair(p.row_scale[nr0 + r]) : 0u;
-        nrho_b = r + 8 < nn ? rho_pair(p.row_scale[nr0 + r + 8]) : 0u;
+        nrho_a = r < nn ? T::rho2(p.row_scale[nr0 + r]) : 0u;
+        nrho_b = r + 8 < nn ? T::rho2(p.row_scale[nr0 + r + 8]) : 0u;
       }
     }
     if constexpr (XM == 2) {
@@ -541,7 +545,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
           uint32_t xsa_s[MT];
 #pragma unroll
           for (int i = 0; i < MT; ++i) xsa_s[i] = xb + xsa[i];
-          gemv_chunk<D, R, IDW, REPL, MT, XM, false, SC>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, p.x, xoff, xsa_s,
+          gemv_chunk<D, R, IDW, REPL, MT, XM, false, NUM>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, p.x, xoff, xsa_s,
                                                      xv, c * kChunkBlocks * D + 4 * q,
                                                      kpart * kChunkBlocks * D + 4 * q, p.K);
           ++it;
@@ -570,10 +574,10 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
         const int c = kpart + j * wpt;
         const int col_base = c * kChunkBlocks * D + 4 * q;
         if (need_mask && c == p.chunks - 1) {
-          gemv_chunk<D, R, IDW, REPL, MT, XM, true, SC>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, p.x, xoff, xsa, xv,
+          gemv_chunk<D, R, IDW, REPL, MT, XM, true, NUM>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, p.x, xoff, xsa, xv,
                                                     col_base, col_base, p.K);
         } else {
-          gemv_chunk<D, R, IDW, REPL, MT, XM, false, SC>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, p.x, xoff, xsa, xv,
+          gemv_chunk<D, R, IDW, REPL, MT, XM, false, NUM>(acc, c0, c1, cb_s, cbl, rho_a, rho_b, ls, p.x, xoff, xsa, xv,
                                                      col_base, col_base, p.K);
         }
       }
@@ -628,20 +632,21 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
 
 // Weight materialisation through the same decode path: fragments stored
 // instead of fed to the tensor cores.  One warp per tile.
-template <int D, int R, int IDW, bool REPL, bool SC>
+template <int D, int R, int IDW, bool REPL, int NUM>
 __global__ void __launch_bounds__(kThreads) rvq_dequant_kernel(const __grid_constant__ GemvParams p, uint16_t* w,
                                                                long long ldw) {
   using C = GemvCfg<D, R, IDW, REPL, 1, 0>;
+  using T = WT<(NUM & 4) != 0>;
   using L = typename C::L;
   constexpr int V = C::V;
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, q = lane & 3;
-  const LaneSel ls(r, q, SC && REPL && R > 1);
+  const LaneSel ls(r, q, (NUM & 3) == kExactScaled && REPL && R > 1);
   int group, tb, te;
   cta_range(p, blockIdx.x, &group, &tb, &te);
   if (tb >= te) return;
-  stage_codebooks<D, R, REPL, SC>(smem, p.codebooks + (size_t)group * R * p.entries * D, p.entries,
+  stage_codebooks<D, R, REPL, NUM>(smem, p.codebooks + (size_t)group * R * p.entries * D, p.entries,
                                   p.stage_scales ? p.stage_scales + (size_t)group * R : nullptr);
   __syncthreads();
   const uint32_t cb_s = smem_u32(smem);
@@ -649,8 +654,8 @@ __global__ void __launch_bounds__(kThreads) rvq_dequant_kernel(const __grid_cons
   const long long tile_bytes = (long long)p.chunks * V * 256;
   for (int t = tb + warp; t < te; t += kWarps) {
     const int4 ti = p.tiles[t];
-    const uint32_t rho_a = r < ti.z ? rho_pair(p.row_scale[ti.y + r]) : 0u;
-    const uint32_t rho_b = r + 8 < ti.z ? rho_pair(p.row_scale[ti.y + r + 8]) : 0u;
+    const uint32_t rho_a = r < ti.z ? T::rho2(p.row_scale[ti.y + r]) : 0u;
+    const uint32_t rho_b = r + 8 < ti.z ? T::rho2(p.row_scale[ti.y + r + 8]) : 0u;
     const uint8_t* tbase = p.packed + (long long)t * tile_bytes;
     for (int c = 0; c < p.chunks; ++c) {
       uint32_t c0[V * 4], c1[V * 4];
@@ -664,8 +669,8 @@ __global__ void __launch_bounds__(kThreads) rvq_dequant_kernel(const __grid_cons
       static_for<0, D>([&](auto ktc) {
         constexpr int kt = decltype(ktc)::value;
         uint32_t ra[2], rb[2];
-        decode_row<D, R, IDW, REPL, kt, C::NW, SC>(ra, c0, cb_s, cbl, rho_a, ls);
-        decode_row<D, R, IDW, REPL, kt, C::NW, SC>(rb, c1, cb_s, cbl, rho_b, ls);
+        decode_row<D, R, IDW, REPL, kt, C::NW, NUM>(ra, c0, cb_s, cbl, rho_a, ls);
+        decode_row<D, R, IDW, REPL, kt, C::NW, NUM>(rb, c1, cb_s, cbl, rho_b, ls);
         const int col = c * kChunkBlocks * D + kt * 16 + 4 * q;
         if (col < p.K) {
           if (r < ti.z) *reinterpret_cast<uint2*>(w + (long long)(ti.y + r) * ldw + col) = make_uint2(ra[0], ra[1]);
@@ -722,6 +727,7 @@ int check_layer(const wal_rvq_layer* L) {
     return WAL_ERR_UNSUPPORTED;
   if (g.in_features % 4 != 0) return WAL_ERR_UNSUPPORTED;
   if (g.num_groups > kMaxGroups) return WAL_ERR_UNSUPPORTED;
+  if (L->sum_mode != WAL_SUM_EXACT && L->sum_mode != WAL_SUM_FAST) return WAL_ERR_INVALID_ARGUMENT;
   if (!L->packed_ids || !L->tile_table || !L->codebooks || !L->row_scale) return WAL_ERR_INVALID_ARGUMENT;
   if (((uintptr_t)L->packed_ids & 15) || ((uintptr_t)L->tile_table & 15) || ((uintptr_t)L->codebooks & 15) ||
       ((uintptr_t)L->stage_scales & 3))
@@ -815,10 +821,10 @@ static int best_wpt(long long tpc, int chunks, int wmax) {
 
 static int log2_pow2(int w) { return w == 1 ? 0 : w == 2 ? 1 : w == 4 ? 2 : w == 8 ? 3 : 4; }
 
-template <int D, int R, int IDW, bool REPL, int MT, int XM, bool SC = false>
+template <int D, int R, int IDW, bool REPL, int MT, int XM, int NUM>
 static int run_gemv(GemvParams p, int num_ctas, cudaStream_t stream) {
   using C = GemvCfg<D, R, IDW, REPL, MT, XM>;
-  auto kern = rvq_gemv_kernel<D, R, IDW, REPL, MT, XM, SC>;
+  auto kern = rvq_gemv_kernel<D, R, IDW, REPL, MT, XM, NUM>;
   const int kpad = p.chunks * kChunkBlocks * D;
   int smem = C::smem(p.entries, p.M, kpad, p.wpt);
   if constexpr (XM == 2) {  // the window ring grows with wpt: choose among the splits that fit
@@ -855,10 +861,10 @@ static int run_gemv(GemvParams p, int num_ctas, cudaStream_t stream) {
   return cudaGetLastError() == cudaSuccess ? WAL_OK : WAL_ERR_CUDA;
 }
 
-template <int D, int R, int IDW, bool REPL, bool SC = false>
+template <int D, int R, int IDW, bool REPL, int NUM>
 static int run_dequant(GemvParams p, uint16_t* w, long long ldw, cudaStream_t stream) {
   using C = GemvCfg<D, R, IDW, REPL, 1, 0>;
-  auto kern = rvq_dequant_kernel<D, R, IDW, REPL, SC>;
+  auto kern = rvq_dequant_kernel<D, R, IDW, REPL, NUM>;
   const int smem = C::cb_bytes(p.entries);
   if (smem > 227 * 1024) return WAL_ERR_UNSUPPORTED;
   int grid = 0;
@@ -870,103 +876,136 @@ static int run_dequant(GemvParams p, uint16_t* w, long long ldw, cudaStream_t st
 
 // mt: n-tiles of 8 tokens per launch (1, 2 or 4); xm: activation mode
 // (1 staged whole, 2 window ring, 0 unstaged)
-template <int D, int R, int IDW, bool REPL, bool SC>
+template <int D, int R, int IDW, bool REPL, int NUM>
 static int run_mt(const GemvParams& p, int num_ctas, cudaStream_t stream, int mt, int xm) {
   if (mt == 1)
-    return xm == 1 ? run_gemv<D, R, IDW, REPL, 1, 1, SC>(p, num_ctas, stream)
-                   : xm == 2 ? run_gemv<D, R, IDW, REPL, 1, 2, SC>(p, num_ctas, stream)
-                             : run_gemv<D, R, IDW, REPL, 1, 0, SC>(p, num_ctas, stream);
+    return xm == 1 ? run_gemv<D, R, IDW, REPL, 1, 1, NUM>(p, num_ctas, stream)
+                   : xm == 2 ? run_gemv<D, R, IDW, REPL, 1, 2, NUM>(p, num_ctas, stream)
+                             : run_gemv<D, R, IDW, REPL, 1, 0, NUM>(p, num_ctas, stream);
   if (mt == 2)
-    return xm == 1 ? run_gemv<D, R, IDW, REPL, 2, 1, SC>(p, num_ctas, stream)
-                   : xm == 2 ? run_gemv<D, R, IDW, REPL, 2, 2, SC>(p, num_ctas, stream)
-                             : run_gemv<D, R, IDW, REPL, 2, 0, SC>(p, num_ctas, stream);
+    return xm == 1 ? run_gemv<D, R, IDW, REPL, 2, 1, NUM>(p, num_ctas, stream)
+                   : xm == 2 ? run_gemv<D, R, IDW, REPL, 2, 2, NUM>(p, num_ctas, stream)
+                             : run_gemv<D, R, IDW, REPL, 2, 0, NUM>(p, num_ctas, stream);
   // 32 rows of whole activations never fit
-  return xm == 2 ? run_gemv<D, R, IDW, REPL, 4, 2, SC>(p, num_ctas, stream)
-                 : xm == 0 ? run_gemv<D, R, IDW, REPL, 4, 0, SC>(p, num_ctas, stream) : WAL_ERR_UNSUPPORTED;
+  return xm == 2 ? run_gemv<D, R, IDW, REPL, 4, 2, NUM>(p, num_ctas, stream)
+                 : xm == 0 ? run_gemv<D, R, IDW, REPL, 4, 0, NUM>(p, num_ctas, stream) : WAL_ERR_UNSUPPORTED;
 }
 
-template <int D, int R, int IDW>
-static int dispatch_gemv(const GemvParams& p, int num_ctas, cudaStream_t stream, bool repl, int mt, int xm) {
+// Numerics mode of a launch: fast (stage tables rounded to the weight type and
+// accumulated in it, stage scales folded into the staged table), exact with
+// fp32 scaled multi-stage tables, or exact (one-stage tables fold their scale
+// into the pre-rounding).
+template <int D, int R, int IDW, bool F16>
+static int dispatch_gemv(const GemvParams& p, int num_ctas, cudaStream_t stream, bool repl, int mt, int xm,
+                         bool fast) {
+  constexpr int kF = F16 ? 4 : 0;
+  if (fast) {
+    if constexpr (IDW == 1) {
+      if (repl) return run_mt<D, R, IDW, true, kFast | kF>(p, num_ctas, stream, mt, xm);
+    }
+    return run_mt<D, R, IDW, false, kFast | kF>(p, num_ctas, stream, mt, xm);
+  }
   if constexpr (IDW == 1 && R > 1) {
     if (p.stage_scales) {  // scaled multi-stage tables: fp32 replicated layout only
       if (!repl) return WAL_ERR_UNSUPPORTED;
-      return run_mt<D, R, IDW, true, true>(p, num_ctas, stream, mt, xm);
+      return run_mt<D, R, IDW, true, kExactScaled | kF>(p, num_ctas, stream, mt, xm);
     }
   }
   if constexpr (IDW == 1) {
-    if (repl) return run_mt<D, R, IDW, true, false>(p, num_ctas, stream, mt, xm);
+    if (repl) return run_mt<D, R, IDW, true, kExact | kF>(p, num_ctas, stream, mt, xm);
   }
-  return run_mt<D, R, IDW, false, false>(p, num_ctas, stream, mt, xm);
+  return run_mt<D, R, IDW, false, kExact | kF>(p, num_ctas, stream, mt, xm);
 }
 
-template <int D, int R, int IDW>
-static int dispatch_dequant(const GemvParams& p, uint16_t* w, long long ldw, cudaStream_t stream, bool repl) {
+template <int D, int R, int IDW, bool F16>
+static int dispatch_dequant(const GemvParams& p, uint16_t* w, long long ldw, cudaStream_t stream, bool repl,
+                            bool fast) {
+  constexpr int kF = F16 ? 4 : 0;
+  if (fast) {
+    if constexpr (IDW == 1) {
+      if (repl) return run_dequant<D, R, IDW, true, kFast | kF>(p, w, ldw, stream);
+    }
+    return run_dequant<D, R, IDW, false, kFast | kF>(p, w, ldw, stream);
+  }
   if constexpr (IDW == 1 && R > 1) {
     if (p.stage_scales) {
       if (!repl) return WAL_ERR_UNSUPPORTED;
-      return run_dequant<D, R, IDW, true, true>(p, w, ldw, stream);
+      return run_dequant<D, R, IDW, true, kExactScaled | kF>(p, w, ldw, stream);
     }
   }
   if constexpr (IDW == 1) {
-    if (repl) return run_dequant<D, R, IDW, true>(p, w, ldw, stream);
+    if (repl) return run_dequant<D, R, IDW, true, kExact | kF>(p, w, ldw, stream);
   }
-  return run_dequant<D, R, IDW, false>(p, w, ldw, stream);
+  return run_dequant<D, R, IDW, false, kExact | kF>(p, w, ldw, stream);
 }
 
-// Per-block-size dispatchers.  Each block size is compiled in its own
-// translation unit (the build passes -DWAL_UNIT_D=8/16/32) so the kernel
-// instantiations build in parallel; the C entry points are in the unit built
-// with -DWAL_UNIT_API.
-int wal_gemv_dispatch_d8(const GemvParams&, int, cudaStream_t, int, int, bool, int, int);
-int wal_gemv_dispatch_d16(const GemvParams&, int, cudaStream_t, int, int, bool, int, int);
-int wal_gemv_dispatch_d32(const GemvParams&, int, cudaStream_t, int, int, bool, int, int);
-int wal_dequant_dispatch_d8(const GemvParams&, uint16_t*, long long, cudaStream_t, int, int, bool);
-int wal_dequant_dispatch_d16(const GemvParams&, uint16_t*, long long, cudaStream_t, int, int, bool);
-int wal_dequant_dispatch_d32(const GemvParams&, uint16_t*, long long, cudaStream_t, int, int, bool);
+// Per-(block size, weight type) dispatchers.  Each pair is compiled in its own
+// translation unit (the build passes -DWAL_UNIT_D=8/16/32 and -DWAL_UNIT_T=0
+// for bf16, 1 for fp16) so the kernel instantiations build in parallel; the C
+// entry points are in the unit built with -DWAL_UNIT_API.
+#define WAL_DECLARE_UNIT(d, t)                                                                                    \
+  int wal_gemv_dispatch_d##d##_t##t(const GemvParams&, int, cudaStream_t, int, int, bool, int, int, bool);       \
+  int wal_dequant_dispatch_d##d##_t##t(const GemvParams&, uint16_t*, long long, cudaStream_t, int, int, bool, bool);
+// fp32 activations and weights (CUDA cores), in wal_rvq_f32.cu
+int wal_rvq_gemv_f32_impl(const wal_rvq_layer* layer, const float* x, int64_t M, int64_t ldx, float* y, int64_t ldy,
+                          cudaStream_t stream);
+int wal_rvq_dequant_f32_impl(const wal_rvq_layer* layer, float* w, int64_t ldw, cudaStream_t stream);
+WAL_DECLARE_UNIT(8, 0)
+WAL_DECLARE_UNIT(16, 0)
+WAL_DECLARE_UNIT(32, 0)
+WAL_DECLARE_UNIT(8, 1)
+WAL_DECLARE_UNIT(16, 1)
+WAL_DECLARE_UNIT(32, 1)
 
 #ifdef WAL_UNIT_D
-#define WAL_CAT2(a, b) a##b
-#define WAL_CAT(a, b) WAL_CAT2(a, b)
-int WAL_CAT(wal_gemv_dispatch_d, WAL_UNIT_D)(const GemvParams& p, int num_ctas, cudaStream_t s, int R, int idw,
-                                             bool repl, int mt, int xs) {
+#define WAL_CAT2(a, b, c, d) a##b##c##d
+#define WAL_CAT(a, b, c, d) WAL_CAT2(a, b, c, d)
+int WAL_CAT(wal_gemv_dispatch_d, WAL_UNIT_D, _t, WAL_UNIT_T)(const GemvParams& p, int num_ctas, cudaStream_t s, int R,
+                                                            int idw, bool repl, int mt, int xs, bool fast) {
   constexpr int D = WAL_UNIT_D;
+  constexpr bool F16 = WAL_UNIT_T != 0;
   switch (R * 10 + idw) {
-    case 11: return dispatch_gemv<D, 1, 1>(p, num_ctas, s, repl, mt, xs);
-    case 12: return dispatch_gemv<D, 1, 2>(p, num_ctas, s, repl, mt, xs);
-    case 21: return dispatch_gemv<D, 2, 1>(p, num_ctas, s, repl, mt, xs);
-    case 31: return dispatch_gemv<D, 3, 1>(p, num_ctas, s, repl, mt, xs);
-    case 41: return dispatch_gemv<D, 4, 1>(p, num_ctas, s, repl, mt, xs);
+    case 11: return dispatch_gemv<D, 1, 1, F16>(p, num_ctas, s, repl, mt, xs, fast);
+    case 12: return dispatch_gemv<D, 1, 2, F16>(p, num_ctas, s, repl, mt, xs, fast);
+    case 21: return dispatch_gemv<D, 2, 1, F16>(p, num_ctas, s, repl, mt, xs, fast);
+    case 31: return dispatch_gemv<D, 3, 1, F16>(p, num_ctas, s, repl, mt, xs, fast);
+    case 41: return dispatch_gemv<D, 4, 1, F16>(p, num_ctas, s, repl, mt, xs, fast);
     default: return WAL_ERR_UNSUPPORTED;
   }
 }
-int WAL_CAT(wal_dequant_dispatch_d, WAL_UNIT_D)(const GemvParams& p, uint16_t* w, long long ldw, cudaStream_t s,
-                                                int R, int idw, bool repl) {
+int WAL_CAT(wal_dequant_dispatch_d, WAL_UNIT_D, _t, WAL_UNIT_T)(const GemvParams& p, uint16_t* w, long long ldw,
+                                                               cudaStream_t s, int R, int idw, bool repl, bool fast) {
   constexpr int D = WAL_UNIT_D;
+  constexpr bool F16 = WAL_UNIT_T != 0;
   switch (R * 10 + idw) {
-    case 11: return dispatch_dequant<D, 1, 1>(p, w, ldw, s, repl);
-    case 12: return dispatch_dequant<D, 1, 2>(p, w, ldw, s, repl);
-    case 21: return dispatch_dequant<D, 2, 1>(p, w, ldw, s, repl);
-    case 31: return dispatch_dequant<D, 3, 1>(p, w, ldw, s, repl);
-    case 41: return dispatch_dequant<D, 4, 1>(p, w, ldw, s, repl);
+    case 11: return dispatch_dequant<D, 1, 1, F16>(p, w, ldw, s, repl, fast);
+    case 12: return dispatch_dequant<D, 1, 2, F16>(p, w, ldw, s, repl, fast);
+    case 21: return dispatch_dequant<D, 2, 1, F16>(p, w, ldw, s, repl, fast);
+    case 31: return dispatch_dequant<D, 3, 1, F16>(p, w, ldw, s, repl, fast);
+    case 41: return dispatch_dequant<D, 4, 1, F16>(p, w, ldw, s, repl, fast);
     default: return WAL_ERR_UNSUPPORTED;
   }
 }
 #endif  // WAL_UNIT_D
 
 #ifdef WAL_UNIT_API
-static int gemv_by_d(int d, const GemvParams& p, int num_ctas, cudaStream_t s, int R, int idw, bool repl, int mt,
-                     int xs) {
-  if (d == 8) return wal_gemv_dispatch_d8(p, num_ctas, s, R, idw, repl, mt, xs);
-  if (d == 16) return wal_gemv_dispatch_d16(p, num_ctas, s, R, idw, repl, mt, xs);
-  if (d == 32) return wal_gemv_dispatch_d32(p, num_ctas, s, R, idw, repl, mt, xs);
+static int gemv_by_d(int d, bool f16, const GemvParams& p, int num_ctas, cudaStream_t s, int R, int idw, bool repl,
+                     int mt, int xs, bool fast) {
+  if (d == 8) return (f16 ? wal_gemv_dispatch_d8_t1 : wal_gemv_dispatch_d8_t0)(p, num_ctas, s, R, idw, repl, mt, xs, fast);
+  if (d == 16)
+    return (f16 ? wal_gemv_dispatch_d16_t1 : wal_gemv_dispatch_d16_t0)(p, num_ctas, s, R, idw, repl, mt, xs, fast);
+  if (d == 32)
+    return (f16 ? wal_gemv_dispatch_d32_t1 : wal_gemv_dispatch_d32_t0)(p, num_ctas, s, R, idw, repl, mt, xs, fast);
   return WAL_ERR_UNSUPPORTED;
 }
 
-static int dequant_by_d(int d, const GemvParams& p, uint16_t* w, long long ldw, cudaStream_t s, int R, int idw,
-                        bool repl) {
-  if (d == 8) return wal_dequant_dispatch_d8(p, w, ldw, s, R, idw, repl);
-  if (d == 16) return wal_dequant_dispatch_d16(p, w, ldw, s, R, idw, repl);
-  if (d == 32) return wal_dequant_dispatch_d32(p, w, ldw, s, R, idw, repl);
+static int dequant_by_d(int d, bool f16, const GemvParams& p, uint16_t* w, long long ldw, cudaStream_t s, int R,
+                        int idw, bool repl, bool fast) {
+  if (d == 8) return (f16 ? wal_dequant_dispatch_d8_t1 : wal_dequant_dispatch_d8_t0)(p, w, ldw, s, R, idw, repl, fast);
+  if (d == 16)
+    return (f16 ? wal_dequant_dispatch_d16_t1 : wal_dequant_dispatch_d16_t0)(p, w, ldw, s, R, idw, repl, fast);
+  if (d == 32)
+    return (f16 ? wal_dequant_dispatch_d32_t1 : wal_dequant_dispatch_d32_t0)(p, w, ldw, s, R, idw, repl, fast);
   return WAL_ERR_UNSUPPORTED;
 }
 
@@ -989,12 +1028,22 @@ static int make_params(const wal_rvq_layer* L, GemvParams* p) {
 
 // Shared body of the GEMV entry points; push == NULL writes y, otherwise the
 // fp32 rows go to every rank's receive rows (y, ldy, y_dtype unused).
-static int gemv_common(const wal_rvq_layer* layer, const uint16_t* x, int64_t M, int64_t ldx, void* y, int64_t ldy,
-                       int y_dtype, int warps_per_tile, int num_ctas, const wal_tp_push* push, void* stream) {
+static int gemv_common(const wal_rvq_layer* layer, const void* xv, int x_dtype, int64_t M, int64_t ldx, void* y,
+                       int64_t ldy, int y_dtype, int warps_per_tile, int num_ctas, const wal_tp_push* push,
+                       void* stream) {
   int st = check_layer(layer);
   if (st != WAL_OK) return st;
-  if (!x || (!y && !push)) return WAL_ERR_INVALID_ARGUMENT;
+  if (!xv || (!y && !push)) return WAL_ERR_INVALID_ARGUMENT;
   if (M <= 0) return WAL_ERR_SHAPE;
+  if (x_dtype == WAL_F32) {  // fp32 activations: CUDA-core kernel with fp32 weights
+    if (push) return WAL_ERR_UNSUPPORTED;
+    if (y_dtype != WAL_F32) return WAL_ERR_INVALID_ARGUMENT;
+    return wal_rvq_gemv_f32_impl(layer, static_cast<const float*>(xv), M, ldx, static_cast<float*>(y), ldy,
+                                 static_cast<cudaStream_t>(stream));
+  }
+  if (x_dtype != WAL_BF16 && x_dtype != WAL_F16) return WAL_ERR_INVALID_ARGUMENT;
+  const bool f16 = x_dtype == WAL_F16, fast = layer->sum_mode == WAL_SUM_FAST;
+  const uint16_t* x = static_cast<const uint16_t*>(xv);
   const wal_rvq_geometry& g = layer->geom;
   if (push) {
     if (push->num_ranks < 1 || push->num_ranks > WAL_MAX_RANKS || push->rank < 0 || push->rank >= push->num_ranks)
@@ -1063,9 +1112,9 @@ static int gemv_common(const wal_rvq_layer* layer, const uint16_t* x, int64_t M,
     // whole activations when small, else the window ring, else (shared memory
     // taken by a large codebook) unstaged reads
     int xm = mt < 4 && (long long)mm * kpad * 2 <= kXSmemBudget ? 1 : 2;
-    int rs = gemv_by_d(d, p, num_ctas, s, R, idw, repl, mt, xm);
-    if (rs == WAL_ERR_UNSUPPORTED && xm == 1) rs = gemv_by_d(d, p, num_ctas, s, R, idw, repl, mt, xm = 2);
-    if (rs == WAL_ERR_UNSUPPORTED && xm == 2) rs = gemv_by_d(d, p, num_ctas, s, R, idw, repl, mt, 0);
+    int rs = gemv_by_d(d, f16, p, num_ctas, s, R, idw, repl, mt, xm, fast);
+    if (rs == WAL_ERR_UNSUPPORTED && xm == 1) rs = gemv_by_d(d, f16, p, num_ctas, s, R, idw, repl, mt, xm = 2, fast);
+    if (rs == WAL_ERR_UNSUPPORTED && xm == 2) rs = gemv_by_d(d, f16, p, num_ctas, s, R, idw, repl, mt, 0, fast);
     if (rs == WAL_ERR_UNSUPPORTED && mt > 1) {
       cap = mt == 4 ? 16 : 8;
       continue;
@@ -1076,28 +1125,38 @@ static int gemv_common(const wal_rvq_layer* layer, const uint16_t* x, int64_t M,
   return WAL_OK;
 }
 
+extern "C" int wal_rvq_gemv_typed(const wal_rvq_layer* layer, const void* x, int x_dtype, int64_t M, int64_t ldx,
+                                  void* y, int64_t ldy, int y_dtype, int warps_per_tile, int num_ctas, void* stream) {
+  return gemv_common(layer, x, x_dtype, M, ldx, y, ldy, y_dtype, warps_per_tile, num_ctas, nullptr, stream);
+}
+
 extern "C" int wal_rvq_gemv_ex(const wal_rvq_layer* layer, const uint16_t* x, int64_t M, int64_t ldx, void* y,
                                int64_t ldy, int y_dtype, int warps_per_tile, int num_ctas, void* stream) {
-  return gemv_common(layer, x, M, ldx, y, ldy, y_dtype, warps_per_tile, num_ctas, nullptr, stream);
+  return gemv_common(layer, x, WAL_BF16, M, ldx, y, ldy, y_dtype, warps_per_tile, num_ctas, nullptr, stream);
 }
 
 extern "C" int wal_rvq_gemv(const wal_rvq_layer* layer, const uint16_t* x, int64_t M, int64_t ldx, void* y,
                             int64_t ldy, int y_dtype, void* stream) {
-  return gemv_common(layer, x, M, ldx, y, ldy, y_dtype, 0, 0, nullptr, stream);
+  return gemv_common(layer, x, WAL_BF16, M, ldx, y, ldy, y_dtype, 0, 0, nullptr, stream);
 }
 
 extern "C" int wal_rvq_gemv_push(const wal_rvq_layer* layer, const uint16_t* x, int64_t M, int64_t ldx,
                                  const wal_tp_push* push, void* stream) {
   if (!push) return WAL_ERR_INVALID_ARGUMENT;
-  return gemv_common(layer, x, M, ldx, nullptr, 0, WAL_F32, 0, 0, push, stream);
+  return gemv_common(layer, x, WAL_BF16, M, ldx, nullptr, 0, WAL_F32, 0, 0, push, stream);
 }
 
-extern "C" int wal_rvq_dequant(const wal_rvq_layer* layer, uint16_t* w, int64_t ldw, void* stream) {
+extern "C" int wal_rvq_dequant_typed(const wal_rvq_layer* layer, void* w, int64_t ldw, int w_dtype, void* stream) {
   int st = check_layer(layer);
   if (st != WAL_OK) return st;
   if (!w) return WAL_ERR_INVALID_ARGUMENT;
   const wal_rvq_geometry& g = layer->geom;
   if (ldw < g.in_features) return WAL_ERR_SHAPE;
+  if (w_dtype == WAL_F32) {
+    if ((uintptr_t)w & 3) return WAL_ERR_ALIGNMENT;
+    return wal_rvq_dequant_f32_impl(layer, static_cast<float*>(w), ldw, static_cast<cudaStream_t>(stream));
+  }
+  if (w_dtype != WAL_BF16 && w_dtype != WAL_F16) return WAL_ERR_INVALID_ARGUMENT;
   if ((ldw % 4) || ((uintptr_t)w & 7)) return WAL_ERR_ALIGNMENT;
   const int d = g.block_size, R = g.num_stages, idw = g.num_entries <= 256 ? 1 : 2;
   const bool repl = replicated(d, R, g.num_entries);
@@ -1106,7 +1165,12 @@ extern "C" int wal_rvq_dequant(const wal_rvq_layer* layer, uint16_t* w, int64_t 
   if (st != WAL_OK) return st;
   p.wpt = 1;
   p.wpt_shift = 0;
-  return dequant_by_d(d, p, w, ldw, static_cast<cudaStream_t>(stream), R, idw, repl);
+  return dequant_by_d(d, w_dtype == WAL_F16, p, static_cast<uint16_t*>(w), ldw, static_cast<cudaStream_t>(stream), R,
+                      idw, repl, layer->sum_mode == WAL_SUM_FAST);
+}
+
+extern "C" int wal_rvq_dequant(const wal_rvq_layer* layer, uint16_t* w, int64_t ldw, void* stream) {
+  return wal_rvq_dequant_typed(layer, w, ldw, WAL_BF16, stream);
 }
 
 extern "C" int wal_rvq_unpack_ids(const wal_rvq_layer* layer, void* ids, void* stream) {

@@ -35,6 +35,20 @@ MATMUL_STRATEGIES = frozenset({
     "triton_block_rvq", "stacked_matmul",
 })
 
+# strategies built on the reference's fast reconstruction
+# (``reconstruct_weight_fast`` / ``_hot`` / ``_hot_v2``, src/runtime.py:568-798,
+# and the hot-cold Triton paths whose CPU forms call them): stage tables
+# rounded to the weight type and summed in it, and only the active stages of
+# ``effective_stages_per_split`` (``_compute_active_stage_indices`` at
+# src/runtime.py:588, :612, :663, :755, :930, :1045).  The others (per_group,
+# full_weight, chunked_weight, local_palette, stagewise_einsum,
+# triton_block_rvq, stacked_matmul) build the exact per_group weight from every
+# stage whatever the setting.
+FAST_STRATEGIES = frozenset({
+    "per_group_fast", "full_weight_fast", "full_weight_hot", "full_weight_hot_v2", "triton_hot_cold_persistent",
+    "stage_local_hot_cold", "stage_local_hot_cold_b1", "stage_local_hot_cold_b2", "stage_local_hot_cold_b3",
+})
+
 # token count from which the forward uses the tensor-core prefill GEMM
 PREFILL_MIN_TOKENS = 128
 
@@ -90,12 +104,45 @@ class PackedBlockRVQGroup(nn.Module):
         self.residual_correction = "none" if enc is None else enc.residual_correction
         self.row0, self.row1 = int(row0), int(row1)
         self._parent = weakref.ref(parent)
+        # variable-stage decoding (reference src/runtime.py:320-323, :352-377):
+        # keep the first k stages of every product split
+        self.effective_stages_per_split: int = max(self.stages_per_split) if self.stages_per_split \
+            else self.num_stages
+        self._active_stage_indices: Optional[tuple[int, ...]] = None
+
+    def _compute_active_stage_indices(self) -> tuple[int, ...]:
+        """Stage indices summed under ``effective_stages_per_split`` (reference ``src/runtime.py:352-372``).
+
+        Stages are stored split-major (split 0's stages, then split 1's, ...);
+        the first ``k`` stages of every split are kept, at least one stage in all.
+        """
+        if self._active_stage_indices is not None:
+            return self._active_stage_indices
+        keep = max(1, int(self.effective_stages_per_split))
+        idxs: list[int] = []
+        offset = 0
+        for count in self.stages_per_split:
+            idxs.extend(offset + j for j in range(min(keep, int(count))))
+            offset += int(count)
+        self._active_stage_indices = tuple(idxs) if idxs else (0,)
+        return self._active_stage_indices
+
+    def set_effective_stages_per_split(self, k: int) -> None:
+        """Set the per-split active stage count (reference ``src/runtime.py:374-377``)."""
+        self.effective_stages_per_split = int(k)
+        self._active_stage_indices = None
 
     def reconstruct_weight(self, out_dtype: torch.dtype = torch.bfloat16) -> Tensor:
         parent = self._parent()
         if parent is None:
             raise RuntimeError("group outlived its packed linear")
         return parent.reconstruct_weight(out_dtype)[self.row0:self.row1]
+
+    def reconstruct_weight_fast(self, out_dtype: torch.dtype = torch.bfloat16) -> Tensor:
+        parent = self._parent()
+        if parent is None:
+            raise RuntimeError("group outlived its packed linear")
+        return parent.reconstruct_weight_fast(out_dtype)[self.row0:self.row1]
 
 
 class PackedGroupedBlockRVQLinear(nn.Module):
@@ -256,22 +303,74 @@ class PackedGroupedBlockRVQLinear(nn.Module):
         return [r1 - r0 for r0, r1 in self.row_slices]
 
     # -- C ABI plumbing -----------------------------------------------------
-    def layer_struct(self) -> _abi.Layer:
-        """The ``wal_rvq_layer`` descriptor of this module's current device buffers."""
-        key = (self.packed_ids.data_ptr(), self.tile_table.data_ptr(), self.codebooks.data_ptr(),
+    def _active_stages(self) -> Optional[tuple[tuple[int, ...], ...]]:
+        """Per-group active stage indices when this strategy drops stages, else None (all stages)."""
+        if self.matmul_strategy not in FAST_STRATEGIES:
+            return None
+        active = tuple(g._compute_active_stage_indices() for g in self.groups)
+        full = tuple(range(self.num_stages))
+        return None if all(a == full for a in active) else active
+
+    def _stage_view(self, active: tuple[tuple[int, ...], ...]) -> tuple:
+        """Packed stream, codebooks and stage scales holding only the union of the active stages.
+
+        Cut from this module's device buffers (the packed stream keeps whole
+        16-byte stage vectors, so the cut is a selection of vectors per
+        chunk): the GEMV then streams only the active stages' ids.  A stage
+        of the union that a group does not keep gets an all-zero codebook in
+        that group; adding +0.0 to the fp32 stage sum changes no bit (the sum
+        starts from +0.0, so it is never -0.0).  Cached per active set.
+        """
+        key = (active, self.packed_ids.data_ptr(), self.codebooks.data_ptr())
+        cache = getattr(self, "_stage_cache", None)
+        if cache is not None and cache[0] == key:
+            return cache[1]
+        union = sorted(set().union(*active))
+        idw = 1 if self.num_entries <= 256 else 2
+        blocks = -(-self.in_features // self.block_size)
+        chunks = -(-blocks // 16)
+        V = self.num_stages * idw
+        vec = torch.tensor([s * idw + h for s in union for h in range(idw)], device=self.packed_ids.device)
+        packed = self.packed_ids.view(self.num_tiles * chunks, V, 256).index_select(1, vec).reshape(-1).contiguous()
+        books = self.codebooks[:, union].clone()
+        for g, act in enumerate(active):
+            for j, st in enumerate(union):
+                if st not in act:
+                    books[g, j].zero_()
+        scales = None if self.stage_scales is None else self.stage_scales[:, union].contiguous()
+        view = (len(union), packed, books.contiguous(), scales)
+        self._stage_cache = (key, view)
+        return view
+
+    def sum_mode(self) -> int:
+        """``WAL_SUM_FAST`` for the strategies built on the reference's fast reconstruction, else exact."""
+        return _abi.WAL_SUM_FAST if self.matmul_strategy in FAST_STRATEGIES else _abi.WAL_SUM_EXACT
+
+    def layer_struct(self, stages: Optional[tuple[tuple[int, ...], ...]] = None,
+                     sum_mode: int = _abi.WAL_SUM_EXACT) -> _abi.Layer:
+        """The ``wal_rvq_layer`` descriptor of this module's current device buffers.
+
+        ``stages``: per-group active stage indices (``_active_stages()``); the
+        descriptor then points at the stage view holding only those stages.
+        ``sum_mode``: how stage values become a weight (``WAL_SUM_*``).
+        """
+        R, packed, books, scales = self.num_stages, self.packed_ids, self.codebooks, self.stage_scales
+        if stages is not None:
+            R, packed, books, scales = self._stage_view(stages)
+        key = (R, packed.data_ptr(), self.tile_table.data_ptr(), books.data_ptr(),
                self.row_scale.data_ptr(), None if self.bias is None else self.bias.data_ptr(),
-               None if self.stage_scales is None else self.stage_scales.data_ptr())
+               None if scales is None else scales.data_ptr(), int(sum_mode))
         if self._layer_cache is not None and self._layer_cache[0] == key:
             return self._layer_cache[1]
         geom = _abi.Geometry(out_features=self.out_features, in_features=self.in_features,
-                             block_size=self.block_size, num_stages=self.num_stages,
+                             block_size=self.block_size, num_stages=R,
                              num_entries=self.num_entries, num_groups=self.num_groups)
         rows = [r1 - r0 for r0, r1 in self.row_slices]
         self._group_rows = (ctypes.c_int64 * len(rows))(*rows)  # kept alive with the descriptor
-        layer = _abi.Layer(geom=geom, num_tiles=self.num_tiles, packed_ids=key[0], tile_table=key[1],
-                           codebooks=key[2], row_scale=key[3], bias=key[4],
+        layer = _abi.Layer(geom=geom, num_tiles=self.num_tiles, packed_ids=key[1], tile_table=key[2],
+                           codebooks=key[3], row_scale=key[4], bias=key[5],
                            group_rows=ctypes.cast(self._group_rows, ctypes.POINTER(ctypes.c_int64)),
-                           stage_scales=key[5])
+                           stage_scales=key[6], sum_mode=key[7])
         self._layer_cache = (key, layer)
         return layer
 
@@ -284,23 +383,33 @@ class PackedGroupedBlockRVQLinear(nn.Module):
 
     # -- public API ---------------------------------------------------------
     def forward(self, x: Tensor) -> Tensor:
+        """y = x @ w^T (+ bias) in ``x.dtype`` (bf16, fp16 or fp32), as the reference forward.
+
+        The weight is decoded in ``x.dtype`` with the reference's roundings
+        for this strategy (``reconstruct_weight`` for per_group and the other
+        exact strategies, ``reconstruct_weight_fast`` for the fast ones) and
+        never materialised; products accumulate in fp32.
+        """
         self._require_cuda(x)
-        if x.dtype != torch.bfloat16:
-            raise ValueError(f"PackedGroupedBlockRVQLinear expects bfloat16 activations, got {x.dtype}")
+        if x.dtype not in _abi.DTYPE_CODE:
+            raise ValueError(f"PackedGroupedBlockRVQLinear supports bfloat16, float16 and float32 activations, "
+                             f"got {x.dtype}")
         orig = x.shape
         if orig[-1] != self.in_features:
             raise ValueError(f"Feature mismatch: {orig[-1]} != {self.in_features}")
         x2 = x.reshape(-1, self.in_features)
-        if x2.stride(-1) != 1 or x2.stride(0) % 8 != 0 or x2.data_ptr() % 16 != 0:
-            if self.in_features % 8 == 0:
+        align = 4 if x.dtype == torch.float32 else 8  # elements per 16 bytes
+        if x2.stride(-1) != 1 or x2.stride(0) % align != 0 or x2.data_ptr() % 16 != 0:
+            if self.in_features % align == 0:
                 x2 = x2.contiguous()
-            else:  # pad rows to a multiple of 8 elements so every row starts 16-byte aligned
-                xp = torch.zeros((x2.shape[0], -(-self.in_features // 8) * 8), device=x.device, dtype=x.dtype)
+            else:  # pad rows so every row starts 16-byte aligned
+                xp = torch.zeros((x2.shape[0], -(-self.in_features // align) * align), device=x.device,
+                                 dtype=x.dtype)
                 xp[:, :self.in_features] = x2
                 x2 = xp
         M = x2.shape[0]
-        y = torch.empty((M, self.out_features), device=x.device, dtype=torch.bfloat16)
-        if M >= PREFILL_MIN_TOKENS and self.gemm_into(x2, y):
+        y = torch.empty((M, self.out_features), device=x.device, dtype=x.dtype)
+        if M >= PREFILL_MIN_TOKENS and x.dtype != torch.float32 and self.gemm_into(x2, y):
             pass
         elif M > 0:
             self.gemv_into(x2, y)
@@ -309,38 +418,49 @@ class PackedGroupedBlockRVQLinear(nn.Module):
     def gemm_into(self, x2: Tensor, y: Tensor, status: Optional[Tensor] = None) -> bool:
         """Prefill GEMM on the tcgen05 path; False when this layer's format is not covered by it."""
         lib = _abi.load()
-        layer = self.layer_struct()
+        layer = self.layer_struct(self._active_stages(), self.sum_mode())
         with torch.cuda.device(x2.device):
-            st = lib.wal_rvq_gemm(ctypes.byref(layer), x2.data_ptr(), x2.shape[0], x2.stride(0), y.data_ptr(),
-                                  y.stride(0), _abi.DTYPE_CODE[y.dtype], None if status is None else status.data_ptr(),
-                                  _abi.stream_handle(x2.device))
+            st = lib.wal_rvq_gemm_typed(ctypes.byref(layer), x2.data_ptr(), _abi.DTYPE_CODE[x2.dtype], x2.shape[0],
+                                        x2.stride(0), y.data_ptr(), y.stride(0), _abi.DTYPE_CODE[y.dtype],
+                                        None if status is None else status.data_ptr(), _abi.stream_handle(x2.device))
         if st == _abi.WAL_ERR_UNSUPPORTED:
             return False
         _abi.check(st, "wal_rvq_gemm")
         return True
 
     def gemv_into(self, x2: Tensor, y: Tensor, *, warps_per_tile: int = 0, num_ctas: int = 0) -> None:
-        """y[M, N] <- x2[M, K] @ w^T (+ bias) through ``wal_rvq_gemv_ex`` on the current stream."""
+        """y[M, N] <- x2[M, K] @ w^T (+ bias) through ``wal_rvq_gemv_typed`` on the current stream."""
         lib = _abi.load()
-        layer = self.layer_struct()
+        layer = self.layer_struct(self._active_stages(), self.sum_mode())
         with torch.cuda.device(x2.device):
-            st = lib.wal_rvq_gemv_ex(ctypes.byref(layer), x2.data_ptr(), x2.shape[0], x2.stride(0), y.data_ptr(),
-                                     y.stride(0), _abi.DTYPE_CODE[y.dtype], warps_per_tile, num_ctas,
-                                     _abi.stream_handle(x2.device))
+            st = lib.wal_rvq_gemv_typed(ctypes.byref(layer), x2.data_ptr(), _abi.DTYPE_CODE[x2.dtype], x2.shape[0],
+                                        x2.stride(0), y.data_ptr(), y.stride(0), _abi.DTYPE_CODE[y.dtype],
+                                        warps_per_tile, num_ctas, _abi.stream_handle(x2.device))
         _abi.check(st, "wal_rvq_gemv")
 
     def reconstruct_weight(self, out_dtype: torch.dtype = torch.bfloat16) -> Tensor:
-        """Materialise the weight, bit-identical to the reference's bf16 reconstruction."""
-        if out_dtype != torch.bfloat16:
-            raise ValueError("reconstruct_weight supports torch.bfloat16 (the forward's weight dtype)")
+        """The weight in ``out_dtype`` (bf16, fp16 or fp32), bit-identical to the reference's
+        ``reconstruct_weight(out_dtype)`` (every stage, exact sum; ``src/runtime.py:1234-1236``)."""
+        return self._dequant(out_dtype, None, _abi.WAL_SUM_EXACT)
+
+    def reconstruct_weight_fast(self, out_dtype: torch.dtype = torch.bfloat16) -> Tensor:
+        """The weight of the reference's ``reconstruct_weight_fast(out_dtype)`` (``src/runtime.py:1238-1240``):
+        the active stages of ``effective_stages_per_split``, each rounded to ``out_dtype`` and summed in it."""
+        active = tuple(g._compute_active_stage_indices() for g in self.groups)
+        full = tuple(range(self.num_stages))
+        return self._dequant(out_dtype, None if all(a == full for a in active) else active, _abi.WAL_SUM_FAST)
+
+    def _dequant(self, out_dtype: torch.dtype, stages, sum_mode: int) -> Tensor:
+        if out_dtype not in _abi.DTYPE_CODE:
+            raise ValueError(f"reconstruct_weight supports bfloat16, float16 and float32, got {out_dtype}")
         dev = self.packed_ids.device
         if dev.type != "cuda":
             raise ValueError("reconstruct_weight runs on CUDA only; move the module to a CUDA device")
-        w = torch.empty((self.out_features, self.in_features), device=dev, dtype=torch.bfloat16)
+        w = torch.empty((self.out_features, self.in_features), device=dev, dtype=out_dtype)
         lib = _abi.load()
         with torch.cuda.device(dev):
-            st = lib.wal_rvq_dequant(ctypes.byref(self.layer_struct()), w.data_ptr(), w.stride(0),
-                                     _abi.stream_handle(dev))
+            st = lib.wal_rvq_dequant_typed(ctypes.byref(self.layer_struct(stages, sum_mode)), w.data_ptr(),
+                                           w.stride(0), _abi.DTYPE_CODE[out_dtype], _abi.stream_handle(dev))
         _abi.check(st, "wal_rvq_dequant")
         return w
 
@@ -435,3 +555,48 @@ def replace_with_preencoded_packed_block_rvq(
             "bits_per_weight": float(enc.bits_per_weight()),
         })
     return stats
+
+
+# ---------------------------------------------------------------------------
+# variable-stage decoding helpers (reference src/runtime.py:2274-2327)
+# ---------------------------------------------------------------------------
+def set_global_effective_stages(model: nn.Module, stages: int) -> int:
+    """Set ``effective_stages_per_split`` on every ``PackedBlockRVQGroup``; returns the groups updated."""
+    n = 0
+    for module in model.modules():
+        if isinstance(module, PackedBlockRVQGroup):
+            module.set_effective_stages_per_split(int(stages))
+            n += 1
+    return n
+
+
+def set_effective_stages_by_name(model: nn.Module, attn_stages: Optional[int],
+                                 mlp_stages: Optional[int]) -> dict[str, int]:
+    """Per-role stage cap: ``.self_attn.`` linears get ``attn_stages``, ``.mlp.`` ones ``mlp_stages``."""
+    counts = {"attn": 0, "mlp": 0, "other": 0}
+    for name, module in model.named_modules():
+        if not isinstance(module, PackedGroupedBlockRVQLinear):
+            continue
+        bucket = "attn" if ".self_attn." in name else ("mlp" if ".mlp." in name else "other")
+        target = attn_stages if bucket == "attn" else (mlp_stages if bucket == "mlp" else None)
+        if target is None:
+            continue
+        for sub in module.modules():
+            if isinstance(sub, PackedBlockRVQGroup):
+                sub.set_effective_stages_per_split(int(target))
+        counts[bucket] += 1
+    return counts
+
+
+def set_effective_stages_from_map(model: nn.Module, name_to_k: dict[str, int]) -> int:
+    """Per-layer stage cap from ``{layer name: k}``; returns the layers updated (unknown names skipped)."""
+    updated = 0
+    for name, module in model.named_modules():
+        if not isinstance(module, PackedGroupedBlockRVQLinear) or name not in name_to_k:
+            continue
+        k = int(name_to_k[name])
+        for sub in module.modules():
+            if isinstance(sub, PackedBlockRVQGroup):
+                sub.set_effective_stages_per_split(k)
+        updated += 1
+    return updated

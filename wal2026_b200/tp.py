@@ -212,7 +212,7 @@ class PeerExchange:
         """Row-parallel GEMV whose fp32 partial lands in `slot` on every rank."""
         if x2.shape[0] > self.max_rows or lin.out_features != self.width:
             raise ValueError("push GEMV shape exceeds the exchange's slot")
-        st = self._lib.wal_rvq_gemv_push(ctypes.byref(lin.layer_struct()), x2.data_ptr(), x2.shape[0],
+        st = self._lib.wal_rvq_gemv_push(ctypes.byref(lin.layer_struct(lin._active_stages(), lin.sum_mode())), x2.data_ptr(), x2.shape[0],
                                          x2.stride(0), ctypes.byref(self._pushes[slot]),
                                          _abi.stream_handle(x2.device))
         _abi.check(st, "wal_rvq_gemv_push")
