@@ -222,6 +222,53 @@ WAL_API int wal_rvq_dequant_typed(const wal_rvq_layer* layer, void* w, int64_t l
 WAL_API int wal_rvq_unpack_ids(const wal_rvq_layer* layer, void* ids, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Per-block corrections (reference src/runtime.py:389-412): after the fp32
+ * stage sum S of a block (one unit, d columns), in this order
+ *   WAL_CORR_SIGN         S += (sigma * residual_scale[u]) @ sign_matrix, sigma_i = +1
+ *                         when bit i of residual_signs[u] is set, else -1
+ *   WAL_CORR_BLOCK_SCALE  S *= block_scale[u]
+ *   WAL_CORR_POLAR        S = inverse polar transform of S (radius, then angle
+ *                         groups of widths 1, 2, 4, ..., angles in units of pi)
+ *   WAL_CORR_MATRIX       S = S @ transform[g]          (otherwise, if set)
+ *   WAL_CORR_BIAS         S += transform_bias[g]
+ * then w = T(T(S) * T(rho)).  Unit u = row * blocks + block over the layer's
+ * rows (groups concatenated).  The matrix products run in ascending index
+ * order with fused multiply-adds; the reference's CPU matrix product may sum
+ * in another order, so a weight can differ in the last fp32 bit before its
+ * rounding (visible after rounding in about one weight in 10^4).
+ * ------------------------------------------------------------------------ */
+#define WAL_CORR_SIGN 1
+#define WAL_CORR_BLOCK_SCALE 2
+#define WAL_CORR_MATRIX 4
+#define WAL_CORR_POLAR 8
+#define WAL_CORR_BIAS 16
+
+typedef struct wal_rvq_corrections {
+  const int32_t* group_flags;     /* device int32 [num_groups]: WAL_CORR_* bits          */
+  const int32_t* residual_signs;  /* device int32 [N * blocks] (sign bits) or NULL      */
+  const uint16_t* residual_scale; /* device fp16 [N * blocks] or NULL                   */
+  const uint16_t* block_scale;    /* device fp16 [N * blocks] or NULL                   */
+  const float* sign_matrix;       /* device fp32 [d][d] or NULL                         */
+  const float* transform;         /* device fp32 [num_groups][d][d] or NULL             */
+  const float* transform_bias;    /* device fp32 [num_groups][d] or NULL                */
+} wal_rvq_corrections;
+
+/*
+ * y[M, N] = x[M, K] @ w^T (+ bias) for a layer with corrections, x_dtype
+ * WAL_BF16 / WAL_F16 / WAL_F32 (weights in that type), y_dtype any of the
+ * three; CUDA-core fp32 accumulation, 8 tokens per launch.  The layer's
+ * sum_mode must be WAL_SUM_EXACT (the reference's fast reconstruction does not
+ * take corrections).  Replaces reference src/runtime.py:1501-1507 for such
+ * encodings, which the reference's fused kernels refuse (src/runtime.py:837-853).
+ */
+WAL_API int wal_rvq_gemv_corrected(const wal_rvq_layer* layer, const wal_rvq_corrections* corr, const void* x,
+                           int x_dtype, int64_t M, int64_t ldx, void* y, int64_t ldy, int y_dtype, void* stream);
+
+/* The corrected weight [N, K] in w_dtype (reference reconstruct_weight(out_dtype)). */
+WAL_API int wal_rvq_dequant_corrected(const wal_rvq_layer* layer, const wal_rvq_corrections* corr, void* w,
+                              int64_t ldw, int w_dtype, void* stream);
+
+/* ------------------------------------------------------------------------
  * ID-route linear (reference src/runtime.py:52-97, PackedIDRouteLinear; fused
  * Triton kernel src/triton_id_matmul.py:19-67): one int16 id per weight into
  * a scalar fp16 route table codebook_sum[num_routes].  The weight is, bit for

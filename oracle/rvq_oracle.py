@@ -131,10 +131,115 @@ def reconstruct_group_typed(stage_ids: list[np.ndarray], codebooks: list[np.ndar
     return _round_to(w * rho, dtype)
 
 
+def _hadamard_t(n: int):
+    """Normalised Sylvester Hadamard matrix as the reference builds it (torch, ``src/block_vq.py:10-22``)."""
+    import math
+
+    import torch
+
+    mat = torch.tensor([[1.0]], dtype=torch.float32)
+    while mat.shape[0] < n:
+        mat = torch.cat((torch.cat((mat, mat), dim=1), torch.cat((mat, -mat), dim=1)), dim=0)
+    return mat / math.sqrt(float(n))
+
+
+def _rand_hadamard(n: int) -> np.ndarray:
+    """The randomised Hadamard / sign-correction matrix (reference ``src/block_vq.py:25-35``, ``:106-107``):
+    rows permuted and signed by draws from a CPU generator seeded with 0, in the reference's order."""
+    import torch
+
+    base = _hadamard_t(n)
+    gen = torch.Generator(device="cpu").manual_seed(0)
+    perm = torch.randperm(n, generator=gen)
+    flip = torch.randint(0, 2, (n,), generator=gen, dtype=torch.int64) > 0
+    signs = torch.where(flip, torch.ones(n), -torch.ones(n))
+    return (base[perm] * signs.unsqueeze(1)).numpy()
+
+
+def _fixed_transform(kind: str, n: int) -> np.ndarray | None:
+    """DCT / Hadamard / randomised Hadamard matrices (reference ``src/block_vq.py:10-61``)."""
+    if kind == "hadamard":
+        return _hadamard_t(n).numpy()
+    if kind == "rand_hadamard":
+        return _rand_hadamard(n)
+    if kind == "dct":
+        import math
+
+        import torch
+
+        idx = torch.arange(n, dtype=torch.float32)
+        mat = torch.cos(math.pi / float(n) * (idx + 0.5)[None, :] * idx[:, None])
+        mat[0] *= math.sqrt(1.0 / float(n))
+        if n > 1:
+            mat[1:] *= math.sqrt(2.0 / float(n))
+        return mat.numpy()
+    return None
+
+
+def _matmul_rows(v: np.ndarray, m: np.ndarray) -> np.ndarray:
+    """Rows of v times m: each output the exact dot product rounded once to float32."""
+    return (v.astype(np.float64) @ m.astype(np.float64)).astype(np.float32)
+
+
+def apply_corrections(acc: np.ndarray, g: dict) -> np.ndarray:
+    """Per-block corrections of reference ``src/runtime.py:389-412`` on fp32 block vectors ``[rows, blocks, d]``.
+
+    Sign residual ``(sigma * residual_scale) @ H``, block scale, inverse polar
+    transform or ``@ M`` (DCT, Hadamard, randomised Hadamard or the stored PCA
+    matrix), transform bias - in that order, in float32 (matrix products as
+    exact dot products rounded once; the reference's CPU matrix product may
+    differ from that in the last bit).
+    """
+    rows, blocks, d = acc.shape
+    v = acc.reshape(rows * blocks, d).astype(np.float32)
+    if g.get("residual_signs") is not None and g.get("residual_scale") is not None \
+            and g.get("residual_correction", "sign") != "none":
+        words = np.asarray(g["residual_signs"]).astype(np.int64).reshape(rows * blocks, -1)
+        bits = np.stack([(words[:, c // 32] >> (c % 32)) & 1 for c in range(d)], axis=1)
+        sigma = np.where(bits == 1, np.float32(1.0), np.float32(-1.0)).astype(np.float32)
+        rs = np.asarray(g["residual_scale"], dtype=np.float16).astype(np.float32).reshape(-1, 1)
+        v = (v + _matmul_rows(sigma * rs, _rand_hadamard(d))).astype(np.float32)
+    if g.get("block_scale") is not None:
+        v = (v * np.asarray(g["block_scale"], dtype=np.float16).astype(np.float32).reshape(-1, 1)).astype(np.float32)
+    kind = g.get("transform_kind", "none")
+    if kind == "polar":
+        cur = v[:, :1]
+        offset, width = 1, 1
+        while width < d:
+            ang = (np.float32(np.pi) * v[:, offset:offset + width]).astype(np.float32)
+            cur = np.stack((cur * np.cos(ang), cur * np.sin(ang)), axis=-1).reshape(v.shape[0], 2 * width)
+            cur = cur.astype(np.float32)
+            offset += width
+            width *= 2
+        v = cur
+    else:
+        m = g.get("transform_matrix")
+        m = _fixed_transform(kind, d) if m is None else np.asarray(m, dtype=np.float16).astype(np.float32)
+        if m is not None:
+            v = _matmul_rows(v, m)
+    if g.get("transform_bias") is not None:
+        v = (v + np.asarray(g["transform_bias"], dtype=np.float16).astype(np.float32).reshape(1, d)).astype(np.float32)
+    return v.reshape(rows, blocks, d)
+
+
+def reconstruct_group_corrected(g: dict, in_features: int, dtype: str = "bf16") -> np.ndarray:
+    """Weight values of one group with per-block corrections (exact reconstruction, ``dtype`` values in float32)."""
+    acc = apply_corrections(stage_sum_f32(g["stage_ids"], g["codebooks"], g.get("stage_scales")), g)
+    rho = _round_to(np.asarray(g["row_scale"], dtype=np.float16).astype(np.float32).reshape(-1, 1), dtype)
+    w = acc.reshape(acc.shape[0], -1)[:, :in_features]
+    return _round_to(_round_to(w, dtype) * rho, dtype)
+
+
 def reconstruct_typed(groups: list[dict], in_features: int, dtype: str = "bf16", mode: str = "exact") -> np.ndarray:
     """Concatenated group weights in ``dtype`` for either reconstruction mode (float32 values)."""
-    return np.concatenate([reconstruct_group_typed(g["stage_ids"], g["codebooks"], g["row_scale"], in_features, dtype,
-                                                   mode, g.get("stage_scales")) for g in groups], axis=0)
+    parts = []
+    for g in groups:
+        if g.get("corrected"):
+            parts.append(reconstruct_group_corrected(g, in_features, dtype))
+        else:
+            parts.append(reconstruct_group_typed(g["stage_ids"], g["codebooks"], g["row_scale"], in_features, dtype,
+                                                 mode, g.get("stage_scales")))
+    return np.concatenate(parts, axis=0)
 
 
 def reconstruct_bits(groups: list[dict], in_features: int) -> np.ndarray:
@@ -185,6 +290,17 @@ def groups_from_encoding(enc) -> list[dict]:
                 else g.stage_scales.cpu().float().numpy(),
             }
         )
+        if hasattr(g, "is_plain") and not g.is_plain():
+            out[-1].update({
+                "corrected": True,
+                "residual_correction": g.residual_correction,
+                "residual_signs": None if g.residual_signs is None else g.residual_signs.cpu().numpy(),
+                "residual_scale": None if g.residual_scale is None else g.residual_scale.cpu().numpy(),
+                "block_scale": None if g.block_scale is None else g.block_scale.cpu().numpy(),
+                "transform_kind": g.transform_kind,
+                "transform_matrix": None if g.transform_matrix is None else g.transform_matrix.cpu().numpy(),
+                "transform_bias": None if g.transform_bias is None else g.transform_bias.cpu().numpy(),
+            })
     return out
 
 

@@ -232,6 +232,69 @@ def dtype_cases(ref_runtime, ref_block_vq) -> None:
                                              [[1.2001953125]]), [2], 44, None, ref_runtime, ref_block_vq)
 
 
+def run_correction_case(name, ref_enc, Ms, x_seed, bias, ref_runtime, ref_io):
+    """A reference-encoded grouped encoding with per-block corrections (src/runtime.py:389-412): the encoding
+    itself (written by the reference's own map saver), its weights in every dtype and the forward."""
+    ref_io.save_grouped_encoding_map(HERE / f"{name}.pt", {"layer": ref_enc})
+    mod = ref_runtime.PackedGroupedBlockRVQLinear(ref_enc, bias, matmul_strategy="per_group")
+    with torch.no_grad():
+        wb = mod.reconstruct_weight(torch.bfloat16)
+        w16 = mod.reconstruct_weight(torch.float16)
+        w32 = mod.reconstruct_weight(torch.float32)
+    out = {"name": np.array(name), "N": np.array(ref_enc.original_shape[0]), "K": np.array(ref_enc.original_shape[1]),
+           "w_bits": bits(wb), "w16_bits": f16_bits(w16), "w32": w32.numpy(),
+           "kinds": np.array([g.transform_kind for g in ref_enc.groups]),
+           "signs": np.array([g.residual_signs is not None for g in ref_enc.groups]),
+           "block_scale": np.array([g.block_scale is not None for g in ref_enc.groups])}
+    if bias is not None:
+        out["bias_bits"] = bits(bias)
+    for M in Ms:
+        x = synthetic.activations(M, ref_enc.original_shape[1], seed=x_seed)
+        with torch.no_grad():
+            y = mod(x)
+        y32 = x.double() @ wb.double().T
+        if bias is not None:
+            y32 = y32 + bias.double()[None, :]
+        out[f"x{M}_bits"] = bits(x)
+        out[f"y{M}_ref32"] = y32.float().numpy()
+        out[f"y{M}_ref_bf16"] = bits(y)
+    np.savez_compressed(HERE / f"{name}.npz", **out)
+    print(f"wrote {name}.npz/.pt  kinds={out['kinds']} signs={out['signs']} block_scale={out['block_scale']}")
+
+
+def correction_cases(ref_runtime, ref_block_vq) -> None:
+    from src import encoding_io as ref_io  # type: ignore
+
+    def enc(seed, rows, cols, **kw):
+        torch.manual_seed(seed)
+        weight = torch.randn(rows, cols) * 0.02
+        return ref_block_vq.encode_block_residual_vq(weight, codebook_size=256, kmeans_iters=3, **kw)
+
+    def grouped(*encs):
+        rows, slices = 0, []
+        for e in encs:
+            slices.append((rows, rows + e.original_shape[0]))
+            rows += e.original_shape[0]
+        return ref_block_vq.GroupedBlockRVQEncoding(groups=tuple(encs), row_slices=tuple(slices),
+                                                    original_shape=(rows, encs[0].original_shape[1]))
+
+    run_correction_case("corr_sign_amax", grouped(enc(61, 48, 128, block_size=8, num_stages=2, normalize_blocks="amax",
+                                                      residual_correction="sign")), [1, 5], 61,
+                        synthetic.bias_vector(48, seed=61), ref_runtime, ref_io)
+    run_correction_case("corr_dct_l2", grouped(enc(62, 32, 128, block_size=8, num_stages=2, normalize_blocks="l2",
+                                                   transform_kind="dct", residual_correction="sign")), [3], 62, None,
+                        ref_runtime, ref_io)
+    run_correction_case("corr_hadamard_d16", grouped(enc(63, 32, 160, block_size=16, num_stages=1,
+                                                         transform_kind="hadamard", residual_correction="sign")), [2],
+                        63, None, ref_runtime, ref_io)
+    run_correction_case("corr_grouped_pca_rand",
+                        grouped(enc(64, 32, 128, block_size=8, num_stages=2, transform_kind="pca"),
+                                enc(65, 16, 128, block_size=8, num_stages=2, transform_kind="rand_hadamard",
+                                    normalize_blocks="amax")), [4], 64, None, ref_runtime, ref_io)
+    run_correction_case("corr_polar", grouped(enc(66, 32, 128, block_size=8, num_stages=2, transform_kind="polar")),
+                        [3], 66, None, ref_runtime, ref_io)
+
+
 def stage_drop_cases(ref_runtime, ref_block_vq) -> None:
     run_stage_drop_case("stage_drop_r3", single_group(synthetic.rvq_encoding(64, 192, d=8, R=3, seed=31)), 2,
                         [1, 5], 31, ref_runtime, ref_block_vq)
@@ -251,7 +314,7 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
     ap.add_argument("--skip-full", action="store_true")
-    ap.add_argument("--only", default="", help="comma-separated groups to (re)generate: stage_drop, dtype")
+    ap.add_argument("--only", default="", help="comma-separated groups to (re)generate: stage_drop, dtype, corrections")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     from src import block_vq as ref_block_vq  # type: ignore
@@ -264,6 +327,8 @@ def main() -> None:
             stage_drop_cases(ref_runtime, ref_block_vq)
         if "dtype" in only:
             dtype_cases(ref_runtime, ref_block_vq)
+        if "corrections" in only:
+            correction_cases(ref_runtime, ref_block_vq)
         return
     small = [
         ("small_r2_d8", single_group(synthetic.rvq_encoding(37, 64, d=8, R=2, seed=11)), [1, 3], 11, True),
@@ -318,6 +383,7 @@ def main() -> None:
                      None, ref_runtime)
     stage_drop_cases(ref_runtime, ref_block_vq)
     dtype_cases(ref_runtime, ref_block_vq)
+    correction_cases(ref_runtime, ref_block_vq)
     if args.skip_full:
         return
     run_case("cfg0", synthetic.cfg0_encoding(0), [1, 4, 16], 0, None, ref_runtime, ref_block_vq, full=False)

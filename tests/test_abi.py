@@ -163,9 +163,13 @@ def test_unsupported_encodings_raise_value_error():
     enc = synthetic.rvq_encoding(16, 32, seed=1)
     import dataclasses
 
-    bad = dataclasses.replace(enc, transform_kind="dct")
+    dct = dataclasses.replace(enc, transform_kind="dct")
     with pytest.raises(ValueError, match="per-block corrections"):
-        PackedGroupedBlockRVQLinear(single_group(bad))
+        pack_grouped(single_group(dct))  # the id packer alone covers the stage sum only
+    mod = PackedGroupedBlockRVQLinear(single_group(dct))  # the module packs the corrections beside it
+    assert mod.has_corrections and mod.corr_flags.tolist() == [_abi.WAL_CORR_MATRIX]
+    with pytest.raises(ValueError, match="transform_kind must be one of"):
+        PackedGroupedBlockRVQLinear(single_group(dataclasses.replace(enc, transform_kind="wavelet")))
     scaled = dataclasses.replace(enc, stage_scales=torch.tensor([1.5, 0.5], dtype=torch.float16))
     mod = PackedGroupedBlockRVQLinear(single_group(scaled))  # per-stage scales are supported
     assert torch.equal(mod.stage_scales, torch.tensor([[1.5, 0.5]]))

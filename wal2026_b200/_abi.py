@@ -68,6 +68,26 @@ class Layer(ctypes.Structure):
     ]
 
 
+class Corrections(ctypes.Structure):
+    """``wal_rvq_corrections``: device buffers of the per-block corrections of one linear."""
+    _fields_ = [
+        ("group_flags", ctypes.c_void_p),
+        ("residual_signs", ctypes.c_void_p),
+        ("residual_scale", ctypes.c_void_p),
+        ("block_scale", ctypes.c_void_p),
+        ("sign_matrix", ctypes.c_void_p),
+        ("transform", ctypes.c_void_p),
+        ("transform_bias", ctypes.c_void_p),
+    ]
+
+
+WAL_CORR_SIGN = 1
+WAL_CORR_BLOCK_SCALE = 2
+WAL_CORR_MATRIX = 4
+WAL_CORR_POLAR = 8
+WAL_CORR_BIAS = 16
+
+
 class TPPush(ctypes.Structure):
     """``wal_tp_push``: where a row-parallel GEMV stores its tagged partial."""
     _fields_ = [
@@ -106,6 +126,9 @@ SIGNATURES: dict[str, tuple] = {
     "wal_rvq_gemv": (_c_int, [_LP, _vp, _c_i64, _c_i64, _vp, _c_i64, _c_int, _vp]),
     "wal_rvq_gemv_typed": (_c_int, [_LP, _vp, _c_int, _c_i64, _c_i64, _vp, _c_i64, _c_int, _c_int, _c_int, _vp]),
     "wal_rvq_dequant_typed": (_c_int, [_LP, _vp, _c_i64, _c_int, _vp]),
+    "wal_rvq_gemv_corrected": (_c_int, [_LP, ctypes.POINTER(Corrections), _vp, _c_int, _c_i64, _c_i64, _vp, _c_i64,
+                                        _c_int, _vp]),
+    "wal_rvq_dequant_corrected": (_c_int, [_LP, ctypes.POINTER(Corrections), _vp, _c_i64, _c_int, _vp]),
     "wal_rvq_gemm_typed": (_c_int, [_LP, _vp, _c_int, _c_i64, _c_i64, _vp, _c_i64, _c_int, _vp, _vp]),
     "wal_rvq_gemv_ex": (_c_int, [_LP, _vp, _c_i64, _c_i64, _vp, _c_i64, _c_int, _c_int, _c_int, _vp]),
     "wal_rvq_gemm": (_c_int, [_LP, _vp, _c_i64, _c_i64, _vp, _c_i64, _c_int, _vp, _vp]),

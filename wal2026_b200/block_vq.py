@@ -61,11 +61,11 @@ class BlockRVQEncoding:
     def is_plain(self) -> bool:
         """True when the encoding uses none of the per-block corrections.
 
-        The fused CUDA path implements the sum-of-stages decode, with optional
-        per-stage scales (each stage value ``fp32(c) * scale`` before the sum,
-        reference ``src/block_vq.py:264-268``); block scales, sign residuals and
-        transforms are rejected by the packer with ``ValueError`` (the
-        reference's fused path rejects corrections too, ``src/runtime.py:828-853``).
+        Plain encodings (the sum of stages, with optional per-stage scales:
+        each stage value ``fp32(c) * scale`` before the sum, reference
+        ``src/block_vq.py:264-268``) run on the tensor-core decode kernels;
+        block scales, sign residuals and transforms (reference
+        ``src/runtime.py:389-412``) run on the corrected-decode kernels.
         """
         return (
             self.block_scale is None

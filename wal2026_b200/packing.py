@@ -8,6 +8,7 @@ reference's ``PackedBlockRVQGroup`` (reference ``src/runtime.py:249-344``).
 from __future__ import annotations
 
 import ctypes
+import math
 from dataclasses import dataclass
 from typing import Optional
 
@@ -36,11 +37,12 @@ def _geometry(N: int, K: int, d: int, R: int, entries: int, groups: int) -> _abi
                          num_groups=groups)
 
 
-def validate_grouped(enc: GroupedBlockRVQEncoding) -> tuple[int, int, int, int]:
-    """Check an encoding is supported by the fused path; return (d, R, entries, K).
+def validate_grouped(enc: GroupedBlockRVQEncoding, allow_corrections: bool = False) -> tuple[int, int, int, int]:
+    """Check an encoding is supported by the packed path; return (d, R, entries, K).
 
     Unsupported encodings raise ``ValueError`` like the reference's fused path
-    does (``src/runtime.py:848-853``).
+    does (``src/runtime.py:848-853``).  Per-block corrections are accepted when
+    ``allow_corrections`` (their side arrays come from ``pack_corrections``).
     """
     if not enc.groups:
         raise ValueError("encoding has no groups")
@@ -51,9 +53,9 @@ def validate_grouped(enc: GroupedBlockRVQEncoding) -> tuple[int, int, int, int]:
     entries = int(first.codebooks[0].shape[0])
     row = 0
     for g, (r0, r1) in zip(enc.groups, enc.row_slices):
-        if not g.is_plain():
-            raise ValueError("packed CUDA path supports Block-RVQ encodings without per-block corrections "
-                             "(no block_scale, residual correction or transform)")
+        if not g.is_plain() and not allow_corrections:
+            raise ValueError("the packed id stream covers the stage sum only; pack the per-block corrections "
+                             "(block_scale, residual correction, transform) with pack_corrections")
         if int(g.block_size) != d or int(g.num_stages) != R:
             raise ValueError("all row groups must share block_size and num_stages")
         if any(int(c.shape[0]) != entries or int(c.shape[1]) != d for c in g.codebooks):
@@ -98,8 +100,8 @@ def _ids_array(t: torch.Tensor, entries: int) -> np.ndarray:
     return t.to(torch.int32).numpy().astype(np.uint16)
 
 
-def pack_grouped(enc: GroupedBlockRVQEncoding) -> PackedArrays:
-    d, R, entries, K = validate_grouped(enc)
+def pack_grouped(enc: GroupedBlockRVQEncoding, allow_corrections: bool = False) -> PackedArrays:
+    d, R, entries, K = validate_grouped(enc, allow_corrections)
     lib = _abi.load()
     N = int(enc.original_shape[0])
     G = len(enc.groups)
@@ -168,3 +170,125 @@ def pack_routes(route: torch.Tensor, code: torch.Tensor, codebooks: torch.Tensor
     books = codebooks.detach().cpu().to(torch.float16).reshape(1, 1, G * C, d).contiguous()
     rho = row_scale.detach().cpu().to(torch.float16).reshape(-1).contiguous()
     return PackedArrays(geom, int(ntiles.value), packed, table, books, rho)
+
+
+# ---------------------------------------------------------------------------
+# per-block corrections (reference src/runtime.py:389-412)
+# ---------------------------------------------------------------------------
+@dataclass
+class CorrectionArrays:
+    """Host tensors of ``wal_rvq_corrections`` for one linear (units = rows x blocks, groups concatenated)."""
+
+    group_flags: torch.Tensor                # int32 [groups] of WAL_CORR_* bits
+    residual_signs: Optional[torch.Tensor]   # int32 [N * blocks]
+    residual_scale: Optional[torch.Tensor]   # fp16 [N * blocks]
+    block_scale: Optional[torch.Tensor]      # fp16 [N * blocks]
+    sign_matrix: Optional[torch.Tensor]      # fp32 [d, d]
+    transform: Optional[torch.Tensor]        # fp32 [groups, d, d]
+    transform_bias: Optional[torch.Tensor]   # fp32 [groups, d]
+
+
+def hadamard_matrix(n: int) -> torch.Tensor:
+    """Normalised Sylvester Hadamard matrix (the reference's ``_hadamard_matrix``, src/block_vq.py:10-22)."""
+    if n < 1 or n & (n - 1):
+        raise ValueError("hadamard transform requires power-of-two block_size")
+    h = torch.ones(1, 1, dtype=torch.float32)
+    while h.shape[0] < n:
+        h = torch.cat((torch.cat((h, h), dim=1), torch.cat((h, -h), dim=1)), dim=0)
+    return h / math.sqrt(float(n))
+
+
+def rand_hadamard_matrix(n: int) -> torch.Tensor:
+    """Row-permuted, row-signed Hadamard matrix from a fixed CPU generator (src/block_vq.py:25-35).
+
+    The permutation and signs are drawn in the same order from a generator
+    seeded with 0, so the matrix is the reference's, bit for bit.
+    """
+    base = hadamard_matrix(n)
+    gen = torch.Generator(device="cpu").manual_seed(0)
+    perm = torch.randperm(n, generator=gen)
+    flip = torch.randint(0, 2, (n,), generator=gen, dtype=torch.int64) > 0
+    signs = torch.where(flip, torch.ones(n), -torch.ones(n))
+    return base[perm] * signs.unsqueeze(1)
+
+
+def dct_matrix(n: int) -> torch.Tensor:
+    """Orthonormal DCT-II matrix, rows = frequencies (src/block_vq.py:38-45)."""
+    idx = torch.arange(n, dtype=torch.float32)
+    mat = torch.cos(math.pi / float(n) * (idx + 0.5)[None, :] * idx[:, None])
+    mat[0] *= math.sqrt(1.0 / float(n))
+    if n > 1:
+        mat[1:] *= math.sqrt(2.0 / float(n))
+    return mat
+
+
+def transform_matrix(kind: str, n: int) -> Optional[torch.Tensor]:
+    """The fixed d x d matrix of a transform kind (None for none / polar / pca), src/block_vq.py:48-61."""
+    if kind in ("none", "polar", "pca"):
+        return None
+    if kind == "dct":
+        return dct_matrix(n)
+    if kind == "hadamard":
+        return hadamard_matrix(n)
+    if kind == "rand_hadamard":
+        return rand_hadamard_matrix(n)
+    raise ValueError("transform_kind must be one of: none, dct, hadamard, rand_hadamard, polar, pca")
+
+
+def pack_corrections(enc: GroupedBlockRVQEncoding) -> Optional[CorrectionArrays]:
+    """Side arrays of the per-block corrections, or None when every group is plain."""
+    if all(g.is_plain() for g in enc.groups):
+        return None
+    d = int(enc.groups[0].block_size)
+    B = -(-int(enc.original_shape[1]) // d)
+    G = len(enc.groups)
+    flags = []
+    signs, rscale, bscale = [], [], []
+    mats = torch.zeros(G, d, d, dtype=torch.float32)
+    tbias = torch.zeros(G, d, dtype=torch.float32)
+    any_sign = any_bs = any_mat = any_bias = False
+    for gi, g in enumerate(enc.groups):
+        rows = int(g.original_shape[0])
+        f = 0
+        if g.residual_correction != "none" and g.residual_signs is not None and g.residual_scale is not None:
+            words = g.residual_signs.detach().cpu().reshape(rows * B, -1)
+            if words.shape[1] != 1:
+                raise ValueError("sign residuals wider than 32 columns are not supported")
+            signs.append(words[:, 0].to(torch.int32))
+            rscale.append(g.residual_scale.detach().cpu().to(torch.float16).reshape(rows * B))
+            f |= _abi.WAL_CORR_SIGN
+            any_sign = True
+        else:
+            signs.append(torch.zeros(rows * B, dtype=torch.int32))
+            rscale.append(torch.zeros(rows * B, dtype=torch.float16))
+        if g.block_scale is not None:
+            bscale.append(g.block_scale.detach().cpu().to(torch.float16).reshape(rows * B))
+            f |= _abi.WAL_CORR_BLOCK_SCALE
+            any_bs = True
+        else:
+            bscale.append(torch.ones(rows * B, dtype=torch.float16))
+        if g.transform_kind == "polar":
+            if d & (d - 1):
+                raise ValueError("polar transform requires power-of-two block_size")
+            f |= _abi.WAL_CORR_POLAR
+        else:
+            m = g.transform_matrix
+            m = transform_matrix(g.transform_kind, d) if m is None else m.detach().cpu().to(torch.float32)
+            if m is not None:
+                mats[gi] = m.reshape(d, d)
+                f |= _abi.WAL_CORR_MATRIX
+                any_mat = True
+        if g.transform_bias is not None:
+            tbias[gi] = g.transform_bias.detach().cpu().to(torch.float32).reshape(d)
+            f |= _abi.WAL_CORR_BIAS
+            any_bias = True
+        flags.append(f)
+    return CorrectionArrays(
+        group_flags=torch.tensor(flags, dtype=torch.int32),
+        residual_signs=torch.cat(signs).contiguous() if any_sign else None,
+        residual_scale=torch.cat(rscale).contiguous() if any_sign else None,
+        block_scale=torch.cat(bscale).contiguous() if any_bs else None,
+        sign_matrix=rand_hadamard_matrix(d).contiguous() if any_sign else None,
+        transform=mats.contiguous() if any_mat else None,
+        transform_bias=tbias.contiguous() if any_bias else None,
+    )

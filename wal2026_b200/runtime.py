@@ -25,7 +25,7 @@ from torch import Tensor, nn
 
 from . import _abi
 from .block_vq import GroupedBlockRVQEncoding, single_group
-from .packing import PackedArrays, pack_grouped, pack_routes
+from .packing import CorrectionArrays, PackedArrays, pack_corrections, pack_grouped, pack_routes
 
 # the reference's accepted strategy names (src/runtime.py:1192)
 MATMUL_STRATEGIES = frozenset({
@@ -51,6 +51,9 @@ FAST_STRATEGIES = frozenset({
 
 # token count from which the forward uses the tensor-core prefill GEMM
 PREFILL_MIN_TOKENS = 128
+# encodings with per-block corrections: the fused CUDA-core GEMV up to this many
+# tokens, beyond it the corrected weight is materialised once for a library GEMM
+CORRECTED_GEMV_MAX_TOKENS = 64
 
 TARGET_LINEAR_SUFFIXES = (
     "self_attn.q_proj",
@@ -177,8 +180,9 @@ class PackedGroupedBlockRVQLinear(nn.Module):
         self.hot_score_mode = hot_score_mode
         self.hot_min_stage_share = float(hot_min_stage_share)
         self.hot_score_threshold_ratio = float(hot_score_threshold_ratio)
-        packed = _packed if _packed is not None else pack_grouped(enc)
+        packed = _packed if _packed is not None else pack_grouped(enc, allow_corrections=True)
         self._set_packed(packed)
+        self._set_corrections(pack_corrections(enc))
         self.groups = nn.ModuleList(
             PackedBlockRVQGroup(self, r0, r1, block_size=g.block_size, in_features=self.in_features,
                                 num_stages=len(g.stage_ids), enc=g)
@@ -205,6 +209,26 @@ class PackedGroupedBlockRVQLinear(nn.Module):
             self.register_buffer("stage_scales", packed.stage_scales.to(torch.float32).contiguous())
         else:
             self.stage_scales = None
+
+    CORRECTION_BUFFERS = ("corr_flags", "corr_signs", "corr_rscale", "corr_bscale", "corr_sign_matrix",
+                          "corr_transform", "corr_tbias")
+
+    def _set_corrections(self, corr: Optional[CorrectionArrays]) -> None:
+        """Register the per-block correction arrays (reference ``src/runtime.py:266-290`` buffers) or mark none."""
+        self.has_corrections = corr is not None
+        values = (None,) * len(self.CORRECTION_BUFFERS) if corr is None else (
+            corr.group_flags, corr.residual_signs, corr.residual_scale, corr.block_scale, corr.sign_matrix,
+            corr.transform, corr.transform_bias)
+        for name, value in zip(self.CORRECTION_BUFFERS, values):
+            if value is None:
+                setattr(self, name, None)
+            else:
+                self.register_buffer(name, value)
+
+    def corrections_struct(self) -> _abi.Corrections:
+        """The ``wal_rvq_corrections`` descriptor of this module's correction buffers."""
+        ptrs = [None if getattr(self, n) is None else getattr(self, n).data_ptr() for n in self.CORRECTION_BUFFERS]
+        return _abi.Corrections(*ptrs)
 
     @classmethod
     def random(
@@ -281,6 +305,7 @@ class PackedGroupedBlockRVQLinear(nn.Module):
         obj.matmul_chunk_rows = obj.local_palette_group_cols = obj.hot_topk = None
         obj.hot_score_mode, obj.hot_min_stage_share, obj.hot_score_threshold_ratio = "row_scale_norm", 0.0, 0.0
         obj._set_packed(arrays)
+        obj._set_corrections(None)
         obj.groups = nn.ModuleList(PackedBlockRVQGroup(obj, r0, r1, block_size=d, in_features=K, num_stages=R)
                                    for r0, r1 in obj.row_slices)
         if bias is not None:
@@ -304,8 +329,13 @@ class PackedGroupedBlockRVQLinear(nn.Module):
 
     # -- C ABI plumbing -----------------------------------------------------
     def _active_stages(self) -> Optional[tuple[tuple[int, ...], ...]]:
-        """Per-group active stage indices when this strategy drops stages, else None (all stages)."""
-        if self.matmul_strategy not in FAST_STRATEGIES:
+        """Per-group active stage indices when this strategy drops stages, else None (all stages).
+
+        Encodings with per-block corrections always sum every stage: the
+        reference's fast reconstruction falls back to the full one for them
+        (``supports_fast_reconstruct``, ``src/runtime.py:416-429``).
+        """
+        if self.matmul_strategy not in FAST_STRATEGIES or self.has_corrections:
             return None
         active = tuple(g._compute_active_stage_indices() for g in self.groups)
         full = tuple(range(self.num_stages))
@@ -344,7 +374,8 @@ class PackedGroupedBlockRVQLinear(nn.Module):
 
     def sum_mode(self) -> int:
         """``WAL_SUM_FAST`` for the strategies built on the reference's fast reconstruction, else exact."""
-        return _abi.WAL_SUM_FAST if self.matmul_strategy in FAST_STRATEGIES else _abi.WAL_SUM_EXACT
+        fast = self.matmul_strategy in FAST_STRATEGIES and not self.has_corrections
+        return _abi.WAL_SUM_FAST if fast else _abi.WAL_SUM_EXACT
 
     def layer_struct(self, stages: Optional[tuple[tuple[int, ...], ...]] = None,
                      sum_mode: int = _abi.WAL_SUM_EXACT) -> _abi.Layer:
@@ -408,6 +439,11 @@ class PackedGroupedBlockRVQLinear(nn.Module):
                 xp[:, :self.in_features] = x2
                 x2 = xp
         M = x2.shape[0]
+        if self.has_corrections and M > CORRECTED_GEMV_MAX_TOKENS:
+            # the corrected weight once, then a library GEMM (the reference's own per_group scheme)
+            w = self.reconstruct_weight(x.dtype)
+            bias = None if self.bias is None else self.bias.to(x.dtype)
+            return torch.nn.functional.linear(x2, w, bias).reshape(*orig[:-1], self.out_features)
         y = torch.empty((M, self.out_features), device=x.device, dtype=x.dtype)
         if M >= PREFILL_MIN_TOKENS and x.dtype != torch.float32 and self.gemm_into(x2, y):
             pass
@@ -417,6 +453,8 @@ class PackedGroupedBlockRVQLinear(nn.Module):
 
     def gemm_into(self, x2: Tensor, y: Tensor, status: Optional[Tensor] = None) -> bool:
         """Prefill GEMM on the tcgen05 path; False when this layer's format is not covered by it."""
+        if self.has_corrections:
+            return False
         lib = _abi.load()
         layer = self.layer_struct(self._active_stages(), self.sum_mode())
         with torch.cuda.device(x2.device):
@@ -432,6 +470,14 @@ class PackedGroupedBlockRVQLinear(nn.Module):
         """y[M, N] <- x2[M, K] @ w^T (+ bias) through ``wal_rvq_gemv_typed`` on the current stream."""
         lib = _abi.load()
         layer = self.layer_struct(self._active_stages(), self.sum_mode())
+        if self.has_corrections:
+            corr = self.corrections_struct()
+            with torch.cuda.device(x2.device):
+                st = lib.wal_rvq_gemv_corrected(ctypes.byref(layer), ctypes.byref(corr), x2.data_ptr(),
+                                                _abi.DTYPE_CODE[x2.dtype], x2.shape[0], x2.stride(0), y.data_ptr(),
+                                                y.stride(0), _abi.DTYPE_CODE[y.dtype], _abi.stream_handle(x2.device))
+            _abi.check(st, "wal_rvq_gemv_corrected")
+            return
         with torch.cuda.device(x2.device):
             st = lib.wal_rvq_gemv_typed(ctypes.byref(layer), x2.data_ptr(), _abi.DTYPE_CODE[x2.dtype], x2.shape[0],
                                         x2.stride(0), y.data_ptr(), y.stride(0), _abi.DTYPE_CODE[y.dtype],
@@ -446,6 +492,8 @@ class PackedGroupedBlockRVQLinear(nn.Module):
     def reconstruct_weight_fast(self, out_dtype: torch.dtype = torch.bfloat16) -> Tensor:
         """The weight of the reference's ``reconstruct_weight_fast(out_dtype)`` (``src/runtime.py:1238-1240``):
         the active stages of ``effective_stages_per_split``, each rounded to ``out_dtype`` and summed in it."""
+        if self.has_corrections:  # the reference falls back to the full reconstruction
+            return self.reconstruct_weight(out_dtype)
         active = tuple(g._compute_active_stage_indices() for g in self.groups)
         full = tuple(range(self.num_stages))
         return self._dequant(out_dtype, None if all(a == full for a in active) else active, _abi.WAL_SUM_FAST)
@@ -458,6 +506,13 @@ class PackedGroupedBlockRVQLinear(nn.Module):
             raise ValueError("reconstruct_weight runs on CUDA only; move the module to a CUDA device")
         w = torch.empty((self.out_features, self.in_features), device=dev, dtype=out_dtype)
         lib = _abi.load()
+        if self.has_corrections:
+            corr = self.corrections_struct()
+            with torch.cuda.device(dev):
+                st = lib.wal_rvq_dequant_corrected(ctypes.byref(self.layer_struct()), ctypes.byref(corr), w.data_ptr(),
+                                                   w.stride(0), _abi.DTYPE_CODE[out_dtype], _abi.stream_handle(dev))
+            _abi.check(st, "wal_rvq_dequant_corrected")
+            return w
         with torch.cuda.device(dev):
             st = lib.wal_rvq_dequant_typed(ctypes.byref(self.layer_struct(stages, sum_mode)), w.data_ptr(),
                                            w.stride(0), _abi.DTYPE_CODE[out_dtype], _abi.stream_handle(dev))

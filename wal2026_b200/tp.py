@@ -83,6 +83,8 @@ def shard_packed(lin: PackedGroupedBlockRVQLinear, rank: int, size: int, mode: s
     module was packed from.  Row-parallel shards drop the bias (partials are
     summed; the caller adds a bias once).
     """
+    if getattr(lin, "has_corrections", False):
+        raise ValueError("tensor-parallel shards of layers with per-block corrections are not supported")
     d, R = lin.block_size, lin.num_stages
     idw = 1 if lin.num_entries <= 256 else 2
     blocks = -(-lin.in_features // d)
