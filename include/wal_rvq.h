@@ -423,6 +423,18 @@ WAL_API int wal_decode_attention(const uint16_t* q, int64_t ld_q, const uint16_t
                          void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * wal_decode_attention with an explicit split count (0 = library default):
+ * num_splits splits of at most 128 and at least 32 positions each
+ * (ceil(n / 128) <= num_splits <= ceil(n / 32), else WAL_ERR_SHAPE); the
+ * workspace must hold that many splits' partials (WAL_ERR_BUFFER_TOO_SMALL
+ * otherwise).  For tuning and tests.
+ */
+WAL_API int wal_decode_attention_ex(const uint16_t* q, int64_t ld_q, const uint16_t* k_cache,
+                         const uint16_t* v_cache, int64_t B, int32_t hq, int32_t hkv, int32_t hd,
+                         int64_t cache_len, int64_t n, float scale, uint16_t* out, int64_t ld_out,
+                         void* workspace, size_t workspace_bytes, int num_splits, void* stream);
+
+/*
  * Decode attention that allocates nothing, for callers that cannot call
  * cudaMalloc: a plugin run by a host engine that owns all device memory and
  * hands it inputs and outputs but no workspace, or a serving loop that must

@@ -187,7 +187,8 @@ def test_route_module_shape():
 def test_profile_cases_cli_lists_its_cases():
     from wal2026_b200 import profile_cases
 
-    assert set(profile_cases.CASES) == {"cfg1_gemv", "gemv_window", "idroute_mlp", "attention", "prefill_gate_up"}
+    assert set(profile_cases.CASES) == {"cfg1_gemv", "gemv_window", "idroute_mlp", "attention", "prefill_gate_up",
+                                        "tp_breakdown"}
     assert profile_cases.main(["no_such_case"]) == 2
 
 

@@ -142,6 +142,9 @@ SIGNATURES: dict[str, tuple] = {
                                                          _c_i64]),
     "wal_decode_attention": (_c_int, [_vp, _c_i64, _vp, _vp, _c_i64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                       _c_i64, _c_i64, ctypes.c_float, _vp, _c_i64, _vp, ctypes.c_size_t, _vp]),
+    "wal_decode_attention_ex": (_c_int, [_vp, _c_i64, _vp, _vp, _c_i64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                         _c_i64, _c_i64, ctypes.c_float, _vp, _c_i64, _vp, ctypes.c_size_t, _c_int,
+                                         _vp]),
     "wal_decode_attention_static": (_c_int, [_vp, _c_i64, _vp, _vp, _c_i64, ctypes.c_int32, ctypes.c_int32,
                                              ctypes.c_int32, _c_i64, _c_i64, ctypes.c_float, _vp, _c_i64, _vp]),
     "wal_tp_push_rows": (_c_int, [_vp, _c_i64, _c_int, _c_i64, _c_i64, ctypes.POINTER(TPPush), _vp]),

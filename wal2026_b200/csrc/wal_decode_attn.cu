@@ -29,7 +29,6 @@ namespace {
 
 constexpr int kThreads = 128;     // 4 warps
 constexpr int kMaxChunk = kThreads;  // positions per split: 32 per warp
-constexpr int kTargetCtas = 148;   // one CTA per SM when the batch is small
 
 struct AttnParams {
   const uint16_t* q;
@@ -284,16 +283,18 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   }
 }
 
-// Split count before rounding the chunk to a multiple of 4: about one CTA per
-// SM, at most kMaxChunk and at least 32 positions per split.  Every term is
-// non-decreasing in n, so this is an upper bound of plan()'s split count for
-// every n' <= n (the chunk rounding in plan() only lowers it).
+// Split count before rounding the chunk to a multiple of 4: the fewest splits
+// of at most kMaxChunk positions.  Measured on B200 (8B / 70B shard heads,
+// 2048-4096 positions, batch 1-8), more splits than that only lengthen the
+// merge, which the last CTA of a (sequence, kv head) runs over every split:
+// e.g. 70B heads at tensor parallelism 8 (one kv head, 4096 positions) take
+// 9.7 us with 32 splits against 21.7 us with 128.  Non-decreasing in n, so it
+// also bounds plan()'s split count for every n' <= n (the chunk rounding in
+// plan() only lowers it).
 long long split_bound(long long B, int hkv, long long n) {
-  long long s = (kTargetCtas + B * hkv - 1) / (B * hkv);
-  const long long min_split = (n + kMaxChunk - 1) / kMaxChunk;
-  if (s < min_split) s = min_split;
-  const long long max_split = (n + 31) / 32;  // at least 32 positions per split
-  if (s > max_split) s = max_split;
+  (void)B;
+  (void)hkv;
+  const long long s = (n + kMaxChunk - 1) / kMaxChunk;
   return s < 1 ? 1 : s;
 }
 
@@ -425,22 +426,42 @@ void* g_scratch_addr[kMaxDevices];
 
 extern "C" {
 
-int wal_decode_attention(const uint16_t* q, int64_t ld_q, const uint16_t* k_cache, const uint16_t* v_cache, int64_t B,
-                         int32_t hq, int32_t hkv, int32_t hd, int64_t cache_len, int64_t n, float scale,
-                         uint16_t* out, int64_t ld_out, void* workspace, size_t workspace_bytes, void* stream) {
+int wal_decode_attention_ex(const uint16_t* q, int64_t ld_q, const uint16_t* k_cache, const uint16_t* v_cache,
+                            int64_t B, int32_t hq, int32_t hkv, int32_t hd, int64_t cache_len, int64_t n, float scale,
+                            uint16_t* out, int64_t ld_out, void* workspace, size_t workspace_bytes, int num_splits,
+                            void* stream) {
   AttnParams p;
   int st = prepare(q, ld_q, k_cache, v_cache, B, hq, hkv, hd, cache_len, n, scale, out, ld_out, &p);
   if (st != WAL_OK) return st;
   if (!workspace) return WAL_ERR_INVALID_ARGUMENT;
   if ((uintptr_t)workspace & 255) return WAL_ERR_ALIGNMENT;
-  if (workspace_bytes < wal_decode_attention_workspace(B, hq, hkv, hd, n)) return WAL_ERR_BUFFER_TOO_SMALL;
   const int G = hq / hkv;
+  if (num_splits < 0) return WAL_ERR_INVALID_ARGUMENT;
+  if (num_splits > 0) {  // explicit split: at most kMaxChunk and at least 32 positions per split
+    long long sp = num_splits;
+    if (sp < (n + kMaxChunk - 1) / kMaxChunk || sp > (n + 31) / 32) return WAL_ERR_SHAPE;
+    long long c = ((n + sp - 1) / sp + 3) & ~3LL;
+    p.nsplit = (int)((n + c - 1) / c);
+    p.chunk = (int)c;
+    if (smem_bytes(hd, G, p.nsplit) > kMaxSmem) return WAL_ERR_SHAPE;
+    if (workspace_bytes < counter_bytes(B, hkv) + part_bytes(B, hkv, p.nsplit, G, hd) + stats_bytes(B, hkv, p.nsplit, G))
+      return WAL_ERR_BUFFER_TOO_SMALL;
+  } else if (workspace_bytes < wal_decode_attention_workspace(B, hq, hkv, hd, n)) {
+    return WAL_ERR_BUFFER_TOO_SMALL;
+  }
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   const size_t cb = counter_bytes(B, hkv);
   p.counter = reinterpret_cast<unsigned*>(ws);
   p.part = reinterpret_cast<float*>(ws + cb);
   p.stats = reinterpret_cast<float2*>(ws + cb + part_bytes(B, hkv, p.nsplit, G, hd));
   return run(p, B, stream);
+}
+
+int wal_decode_attention(const uint16_t* q, int64_t ld_q, const uint16_t* k_cache, const uint16_t* v_cache, int64_t B,
+                         int32_t hq, int32_t hkv, int32_t hd, int64_t cache_len, int64_t n, float scale,
+                         uint16_t* out, int64_t ld_out, void* workspace, size_t workspace_bytes, void* stream) {
+  return wal_decode_attention_ex(q, ld_q, k_cache, v_cache, B, hq, hkv, hd, cache_len, n, scale, out, ld_out,
+                                 workspace, workspace_bytes, 0, stream);
 }
 
 int wal_decode_attention_static(const uint16_t* q, int64_t ld_q, const uint16_t* k_cache, const uint16_t* v_cache,

@@ -26,9 +26,12 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cooperative_groups.h>
 #include <cstring>
 
 namespace {
+
+namespace cg = cooperative_groups;
 
 __device__ __forceinline__ void dependency_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 __device__ __forceinline__ void dependents_launch() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
@@ -190,6 +193,144 @@ __global__ void __launch_bounds__(kNormThreads) residual_rmsnorm_kernel(const __
   }
 }
 
+// Cluster form of the same operation for wide rows: one cluster of kNormCluster
+// CTAs per token row, each CTA owning N / kNormCluster columns.  Every thread
+// issues the loads of all ranks' words of its 8 columns at once and re-reads
+// (bounded) only the words whose tag is not yet current, so the exchange costs
+// one memory round trip instead of one per rank; the CTAs' sums of squares
+// meet through distributed shared memory and are added in CTA order, so every
+// CTA (and every rank) derives the same scale.
+constexpr int kNormCluster = 8;
+
+__global__ void __launch_bounds__(256) residual_rmsnorm_cluster_kernel(const __grid_constant__ NormParams p) {
+  extern __shared__ float hs[];  // this CTA's columns after the residual add
+  __shared__ float red[8];
+  __shared__ float cta_sum;
+  __shared__ int cta_fail;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int cr = (int)cluster.block_rank();
+  dependency_wait();
+  dependents_launch();
+  const int m = blockIdx.y;
+  const int cols = p.N / kNormCluster;
+  const int c_begin = cr * cols;
+  unsigned tag = 0;
+  unsigned long long deadline = 0;
+  if (p.recv) {
+    tag = *reinterpret_cast<const volatile unsigned*>(p.epoch) + 1u;
+    deadline = global_ns() + kPeerWaitNs;
+  }
+  if (threadIdx.x == 0) cta_fail = 0;
+  __syncthreads();
+  uint16_t* hrow = p.h + (long long)m * p.ldh;
+  float sq = 0.f;
+  bool ok = true;
+  for (int lc = threadIdx.x * 8; lc < cols; lc += blockDim.x * 8) {
+    const int c = c_begin + lc;
+    uint4 hv = *reinterpret_cast<const uint4*>(hrow + c);
+    uint16_t hb[8];
+    memcpy(hb, &hv, 16);
+    float s[8];
+    bool have = false;
+    if (p.recv) {
+      const uint4* row = p.recv + ((long long)m * p.ld + c) / 2;
+      uint4 v[WAL_MAX_RANKS][4];
+#pragma unroll
+      for (int r = 0; r < WAL_MAX_RANKS; ++r)
+        if (r < p.num_ranks)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) v[r][j] = ld_volatile_v4(row + r * (p.rank_stride / 2) + j);
+#pragma unroll
+      for (int r = 0; r < WAL_MAX_RANKS; ++r) {
+        if (r >= p.num_ranks) break;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          // re-read only words that are not current yet, until the deadline
+          while (ok && (v[r][j].y != tag || v[r][j].w != tag)) {
+            if (global_ns() > deadline) {
+              ok = false;
+              break;
+            }
+            v[r][j] = ld_volatile_v4(row + r * (p.rank_stride / 2) + j);
+          }
+          const float a = __uint_as_float(v[r][j].x), b = __uint_as_float(v[r][j].z);
+          s[2 * j] = r == 0 ? a : s[2 * j] + a;
+          s[2 * j + 1] = r == 0 ? b : s[2 * j + 1] + b;
+        }
+      }
+      have = ok;
+    } else if (p.partial) {
+      const float* src = p.partial + (long long)m * p.ldp + c;
+      const float4 a = *reinterpret_cast<const float4*>(src);
+      const float4 b = *reinterpret_cast<const float4*>(src + 4);
+      s[0] = a.x; s[1] = a.y; s[2] = a.z; s[3] = a.w; s[4] = b.x; s[5] = b.y; s[6] = b.z; s[7] = b.w;
+      have = true;
+    }
+    if (!ok) break;
+    if (have) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) hb[j] = f32_to_bf16(bf16_to_f32(hb[j]) + bf16_to_f32(f32_to_bf16(s[j])));
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float hn = bf16_to_f32(hb[j]);
+      hs[lc + j] = hn;
+      sq = fmaf(hn, hn, sq);
+    }
+  }
+  if (!ok) cta_fail = 1;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+    cta_sum = t;
+  }
+  cluster.sync();  // every CTA's partial sum and failure flag are published
+  float tot = 0.f;
+  int fail = 0;
+  for (int k = 0; k < kNormCluster; ++k) {
+    tot += *cluster.map_shared_rank(&cta_sum, k);
+    fail |= *cluster.map_shared_rank(&cta_fail, k);
+  }
+  cluster.sync();  // no CTA leaves while another still reads its shared memory
+  if (fail) {
+    if (threadIdx.x == 0 && cr == 0 && p.status) atomicExch(p.status, (int)WAL_ERR_PEER_TIMEOUT);
+    return;  // this row's h and x stay as they were; the call count does not advance
+  }
+  const float rstd = rsqrtf(tot / (float)p.N + p.eps);
+  uint16_t* xrow = p.x + (long long)m * p.ldx;
+  for (int lc = threadIdx.x * 8; lc < cols; lc += blockDim.x * 8) {
+    const int c = c_begin + lc;
+    const uint4 wv = *reinterpret_cast<const uint4*>(p.w + c);
+    uint16_t wb[8], ob[8], hb[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) hb[j] = f32_to_bf16(hs[lc + j]);
+    if (p.recv || p.partial) {
+      uint4 hv;
+      memcpy(&hv, hb, 16);
+      *reinterpret_cast<uint4*>(hrow + c) = hv;
+    }
+    memcpy(wb, &wv, 16);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ob[j] = f32_to_bf16((hs[lc + j] * rstd) * bf16_to_f32(wb[j]));
+    uint4 ov;
+    memcpy(&ov, ob, 16);
+    *reinterpret_cast<uint4*>(xrow + c) = ov;
+  }
+  if (p.recv) {  // the last CTA of the grid advances the slot's call count
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      if (atomicAdd(p.done, 1u) == gridDim.x * gridDim.y - 1) {
+        *p.done = 0u;
+        *p.epoch = tag;
+      }
+    }
+  }
+}
+
 struct RopeParams {
   const uint16_t* qkv;
   long long ld_qkv;
@@ -335,6 +476,28 @@ static int launch_norm(NormParams& p, int64_t M, int64_t N, void* stream) {
   if ((p.ldh % 8) || (p.ldx % 8) || ((uintptr_t)p.h & 15) || ((uintptr_t)p.x & 15) || ((uintptr_t)p.w & 15))
     return WAL_ERR_ALIGNMENT;
   p.N = (int)N;
+  if (N % (8 * kNormCluster) == 0 && N >= 1024) {
+    // one cluster of kNormCluster CTAs per row, 8 columns per thread
+    const int cols = (int)N / kNormCluster;
+    int threads = ((cols / 8 + 31) / 32) * 32;
+    if (threads > 256) threads = 256;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kNormCluster, (unsigned)M);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = cols * 4;
+    cfg.stream = static_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = kNormCluster;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    if (cudaLaunchKernelEx(&cfg, residual_rmsnorm_cluster_kernel, p) != cudaSuccess) return WAL_ERR_CUDA;
+    return cudaGetLastError() == cudaSuccess ? WAL_OK : WAL_ERR_CUDA;
+  }
   const int smem = (int)N * 4;
   if (smem > 48 * 1024 &&
       cudaFuncSetAttribute(residual_rmsnorm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
