@@ -254,38 +254,55 @@ DECODE_LEGS = {
 }
 
 
-def tp_logits_error(st, shape, which: str, rank: int, world: int, dev: torch.device, context: int) -> float | None:
-    """Relative max error of one tensor-parallel decode step's logits against the unsharded stack (rank 0).
-
-    Every rank holds a shard of the same seeded model and a slice of the same
-    cache, so the sharded step (push exchange) must reproduce the single-GPU
-    step up to the order of the fp32 partial sums.
-    """
-    import torch.distributed as dist
-
-    from wal2026_b200.llama import rvq_llama
-
-    batch = 1
-    gen = torch.Generator(device=dev).manual_seed(17)
-    tokens = torch.randint(0, shape.vocab, (batch,), device=dev, generator=gen)
-    st.allocate_cache(batch, context + 1, consistent=True, seed=19)
+def _tp_step_logits(st, shape, dev, context: int, tokens, push: bool) -> torch.Tensor:
+    st.allocate_cache(int(tokens.shape[0]), context + 1, consistent=True, seed=19)
     cos, sin = st.rope_tables(context)
-    st.enable_push_exchange(batch)
-    logits = st.decode_step_fused(tokens, context, cos, sin, exchange="push").float()
+    if push:
+        st.enable_push_exchange(int(tokens.shape[0]))
+    logits = st.decode_step_fused(tokens, context, cos, sin, exchange="push" if push else "nccl").float()
     torch.cuda.synchronize()
     st.k_cache, st.v_cache = [], []
-    torch.cuda.empty_cache()
-    err = None
-    if rank == 0:
-        full = rvq_llama(shape, device=dev, seed=0)
-        full.allocate_cache(batch, context + 1, consistent=True, seed=19)
-        ref = full.decode_step_fused(tokens, context, cos, sin).float()
-        torch.cuda.synchronize()
-        err = float((logits - ref).abs().max() / ref.abs().max())
-        del full, ref
-        torch.cuda.empty_cache()
-    dist.barrier()
-    return err
+    return logits
+
+
+def tp_logits_check(st, shape, which: str, rank: int, world: int, dev: torch.device, context: int) -> dict | None:
+    """One tensor-parallel decode step's logits against the unsharded stack (rank 0 reports).
+
+    Every rank holds a shard of the same seeded model and a slice of the same
+    cache, so the sharded step (push exchange) equals the single-GPU step up to
+    the order of the fp32 partial sums, whose bf16 roundings then propagate
+    through the layers.  Reported for the whole stack and, to show the
+    per-layer size of that effect, for a one-layer stack of the same shape.
+    """
+    import dataclasses
+
+    import torch.distributed as dist
+
+    from wal2026_b200.llama import TPContext, rvq_llama
+
+    gen = torch.Generator(device=dev).manual_seed(17)
+    tokens = torch.randint(0, shape.vocab, (1,), device=dev, generator=gen)
+    res = {}
+    one = dataclasses.replace(shape, layers=1)
+    tp = TPContext(rank, world, dist.group.WORLD)
+    for label, shp, stack in (("stack", shape, st), ("one_layer", one, None)):
+        own = stack if stack is not None else rvq_llama(shp, device=dev, seed=0, tp=tp)
+        logits = _tp_step_logits(own, shp, dev, context, tokens, push=True)
+        if stack is None:
+            own.close()
+            del own
+        if rank == 0:
+            full = rvq_llama(shp, device=dev, seed=0)
+            ref = _tp_step_logits(full, shp, dev, context, tokens, push=False)
+            del full
+            torch.cuda.empty_cache()
+            res[label] = {
+                "max_rel_err": round(float((logits - ref).abs().max() / ref.abs().max()), 6),
+                "cosine": round(float(torch.nn.functional.cosine_similarity(logits, ref, dim=-1).min()), 6),
+                "top1_agree": bool((logits.argmax(-1) == ref.argmax(-1)).all()),
+            }
+        dist.barrier()
+    return res if rank == 0 else None
 
 
 def run_decode(args, rank: int, world: int, dev: torch.device, which: str = "8b") -> dict:
@@ -330,8 +347,7 @@ def run_decode(args, rank: int, world: int, dev: torch.device, which: str = "8b"
             if kind == "rvq":
                 out["rvq_projection_bytes_per_rank"] = st.linear_bytes()
                 if world > 1 and args.tp_check:
-                    err = tp_logits_error(st, shape, which, rank, world, dev, context)
-                    out["tp_logits_max_rel_err_vs_unsharded"] = None if err is None else round(err, 6)
+                    out["tp_logits_vs_unsharded"] = tp_logits_check(st, shape, which, rank, world, dev, context)
             st.close()
             del st
             torch.cuda.empty_cache()

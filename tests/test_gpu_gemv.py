@@ -283,3 +283,4 @@ def test_prefill_gemm_at_8b_layer_shapes(rows, K):
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     assert_bf16_within_ulp(bits_of(yb)[:, sample], orc.f32_to_bf16_bits(ref))
+

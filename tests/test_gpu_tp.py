@@ -8,7 +8,6 @@ and keeps its shard, so rank 0 can also build the unsharded model.
 from __future__ import annotations
 
 import os
-import socket
 
 import pytest
 import torch
@@ -18,23 +17,18 @@ pytestmark = pytest.mark.gpu
 TINY_ARGS = dict(layers=2, hidden=1024, mlp=2048, heads=8, kv_heads=4, vocab=2048)
 
 
-def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
-def _rank_main(rank: int, size: int, port: int, kind: str, batch: int, out) -> None:
+def _rank_main(rank: int, size: int, store_path: str, kind: str, batch: int, out) -> None:
     import datetime
 
     import torch.distributed as dist
 
     from wal2026_b200.llama import LlamaShape, TPContext, dense_llama, rvq_llama
 
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=size, device_id=dev,
+    # a file rendezvous: no TCP port to collide with the previous case's
+    dist.init_process_group("nccl", init_method=f"file://{store_path}", rank=rank, world_size=size, device_id=dev,
                             timeout=datetime.timedelta(seconds=60))
     try:
         shape = LlamaShape(**TINY_ARGS)
@@ -79,13 +73,13 @@ def _rank_main(rank: int, size: int, port: int, kind: str, batch: int, out) -> N
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 @pytest.mark.parametrize("kind,batch", [("rvq", 1), ("rvq", 5), ("dense", 2)])
-def test_tp2_decode_matches_unsharded(kind, batch):
+def test_tp2_decode_matches_unsharded(kind, batch, tmp_path):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     out = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, kind, batch, out)) for r in range(2)]
+    store = str(tmp_path / "rendezvous")
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, store, kind, batch, out)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
