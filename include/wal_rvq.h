@@ -269,6 +269,20 @@ WAL_API int wal_rvq_dequant_corrected(const wal_rvq_layer* layer, const wal_rvq_
                               int64_t ldw, int w_dtype, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Encoder: nearest codebook entry (reference src/block_vq.py:180-196,
+ * _assign_to_codebook, the hot loop of its k-means fit and of every stage's
+ * assignment).  blocks: device fp32 [n][d]; codebook: device fp32
+ * [num_entries][d]; ids: device int32 [n] receives the entry minimising
+ * ||x||^2 + ||c||^2 - 2 x.c (fp32; the first of equal minima), min_dist
+ * (device fp32 [n] or NULL) that distance.  d in {4, 8, 16, 32}; the codebook
+ * must fit in shared memory ((num_entries * (d + 1)) * 4 <= 227 KB).  A block
+ * whose two best entries lie within a few fp32 units of each other can be
+ * assigned differently from the reference's CPU matrix product.
+ * ------------------------------------------------------------------------ */
+WAL_API int wal_rvq_assign(const float* blocks, int64_t n, int32_t d, const float* codebook, int32_t num_entries,
+                   int32_t* ids, float* min_dist, void* stream);
+
+/* ------------------------------------------------------------------------
  * ID-route linear (reference src/runtime.py:52-97, PackedIDRouteLinear; fused
  * Triton kernel src/triton_id_matmul.py:19-67): one int16 id per weight into
  * a scalar fp16 route table codebook_sum[num_routes].  The weight is, bit for

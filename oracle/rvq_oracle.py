@@ -324,3 +324,18 @@ def idroute_weight_bits(ids: np.ndarray, codebook_sum_bits: np.ndarray, row_scal
     w16 = idroute_weight_f16_bits(ids, codebook_sum_bits, row_scale_bits).view(np.float16)
     return f32_to_bf16_bits(w16.astype(np.float32))
 
+
+
+# ---------------------------------------------------------------------------
+# Encoder (reference src/block_vq.py:180-196, _assign_to_codebook)
+# ---------------------------------------------------------------------------
+def assign_to_codebook(blocks: np.ndarray, codebook: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """Nearest entry per block: argmin of ||x||^2 + ||c||^2 - 2 x.c in float32 (first minimum on ties)."""
+    x = np.asarray(blocks, dtype=np.float32)
+    c = np.asarray(codebook, dtype=np.float32)
+    xsq = (x * x).sum(axis=1, dtype=np.float32)[:, None]
+    csq = (c * c).sum(axis=1, dtype=np.float32)[None, :]
+    dot = (x @ c.T).astype(np.float32)
+    dist = ((xsq + csq).astype(np.float32) - np.float32(2.0) * dot).astype(np.float32)
+    ids = dist.argmin(axis=1)
+    return ids, dist[np.arange(x.shape[0]), ids]

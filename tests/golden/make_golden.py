@@ -295,6 +295,32 @@ def correction_cases(ref_runtime, ref_block_vq) -> None:
                         [3], 66, None, ref_runtime, ref_io)
 
 
+def encoder_cases(ref_block_vq) -> None:
+    """The reference's own k-means assignment, fit and encoder (src/block_vq.py:180-531) on seeded inputs."""
+    g = torch.Generator().manual_seed(71)
+    blocks = torch.randn(4096, 8, generator=g) * 0.3
+    sample = blocks[:2048].clone()
+    codebook = ref_block_vq._fit_kmeans(sample, codebook_size=64, iters=4)
+    ids, dist = ref_block_vq._assign_to_codebook(blocks, codebook)
+    out = {"blocks": blocks.numpy(), "sample_rows": np.array(2048), "fit_entries": np.array(64),
+           "fit_iters": np.array(4), "fit_codebook": codebook.numpy(), "ids": ids.numpy(), "min_dist": dist.numpy()}
+    weight = torch.randn(96, 256, generator=g) * 0.02
+    e1 = ref_block_vq.encode_block_residual_vq(weight, block_size=8, codebook_size=64, num_stages=2, kmeans_iters=3)
+    e2 = ref_block_vq.encode_block_residual_vq(weight, block_size=8, codebook_size=64, num_stages=2, product_splits=2,
+                                               stages_per_split=(2, 1), normalize_blocks="amax", kmeans_iters=3)
+    out["weight"] = weight.numpy()
+    for tag, e in (("plain", e1), ("split", e2)):
+        for si, (ids_s, cb_s) in enumerate(zip(e.stage_ids, e.codebooks)):
+            out[f"{tag}_ids{si}"] = ids_s.numpy()
+            out[f"{tag}_book{si}"] = cb_s.numpy()
+        out[f"{tag}_rho"] = e.row_scale.numpy()
+        out[f"{tag}_rel_mse"] = np.array(e.sample_rel_mse)
+        if e.block_scale is not None:
+            out[f"{tag}_block_scale"] = e.block_scale.numpy()
+    np.savez_compressed(HERE / "encoder.npz", **out)
+    print("wrote encoder.npz")
+
+
 def stage_drop_cases(ref_runtime, ref_block_vq) -> None:
     run_stage_drop_case("stage_drop_r3", single_group(synthetic.rvq_encoding(64, 192, d=8, R=3, seed=31)), 2,
                         [1, 5], 31, ref_runtime, ref_block_vq)
@@ -314,7 +340,7 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path of the reference checkout")
     ap.add_argument("--skip-full", action="store_true")
-    ap.add_argument("--only", default="", help="comma-separated groups to (re)generate: stage_drop, dtype, corrections")
+    ap.add_argument("--only", default="", help="comma-separated groups to (re)generate: stage_drop, dtype, corrections, encoder")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     from src import block_vq as ref_block_vq  # type: ignore
@@ -329,6 +355,8 @@ def main() -> None:
             dtype_cases(ref_runtime, ref_block_vq)
         if "corrections" in only:
             correction_cases(ref_runtime, ref_block_vq)
+        if "encoder" in only:
+            encoder_cases(ref_block_vq)
         return
     small = [
         ("small_r2_d8", single_group(synthetic.rvq_encoding(37, 64, d=8, R=2, seed=11)), [1, 3], 11, True),
@@ -384,6 +412,7 @@ def main() -> None:
     stage_drop_cases(ref_runtime, ref_block_vq)
     dtype_cases(ref_runtime, ref_block_vq)
     correction_cases(ref_runtime, ref_block_vq)
+    encoder_cases(ref_block_vq)
     if args.skip_full:
         return
     run_case("cfg0", synthetic.cfg0_encoding(0), [1, 4, 16], 0, None, ref_runtime, ref_block_vq, full=False)

@@ -126,6 +126,7 @@ SIGNATURES: dict[str, tuple] = {
     "wal_rvq_gemv": (_c_int, [_LP, _vp, _c_i64, _c_i64, _vp, _c_i64, _c_int, _vp]),
     "wal_rvq_gemv_typed": (_c_int, [_LP, _vp, _c_int, _c_i64, _c_i64, _vp, _c_i64, _c_int, _c_int, _c_int, _vp]),
     "wal_rvq_dequant_typed": (_c_int, [_LP, _vp, _c_i64, _c_int, _vp]),
+    "wal_rvq_assign": (_c_int, [_vp, _c_i64, ctypes.c_int32, _vp, ctypes.c_int32, _vp, _vp, _vp]),
     "wal_rvq_gemv_corrected": (_c_int, [_LP, ctypes.POINTER(Corrections), _vp, _c_int, _c_i64, _c_i64, _vp, _c_i64,
                                         _c_int, _vp]),
     "wal_rvq_dequant_corrected": (_c_int, [_LP, ctypes.POINTER(Corrections), _vp, _c_i64, _c_int, _vp]),
