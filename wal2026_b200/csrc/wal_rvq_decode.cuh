@@ -357,16 +357,31 @@ __device__ void stage_codebooks_finish(uint8_t* cb, int entries, const float* sc
   constexpr bool kConvert = NM == kFast || R == 1;
   if constexpr (!REPL) {
     if constexpr (kConvert) {
+      // plain layout: entry e of stage s is D contiguous values, so the
+      // stage's table is one contiguous run converted 16 bytes at a time
+      // (with the scale choice hoisted out of the loop: large routed tables
+      // hold thousands of entries and this runs on every launch)
 #pragma unroll
       for (int s = 0; s < R; ++s) {
-        for (int e = threadIdx.x; e < entries; e += blockDim.x) {
-#pragma unroll
-          for (int j = 0; j < L::kPieces; ++j) {
-            uint2* pv = reinterpret_cast<uint2*>(cb + L::piece_offset(s, e, j, 0, entries));
-            uint2 v = *pv;
+        uint4* run = reinterpret_cast<uint4*>(cb + L::stage_offset(s));
+        const int n16 = entries * D / 8;
+        if (scales) {
+          for (int i = threadIdx.x; i < n16; i += blockDim.x) {
+            uint4 v = run[i];
             v.x = staged_word<R, NM, F16>(v.x, scales, s);
             v.y = staged_word<R, NM, F16>(v.y, scales, s);
-            *pv = v;
+            v.z = staged_word<R, NM, F16>(v.z, scales, s);
+            v.w = staged_word<R, NM, F16>(v.w, scales, s);
+            run[i] = v;
+          }
+        } else {
+          for (int i = threadIdx.x; i < n16; i += blockDim.x) {
+            uint4 v = run[i];
+            v.x = staged_word<R, NM, F16>(v.x, nullptr, s);
+            v.y = staged_word<R, NM, F16>(v.y, nullptr, s);
+            v.z = staged_word<R, NM, F16>(v.z, nullptr, s);
+            v.w = staged_word<R, NM, F16>(v.w, nullptr, s);
+            run[i] = v;
           }
         }
       }
