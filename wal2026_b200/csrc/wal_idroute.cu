@@ -161,6 +161,9 @@ __global__ void __launch_bounds__(kT, 1) idroute_gemv_kernel(const __grid_consta
     }
   }
   __syncthreads();
+  // the next kernel of the stream may launch now: its CTAs take each SM as this
+  // grid's CTA there exits, overlapping their prologue with this grid's tail
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 
   const uint32_t tbl_lane = smem_u32(tbl) + (COMPACT ? 0u : (uint32_t)((lane & (copies - 1)) * 4));
   uint32_t xsa[MT];
@@ -255,7 +258,6 @@ __global__ void __launch_bounds__(kT, 1) idroute_gemv_kernel(const __grid_consta
     }
     __syncthreads();
   }
-  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
   cp_wait<0>();
 }
 
