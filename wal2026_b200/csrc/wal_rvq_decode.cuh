@@ -325,100 +325,160 @@ __device__ __forceinline__ uint32_t staged_word(uint32_t h2, const float* scales
   }
 }
 
+// 16-byte unit i of one stage's replicated table: entry e, run (16-byte
+// piece of the entry) and byte offset inside the entry's 256-byte row.  The
+// units of an entry are numbered so that consecutive lanes write consecutive
+// 16-byte slots of a 128-byte row (copies of a run side by side), so a warp's
+// stores into the table never conflict.
+template <int D>
+struct ReplUnit {
+  static constexpr int kRuns = D / 8;
+  static constexpr int kCopies = D == 8 ? 8 : 4;
+  static constexpr int kUnits = kRuns * kCopies;  // per entry: 8 (D = 8, 16) or 16 (D = 32)
+  static constexpr int kCopyStride = D == 8 ? 16 : 32;
+  // copy c of the run sits at off; copy 0 of the same run at off - c * kCopyStride
+  __device__ __forceinline__ static void decode(int i, int& e, int& c, int& off) {
+    e = i / kUnits;
+    const int u = i - e * kUnits;
+    if constexpr (D == 32) {  // half h, copy c, run-in-half b: h * 128 + c * 32 + b * 16
+      c = (u >> 1) & 3;
+      off = (u >> 3) * 128 + c * 32 + (u & 1) * 16;
+    } else if constexpr (D == 16) {  // copy c, run: c * 32 + run * 16
+      c = u >> 1;
+      off = u * 16;
+    } else {  // copy c: c * 16
+      c = u;
+      off = u * 16;
+    }
+  }
+};
+
+__device__ __forceinline__ uint4 ldg16_hint(const void* p, uint64_t pol) {
+  uint4 v;
+  asm("ld.global.nc.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;\n"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p), "l"(pol));
+  return v;
+}
+
+template <int R, int NM, bool F16>
+__device__ __forceinline__ void staged_vec(uint4& v, const float* scales, int s) {
+  v.x = staged_word<R, NM, F16>(v.x, scales, s);
+  v.y = staged_word<R, NM, F16>(v.y, scales, s);
+  v.z = staged_word<R, NM, F16>(v.z, scales, s);
+  v.w = staged_word<R, NM, F16>(v.w, scales, s);
+}
+
 // Stage R codebooks of one group (fp16 [R][entries][D] in global memory) into
 // shared memory, in two steps so the copies overlap other prologue work:
 //   stage_codebooks_issue  - every 16-byte run of an entry is fetched with
-//                            cp.async into its copy-0 position (not committed);
-//   stage_codebooks_finish - after the caller's cp.async wait + __syncthreads,
-//                            the words are converted in place (staged_word:
-//                            pre-rounding of one-stage tables, fast-mode
-//                            tables) and copy 0 is expanded into the other
-//                            copies.  Follow it with __syncthreads().
-template <int D, int R, bool REPL>
+//                            cp.async into its copy-0 position (not committed;
+//                            plain layouts that need converting are skipped);
+//   stage_codebooks_finish - after the caller's cp.async wait + __syncthreads:
+//                            replicated layouts: copy 0 is expanded into the
+//                            other copies, converted on the way when the
+//                            numerics need it (staged_word: pre-rounding of
+//                            one-stage tables, fast-mode tables), with lanes
+//                            mapped so that each warp store fills whole
+//                            128-byte rows (copy 0 itself is converted last,
+//                            from copy 1); plain layouts that need converting
+//                            are read here with 16-byte loads, 8 per thread in
+//                            flight, converted in registers and stored once.
+//                            Follow it with __syncthreads().
+// (Expanding entry by entry made the 32 lanes of a warp store into the same
+// four banks: 2.2 us per launch for a d = 8 table; fetching every copy from
+// global memory instead made all CTAs re-read the same few L2 lines eight
+// times over and tripled the launch; landing a 128 KB routed table first and
+// converting it in place cost 1.3 us.)
+template <int D, int R, bool REPL, int NM = kExact, bool F16 = false>
 __device__ void stage_codebooks_issue(uint8_t* cb, const uint16_t* __restrict__ books, int entries) {
   using L = CbLayout<D, REPL>;
-  constexpr int kRuns = D / 8;  // 16-byte runs per entry (two pieces each)
-  const uint32_t base = smem_u32(cb);
-  const uint64_t keep = l2_policy_evict_last();
+  constexpr bool kConvert = NM == kFast || R == 1;
+  if constexpr (REPL || !kConvert) {
+    constexpr int kRuns = D / 8;
+    const uint32_t base = smem_u32(cb);
+    const uint64_t keep = l2_policy_evict_last();
 #pragma unroll
-  for (int s = 0; s < R; ++s) {
-    const uint16_t* sbooks = books + (size_t)s * entries * D;
-    for (int e = threadIdx.x; e < entries; e += blockDim.x) {
+    for (int s = 0; s < R; ++s) {
+      const uint16_t* sbooks = books + (size_t)s * entries * D;
+      for (int e = threadIdx.x; e < entries; e += blockDim.x) {
 #pragma unroll
-      for (int run = 0; run < kRuns; ++run)
-        cp_async_16_hint(base + L::piece_offset(s, e, 2 * run, 0, entries), sbooks + (size_t)e * D + 8 * run, keep);
+        for (int run = 0; run < kRuns; ++run)
+          cp_async_16_hint(base + L::piece_offset(s, e, 2 * run, 0, entries), sbooks + (size_t)e * D + 8 * run, keep);
+      }
     }
   }
 }
 
 template <int D, int R, bool REPL, int NM = kExact, bool F16 = false>
-__device__ void stage_codebooks_finish(uint8_t* cb, int entries, const float* scales = nullptr) {
+__device__ void stage_codebooks_finish(uint8_t* cb, const uint16_t* __restrict__ books, int entries,
+                                       const float* scales = nullptr) {
   using L = CbLayout<D, REPL>;
   constexpr bool kConvert = NM == kFast || R == 1;
-  if constexpr (!REPL) {
-    if constexpr (kConvert) {
-      // plain layout: entry e of stage s is D contiguous values, so the
-      // stage's table is one contiguous run converted 16 bytes at a time
-      // (with the scale choice hoisted out of the loop: large routed tables
-      // hold thousands of entries and this runs on every launch)
+  if constexpr (REPL) {
+    using U = ReplUnit<D>;
+    auto expand = [&](const float* sc) {
 #pragma unroll
       for (int s = 0; s < R; ++s) {
-        uint4* run = reinterpret_cast<uint4*>(cb + L::stage_offset(s));
+        uint8_t* sbase = cb + L::stage_offset(s);
+        for (int i = threadIdx.x; i < entries * U::kUnits; i += blockDim.x) {
+          int e, c, off;
+          U::decode(i, e, c, off);
+          if (c == 0) continue;  // the source
+          uint8_t* row = sbase + e * 256;
+          uint4 v = *reinterpret_cast<const uint4*>(row + off - c * U::kCopyStride);
+          if constexpr (kConvert) staged_vec<R, NM, F16>(v, sc, s);
+          *reinterpret_cast<uint4*>(row + off) = v;
+        }
+      }
+    };
+    if (scales) expand(scales);
+    else expand(nullptr);
+    if constexpr (kConvert) {
+      __syncthreads();  // every copy-0 read above is done; copy 1 holds the converted runs
+      constexpr int kRuns = D / 8;
+#pragma unroll
+      for (int s = 0; s < R; ++s) {
+        uint8_t* sbase = cb + L::stage_offset(s);
+        for (int i = threadIdx.x; i < entries * kRuns; i += blockDim.x) {
+          const int e = i / kRuns, run = i - e * kRuns;
+          const int off0 = D == 32 ? (run >> 1) * 128 + (run & 1) * 16 : run * 16;
+          uint8_t* row = sbase + e * 256;
+          *reinterpret_cast<uint4*>(row + off0) = *reinterpret_cast<const uint4*>(row + off0 + U::kCopyStride);
+        }
+      }
+    }
+  } else if constexpr (kConvert) {
+    // plain layout: entry e of stage s is D contiguous values, so a stage is
+    // one contiguous run of 16-byte vectors
+    constexpr int kBatch = 8;
+    const uint64_t keep = l2_policy_evict_last();
+    auto load_convert = [&](const float* sc) {
+#pragma unroll
+      for (int s = 0; s < R; ++s) {
+        const uint4* src = reinterpret_cast<const uint4*>(books + (size_t)s * entries * D);
+        uint4* dst = reinterpret_cast<uint4*>(cb + L::stage_offset(s));
         const int n16 = entries * D / 8;
-        if (scales) {
-          for (int i = threadIdx.x; i < n16; i += blockDim.x) {
-            uint4 v = run[i];
-            v.x = staged_word<R, NM, F16>(v.x, scales, s);
-            v.y = staged_word<R, NM, F16>(v.y, scales, s);
-            v.z = staged_word<R, NM, F16>(v.z, scales, s);
-            v.w = staged_word<R, NM, F16>(v.w, scales, s);
-            run[i] = v;
+        for (int i0 = threadIdx.x; i0 < n16; i0 += kBatch * blockDim.x) {
+          uint4 v[kBatch];
+#pragma unroll
+          for (int k = 0; k < kBatch; ++k) {
+            const int i = i0 + k * blockDim.x;
+            if (i < n16) v[k] = ldg16_hint(src + i, keep);
           }
-        } else {
-          for (int i = threadIdx.x; i < n16; i += blockDim.x) {
-            uint4 v = run[i];
-            v.x = staged_word<R, NM, F16>(v.x, nullptr, s);
-            v.y = staged_word<R, NM, F16>(v.y, nullptr, s);
-            v.z = staged_word<R, NM, F16>(v.z, nullptr, s);
-            v.w = staged_word<R, NM, F16>(v.w, nullptr, s);
-            run[i] = v;
+#pragma unroll
+          for (int k = 0; k < kBatch; ++k) {
+            const int i = i0 + k * blockDim.x;
+            if (i < n16) {
+              staged_vec<R, NM, F16>(v[k], sc, s);
+              dst[i] = v[k];
+            }
           }
         }
       }
-    }
-    return;  // raw multi-stage fp16 tables, single copy: nothing to do
-  } else {
-    // An entry's copy 0 is D / 8 runs of 16 bytes (D = 32: two per 128-byte
-    // half); copy c sits c * kCopyStride further.
-    constexpr int kRuns = D / 8;
-    constexpr int kCopyStride = D == 8 ? 16 : 32;
-#pragma unroll
-    for (int s = 0; s < R; ++s) {
-      for (int e = threadIdx.x; e < entries; e += blockDim.x) {
-        uint8_t* base = cb + L::stage_offset(s) + e * 256;
-        uint4 v[kRuns];
-#pragma unroll
-        for (int run = 0; run < kRuns; ++run) {
-          const int off = D == 32 ? (run >> 1) * 128 + (run & 1) * 16 : run * 16;
-          v[run] = *reinterpret_cast<const uint4*>(base + off);
-          if constexpr (kConvert) {
-            v[run].x = staged_word<R, NM, F16>(v[run].x, scales, s);
-            v[run].y = staged_word<R, NM, F16>(v[run].y, scales, s);
-            v[run].z = staged_word<R, NM, F16>(v[run].z, scales, s);
-            v[run].w = staged_word<R, NM, F16>(v[run].w, scales, s);
-            *reinterpret_cast<uint4*>(base + off) = v[run];
-          }
-        }
-#pragma unroll
-        for (int c = 1; c < L::kCopies; ++c) {
-#pragma unroll
-          for (int run = 0; run < kRuns; ++run) {
-            const int off = D == 32 ? (run >> 1) * 128 + (run & 1) * 16 : run * 16;
-            *reinterpret_cast<uint4*>(base + c * kCopyStride + off) = v[run];
-          }
-        }
-      }
-    }
+    };
+    if (scales) load_convert(scales);
+    else load_convert(nullptr);
   }
 }
 
@@ -481,10 +541,10 @@ __device__ void stage_codebooks(uint8_t* cb, const uint16_t* __restrict__ books,
     stage_codebooks_scaled<D, R>(cb, books, scales, entries);
     return;
   }
-  stage_codebooks_issue<D, R, REPL>(cb, books, entries);
+  stage_codebooks_issue<D, R, REPL, NM, F16>(cb, books, entries);
   cp_async_wait_all();
   __syncthreads();
-  stage_codebooks_finish<D, R, REPL, NM, F16>(cb, entries, scales);
+  stage_codebooks_finish<D, R, REPL, NM, F16>(cb, books, entries, scales);
 }
 
 // ---------------------------------------------------------------------------

@@ -55,6 +55,7 @@ struct GemvParams {
   int wpt;
   int num_groups;
   int pdl;                               // launched with programmatic dependent launch
+  int early_release;                     // release the next kernel after the prologue (grid leaves SMs idle)
   int wpt_shift;                         // log2(wpt)
   int auto_tpc;                          // tiles per CTA when wpt was chosen automatically, else 0
   int group_tile_start[kMaxGroups + 1];  // first tile of each group, plus the total
@@ -379,7 +380,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
   // groups: 0 = codebooks, 1..kRing-1 = first id chunks, kRing = activations
   const uint16_t* gbooks = p.codebooks + (size_t)group * R * p.entries * D;
   const float* gscales = p.stage_scales ? p.stage_scales + (size_t)group * R : nullptr;
-  if constexpr (!kF32) stage_codebooks_issue<D, R, REPL>(cb, gbooks, p.entries);
+  if constexpr (!kF32) stage_codebooks_issue<D, R, REPL, NM, F16>(cb, gbooks, p.entries);
   cp_async_commit();
 #pragma unroll 1
   for (int s = 0; s < kRing - 1; ++s) issue();
@@ -388,7 +389,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
   } else {
     cp_async_wait<kRing - 1>();  // codebooks landed
     __syncthreads();
-    stage_codebooks_finish<D, R, REPL, NM, F16>(cb, p.entries, gscales);
+    stage_codebooks_finish<D, R, REPL, NM, F16>(cb, gbooks, p.entries, gscales);
   }
   if (p.pdl) grid_dependency_wait();  // x (and y) belong to the previous kernel in the stream
   const uint64_t x_pol = l2_policy_evict_last();
@@ -433,12 +434,14 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
   const unsigned tag = p.push_ranks > 0 ? *reinterpret_cast<const volatile unsigned*>(p.push_epoch) + 1u : 0u;
   cp_async_wait<0>();
   __syncthreads();
-  // Release the next kernel of the stream now: it is scheduled once every CTA
-  // of this grid has issued this (so all of them are resident), and its CTAs
-  // take each SM as soon as this grid's CTA there exits, so its weight
-  // prologue overlaps the CTAs of this grid that finish last (grids of 1-2
-  // tiles per CTA: 8B o/down shapes 9.8 -> 8.3 and 19.9 -> 18.3 us per launch).
-  if (p.pdl) grid_dependents_launch();
+  // A grid smaller than the GPU releases the next kernel of the stream now:
+  // that kernel is scheduled once every CTA of this grid has issued this (so
+  // all of them are resident) and its CTAs start their weight prologue on the
+  // SMs this grid leaves idle (cfg0 2048 x 2048, 128 CTAs: 6.7 -> 5.5 us per
+  // launch).  A full grid releases it after its main loop instead: released
+  // early, the next kernel's CTAs sit resident beside this grid's, and a
+  // decode step of the 8B stack measured 1.7% slower.
+  if (p.pdl && p.early_release) grid_dependents_launch();
 
   // lane (r, q) feeds token 8 * i + r of n-tile i
   uint32_t xoff[MT];  // element offset of the lane's token row (unstaged activations)
@@ -588,6 +591,7 @@ __global__ void __launch_bounds__(GemvCfg<D, R, IDW, REPL, MT, XM>::kT)
         }
       }
     }
+    if (p.pdl && !p.early_release && k + 1 == rounds) grid_dependents_launch();
     // -- reduce the slot's wpt partial sums, add bias, write y ---------------
     if (!slot_live) continue;
     if (wpt == 1) {
@@ -783,7 +787,8 @@ void assign_ctas(GemvParams& p, int ctas) {
 }
 
 template <typename Kern>
-int persistent_grid(Kern kern, int threads, int smem, int num_ctas, GemvParams& p, int* grid_out) {
+int persistent_grid(Kern kern, int threads, int smem, int num_ctas, GemvParams& p, int* grid_out,
+                    int* capacity_out = nullptr) {
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return WAL_ERR_CUDA;
   cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
@@ -797,6 +802,7 @@ int persistent_grid(Kern kern, int threads, int smem, int num_ctas, GemvParams& 
   if (grid > p.num_tiles) grid = p.num_tiles;
   if (grid < p.num_groups) grid = p.num_groups;
   *grid_out = (int)grid;
+  if (capacity_out) *capacity_out = sms * per_sm;
   assign_ctas(p, (int)grid);
   return WAL_OK;
 }
@@ -843,9 +849,10 @@ static int run_gemv(GemvParams p, int num_ctas, cudaStream_t stream) {
   }
   if (smem > 227 * 1024) return WAL_ERR_UNSUPPORTED;
   if (p.wpt > C::kW) return WAL_ERR_INVALID_ARGUMENT;
-  int grid = 0;
-  const int st = persistent_grid(kern, C::kT, smem, num_ctas, p, &grid);
+  int grid = 0, capacity = 0;
+  const int st = persistent_grid(kern, C::kT, smem, num_ctas, p, &grid, &capacity);
   if (st != WAL_OK) return st;
+  p.early_release = grid < capacity ? 1 : 0;
   // the in-kernel id cursor is a 32-bit offset over one CTA's tiles
   for (int g = 0; g < p.num_groups; ++g)
     if ((long long)(p.tiles_q[g] + 1) * p.chunks * C::V * 256 >= (1LL << 31)) return WAL_ERR_UNSUPPORTED;
