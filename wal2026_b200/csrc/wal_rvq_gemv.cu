@@ -788,7 +788,7 @@ void assign_ctas(GemvParams& p, int ctas) {
 
 template <typename Kern>
 int persistent_grid(Kern kern, int threads, int smem, int num_ctas, GemvParams& p, int* grid_out,
-                    int* capacity_out = nullptr) {
+                    int* capacity_out = nullptr, bool pair_tiles = false) {
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return WAL_ERR_CUDA;
   cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
@@ -798,11 +798,19 @@ int persistent_grid(Kern kern, int threads, int smem, int num_ctas, GemvParams& 
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess)
     return WAL_ERR_CUDA;
   if (per_sm < 1) return WAL_ERR_UNSUPPORTED;
-  long long grid = num_ctas > 0 ? num_ctas : (long long)sms * per_sm;
+  const long long capacity = (long long)sms * per_sm;
+  long long grid = num_ctas > 0 ? num_ctas : capacity;
   if (grid > p.num_tiles) grid = p.num_tiles;
+  // Two tiles per CTA at most: pair every CTA's tiles rather than leave some
+  // CTAs one tile, so that the SMs left over are idle from the start and the
+  // next kernel's prologue runs on them (8B o and down shapes, 256 tiles:
+  // 128 CTAs 7.4 / 17.6 us against 148 CTAs 8.5 / 18.6 us; three or more
+  // tiles per CTA measured no better packed).
+  if (pair_tiles && num_ctas <= 0 && p.num_tiles > capacity && p.num_tiles <= 2 * capacity)
+    grid = (p.num_tiles + 1) / 2;
   if (grid < p.num_groups) grid = p.num_groups;
   *grid_out = (int)grid;
-  if (capacity_out) *capacity_out = sms * per_sm;
+  if (capacity_out) *capacity_out = (int)capacity;
   assign_ctas(p, (int)grid);
   return WAL_OK;
 }
@@ -813,21 +821,29 @@ int persistent_grid(Kern kern, int threads, int smem, int num_ctas, GemvParams& 
 using namespace wal;
 
 // Warps per tile for a CTA with tpc tiles: rounds of 16/wpt tiles, each round
-// ceil(chunks/wpt) chunks, plus a small reduction cost per round growing with wpt.
+// ceil(chunks/wpt) chunks, plus a small reduction cost per round growing with
+// wpt.  Splits within 5% of the cheapest are ranked by the warps the first
+// round keeps busy (8B gate/up, 13 tiles per CTA: 2 warps per tile, 16 warps
+// busy, 31.7 us against 33.2 us for one warp per tile, 13 warps busy).
 static int best_wpt(long long tpc, int chunks, int wmax) {
+  double cost[5];
+  long long busy[5];
+  int n = 0;
   double best = 1e30;
-  int wpt = 1;
-  for (int w = 1; w <= wmax; w *= 2) {
+  for (int w = 1; w <= wmax; w *= 2, ++n) {
     const long long slots = 16 / w;
     const long long rounds = (tpc + slots - 1) / slots;
     const long long cpw = (chunks + w - 1) / w;
-    const double cost = (double)rounds * ((double)cpw + 0.25 * (w > 1 ? 1 + w / 4.0 : 0.0));
-    if (cost < best - 1e-9) {
-      best = cost;
-      wpt = w;
-    }
+    cost[n] = (double)rounds * ((double)cpw + 0.25 * (w > 1 ? 1 + w / 4.0 : 0.0));
+    busy[n] = (tpc < slots ? tpc : slots) * w;
+    if (cost[n] < best) best = cost[n];
   }
-  return wpt;
+  int pick = -1;
+  for (int i = 0; i < n; ++i)
+    if (cost[i] <= best * 1.05 + 1e-9 &&
+        (pick < 0 || busy[i] > busy[pick] || (busy[i] == busy[pick] && cost[i] < cost[pick])))
+      pick = i;
+  return 1 << pick;
 }
 
 static int log2_pow2(int w) { return w == 1 ? 0 : w == 2 ? 1 : w == 4 ? 2 : w == 8 ? 3 : 4; }
@@ -850,7 +866,7 @@ static int run_gemv(GemvParams p, int num_ctas, cudaStream_t stream) {
   if (smem > 227 * 1024) return WAL_ERR_UNSUPPORTED;
   if (p.wpt > C::kW) return WAL_ERR_INVALID_ARGUMENT;
   int grid = 0, capacity = 0;
-  const int st = persistent_grid(kern, C::kT, smem, num_ctas, p, &grid, &capacity);
+  const int st = persistent_grid(kern, C::kT, smem, num_ctas, p, &grid, &capacity, true);
   if (st != WAL_OK) return st;
   p.early_release = grid < capacity ? 1 : 0;
   // the in-kernel id cursor is a 32-bit offset over one CTA's tiles
