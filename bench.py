@@ -481,7 +481,7 @@ def run_prefill(args, dev: torch.device, peaks: dict) -> dict:
     return {"workload": f"Llama-3-8B-shaped stack, 128 projection GEMMs at M={M} tokens (x bf16, y bf16)",
             "ms_per_step": round(ms, 3), "tokens_per_s": round(M / (ms / 1e3), 1), "tflops": round(tflops, 1),
             "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak, "unit": "TFLOP/s",
-                         "frac": round(tflops / peak, 4), "peak_source": src, "kernel": "rvq_gemm_kernel"},
+                         "frac": round(tflops / peak, 4), "peak_source": src, "kernel": "rvq_gemm_pair_kernel"},
             "gpu_launches": launches, "dense_bf16_cublas": dense}
 
 

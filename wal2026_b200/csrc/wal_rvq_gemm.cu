@@ -1,34 +1,28 @@
-// Prefill path (M >= 256 tokens): fused Block-RVQ decode -> shared memory ->
-// tcgen05.mma (5th-generation tensor cores, fp32 accumulators in TMEM).
+// Prefill path (M >= 128 tokens): fused Block-RVQ decode -> shared memory ->
+// tcgen05.mma on pairs of SMs (cta_group::2, fp32 accumulators in TMEM).
 //
-// One CTA computes a 512 (tokens) x 128 (output rows) tile of y over all of K
-// in stages of 64 columns (a CTA whose tokens end early loads and multiplies
-// only the 128-token tiles that hold tokens), with warp specialisation:
-//   warp 0      TMA producer: the activation tile [512 x 64] bf16 per stage
-//               (two 256-row boxes), cp.async.bulk.tensor into a
-//               128-byte-swizzled K-major buffer (no multicast), completion
-//               on full_a[stage];
-//   warp 1      MMA issuer (one elected lane): waits full_a + full_b, issues
-//               16 x tcgen05.mma (M=128, N=128, K=16: four token tiles share
-//               each decoded weight tile) into four TMEM accumulators and
-//               commits to empty[stage] (the stage's buffers are free again)
-//               and, after the last stage, to acc_full;
-//   warps 2..17 decoders: for every stage decode the 128 x 64 weight tile
-//               exactly (same arithmetic as the decode GEMV: fp32 stage sum,
-//               two bf16 roundings; four threads per row, two blocks each,
-//               ids loaded four stages ahead) straight into the swizzled
-//               K-major B buffer,
-//               fence it for the async proxy and arrive on full_b; then the
-//               epilogue: TMEM -> registers (tcgen05.ld 32x32b), bias,
-//               bf16/fp32 store of y.
-// Sharing each decoded tile over 512 tokens keeps the exact decode (CUDA
-// cores) below the tensor-core time of the same stage.  Measured on B200 with
-// the Llama-3-8B projections at 2048 tokens: this tile runs at 969 TFLOP/s; a
-// 256 x 256 tile (MMA N = 256, three stages: half the activation bytes from L2
-// per FLOP, twice the decode per FLOP) at 797; a persistent stream-K schedule
-// of the same tile (even (tile, k-block) shares per SM, split tiles summed
-// through a workspace) at 810-830, its per-segment epilogues and pipeline
-// refills costing more than the part-empty last wave it removes.
+// Two CTAs of a cluster compute a 256 (output rows) x 512 (tokens) tile of y
+// over all of K in stages of 64 columns.  Each CTA decodes its own 128 weight
+// rows exactly (the same arithmetic as the decode GEMV: fp32 stage sum, two
+// roundings in the weight type) into a 128-byte-swizzled K-major buffer and
+// fetches, by TMA (no multicast), its 128-token halves of the two activation
+// tiles; the leader's elected thread issues 256 x 256 x 16 pair MMAs that read
+// both CTAs' buffers and accumulate each CTA's 128 rows x 512 tokens in its own
+// TMEM.  Roles per CTA (576 threads): warp 0 TMA producer, warp 1 MMA issuer
+// (leader) or decode forwarder (peer), warps 2-17 decoders and then the
+// epilogue (TMEM -> registers -> bias -> bf16/fp16/fp32 stores of y).
+//
+// Why pairs: a single-CTA 128 x 128 x 16 MMA reads 8 KB of operands from
+// shared memory per 64 tensor cycles, the whole port of the SM, and the
+// activation fills and the decoders share that port; the single-CTA kernel
+// (512 tokens x 128 rows per CTA, four accumulators, two stages) spent 1730
+// cycles per 1024-cycle stage and ran the Llama-3-8B projections at 908
+// TFLOP/s.  Split over a pair, each SM reads half the operand bytes and
+// fetches half the activations per MMA cycle: 1470 cycles per stage, gate/up
+// 917 -> 1070 TFLOP/s, the 128-GEMM 8B prefill 908 -> 987 TFLOP/s.  Measured
+// before the pair kernel: a 256 x 256 single-CTA tile ran at 797 TFLOP/s and a
+// persistent stream-K schedule of the 512 x 128 tile at 810-830 (its
+// per-segment epilogues and refills cost more than the tail wave it removes).
 // The dense weight never reaches global memory.  Every mbarrier wait is
 // bounded by a %globaltimer deadline; on expiry the CTA records an error code
 // (if a status word was supplied), stops issuing work, drains and frees TMEM.
@@ -43,21 +37,13 @@
 namespace wal {
 namespace gemm {
 
-constexpr int kBM = 512;   // tokens per CTA: four 128-row MMA tiles share each decoded weight tile
-constexpr int kUM = 128;   // MMA M
-constexpr int kBN = 128;   // output rows per CTA (MMA N)
 constexpr int kBK = 64;
-constexpr int kStages = 2;
-constexpr int kTmaRows = 256;  // TMA box height: two boxes per activation stage
 constexpr int kDecodeWarps = 16;
 constexpr int kRowParts = kDecodeWarps * 32 / 128;  // decoder threads per weight row
 constexpr int kPartBlocks = 8 / kRowParts;          // d = 8 blocks per thread per 64-column stage
 constexpr int kThreads = (2 + kDecodeWarps) * 32;
-constexpr int kABytes = kBM * kBK * 2;  // 64 KB
-constexpr int kBBytes = kBN * kBK * 2;  // 16 KB
 constexpr int kCbCopyBytes = 256 * 16;  // one stage table, one copy
 constexpr int kCbCopies = 8;            // 8-lane phases of 16-byte gathers hit 8 distinct bank quads
-constexpr int kTmemCols = 512;          // four 128 x 128 fp32 accumulators
 constexpr unsigned long long kWaitNs = 2000000000ull;  // 2 s per wait, then give up
 
 struct GemmParams {
@@ -116,13 +102,6 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   }
 }
 
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-      ::"r"(dst), "l"(map), "r"(c0), "r"(c1), "r"(bar)
-      : "memory");
-}
-
 // UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row atoms 1024 B apart.
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
   uint64_t d = 0;
@@ -132,27 +111,6 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
   d |= (uint64_t)1 << 46;                          // descriptor version (sm_100)
   d |= (uint64_t)2 << 61;                          // layout: SWIZZLE_128B
   return d;
-}
-
-// Instruction descriptor: kind::f16, D = f32, A and B both bf16 (format 1) or
-// both fp16 (format 0), both K-major, M = 128, N = kBN.
-template <bool F16>
-__host__ __device__ constexpr uint32_t idesc() {
-  return (1u << 4) | (F16 ? 0u : (1u << 7) | (1u << 10)) | ((uint32_t)(kBN >> 3) << 17) |
-         ((uint32_t)(kUM >> 4) << 24);
-}
-
-template <bool F16>
-__device__ __forceinline__ void umma_16bit(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n}\n"
-      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc<F16>()), "r"(accumulate), "r"(0u)
-      : "memory");
-}
-
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -166,6 +124,89 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
         "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
       : "r"(taddr));
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ---- pair (cta_group::2) primitives -------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// every thread of both CTAs of the pair
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// the shared::cluster address of the same shared-memory offset in CTA `rank` of the pair
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait on a barrier that the other CTA of the pair (or its tensor
+// cores) arrives on.
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (globaltimer() - t0 > kWaitNs) return false;
+  }
+}
+
+// Activation box into this CTA's shared memory; the completed bytes count on
+// the barrier at `bar_cluster` (the leader CTA's), so one barrier covers the
+// boxes of both CTAs.  No multicast: each CTA fetches its own tokens.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                                 uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(map), "r"(c0), "r"(c1), "r"(bar_cluster)
+      : "memory");
+}
+
+// Pair MMA: D[256 x 256] (+)= A[256 x 16] B[256 x 16]^T, A rows 0-127 and B
+// rows 0-127 from the leader's shared memory, rows 128-255 from the peer's,
+// D rows 0-127 in the leader's TMEM and 128-255 in the peer's (same columns).
+template <bool F16>
+__host__ __device__ constexpr uint32_t idesc_pair() {
+  return (1u << 4) | (F16 ? 0u : (1u << 7) | (1u << 10)) | ((uint32_t)(256 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+}
+
+template <bool F16>
+__device__ __forceinline__ void umma_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n}\n"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc_pair<F16>()), "r"(accumulate), "r"(0u)
+      : "memory");
+}
+
+// arrive on the barrier at this offset in both CTAs once the pair MMAs issued
+// so far have completed
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"((uint16_t)3)
+      : "memory");
 }
 
 // Decode the weights of one output row for blocks u0 .. u0 + kPartBlocks - 1
@@ -226,38 +267,75 @@ __device__ __forceinline__ void decode_stage_part(uint32_t bsm_row, int nsw, con
   }
 }
 
+// ---------------------------------------------------------------------------
+// Pair kernel (cta_group::2): two CTAs of a cluster on neighbouring SMs compute
+// a 256 (output rows) x 512 (tokens) tile of y^T as 256 x 256 x 16 pair MMAs:
+// each CTA decodes its own 128 weight rows (the MMA A operand, M = 256 over the
+// pair) and fetches its 128-token halves of the activations (the B operand,
+// N = 256 per accumulator over the pair); the leader CTA's elected thread
+// issues the MMAs, which read both CTAs' shared memory and write each CTA's
+// 128 rows x 512 tokens of fp32 accumulators into its own TMEM.  Per SM and
+// stage the tensor cores read 64 KB of operands instead of the 128 KB of the
+// single-CTA 128 x 128 MMAs, and the activation fetch halves, so the shared
+// memory port (which the operand reads, the TMA fills and the decoders share)
+// no longer caps the tensor pipe near half of its rate.
+//   warp 0      (both CTAs) TMA producer: this CTA's 128 tokens of each
+//               accumulator per 64-column stage; bytes of both CTAs count on
+//               the leader's full_x[stage];
+//   warp 1      (leader) MMA issuer: waits full_x + full_w, 4 x nacc pair
+//               MMAs per stage, commits to empty[stage] of both CTAs;
+//   warps 2-17  (both CTAs) decoders, as in the single-CTA kernel, arriving on
+//               their CTA's full_w[stage] (the peer's warp 1 forwards each
+//               completed stage to the leader's); then the epilogue: each thread
+//               owns one output row and stores its tokens (64- or 128-byte
+//               row segments per warp store).
+namespace pair {
+constexpr int kRows = 128;                  // weight rows per CTA
+constexpr int kTok = 512;                   // tokens per pair tile: two accumulators
+constexpr int kAccN = 256;                  // tokens per accumulator (MMA N)
+constexpr int kHalf = 128;                  // tokens of one accumulator held by one CTA
+constexpr int kStages = 3;
+constexpr int kXBytes = 2 * kHalf * kBK * 2;  // 32 KB: this CTA's halves of both accumulators
+constexpr int kWBytes = kRows * kBK * 2;      // 16 KB: decoded weights
+constexpr int kPairTmemCols = 2 * kAccN;
+
+int smem_bytes(int R) {
+  return 1024 + kStages * (kXBytes + kWBytes) + R * kCbCopyBytes * kCbCopies + 8 * (3 * kStages + 1) + 16;
+}
+}  // namespace pair
+
 template <int R, int NUM>
-__global__ void __launch_bounds__(kThreads, 1) rvq_gemm_kernel(const __grid_constant__ CUtensorMap xmap,
-                                                               const __grid_constant__ GemmParams p) {
+__global__ void __launch_bounds__(kThreads, 1) rvq_gemm_pair_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                                    const __grid_constant__ GemmParams p) {
+  using namespace pair;
+  constexpr int S = pair::kStages;
   constexpr int NM = NUM & 3;
   constexpr bool F16 = (NUM & 4) != 0;
   using T = WT<F16>;
   extern __shared__ uint8_t smem_raw[];
-  // 1024-byte aligned region: [A stages][B stages][codebooks][barriers][tmem slot]
+  // 1024-byte aligned: [x stages][w stages][codebooks][barriers][tmem slot]
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* gbase = smem_raw + (base - raw);
-  const uint32_t a_sm = base;
-  const uint32_t b_sm = a_sm + kStages * kABytes;
-  const uint32_t cb_sm = b_sm + kStages * kBBytes;
+  const uint32_t x_sm = base;
+  const uint32_t w_sm = x_sm + S * kXBytes;
+  const uint32_t cb_sm = w_sm + S * kWBytes;
   uint8_t* cb = gbase + (cb_sm - base);
   const uint32_t bar_sm = cb_sm + R * kCbCopyBytes * kCbCopies;
-  const uint32_t full_a = bar_sm, full_b = bar_sm + 8 * kStages, empty = bar_sm + 16 * kStages;
-  const uint32_t acc_full = bar_sm + 24 * kStages;
+  const uint32_t full_w = bar_sm, full_x = bar_sm + 8 * S, empty = bar_sm + 16 * S;
+  const uint32_t acc_full = bar_sm + 24 * S;
   const uint32_t tmem_slot = acc_full + 8;
   volatile uint32_t* tmem_slot_ptr = reinterpret_cast<volatile uint32_t*>(gbase + (tmem_slot - base));
   __shared__ volatile int abort_flag;
 
+  const uint32_t rank = cluster_ctarank();  // 0: leader
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kBM;
-  const int n0 = blockIdx.y * kBN;
-  // 128-token MMA tiles holding real tokens (the last CTA of a small M needs
-  // fewer than four) and the 256-row activation boxes they read
-  const int mtiles = min(kBM / kUM, (p.M - m0 + kUM - 1) / kUM);
-  const int boxes = (mtiles * kUM + kTmaRows - 1) / kTmaRows;
+  // the pair runs along x (a kernel with pair MMAs needs an even cluster width)
+  const int n0 = blockIdx.x * kRows;  // this CTA's weight rows (the grid may hold one padding CTA)
+  const int m0 = blockIdx.y * kTok;
+  const int nacc = p.M - m0 > kAccN ? 2 : 1;  // accumulators holding tokens (the same in both CTAs)
   const int kblocks = (p.K + kBK - 1) / kBK;
 
-  // row group of this N tile (the host guarantees a tile never straddles groups)
   int g = 0;
   while (g + 1 < p.num_groups && p.group_row_start[g + 1] <= n0) ++g;
   const int g_row0 = p.group_row_start[g], g_row1 = p.group_row_start[g + 1];
@@ -265,91 +343,110 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_kernel(const __grid_cons
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(full_a + 8 * s, 1);
-      mbar_init(full_b + 8 * s, kDecodeWarps);
-      mbar_init(empty + 8 * s, 1);
+    for (int s = 0; s < S; ++s) {
+      // leader: its decoder warps + the peer's forwarded arrival; peer: its decoder warps
+      mbar_init(full_w + 8 * s, kDecodeWarps + (rank == 0 ? 1 : 0));
+      mbar_init(full_x + 8 * s, 1);                 // the leader's expect_tx (used in the leader)
+      mbar_init(empty + 8 * s, 1);                  // the pair commit (both CTAs)
     }
     mbar_init(acc_full, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot),
-                 "r"(kTmemCols)
+  if (warp == 0) {  // both CTAs, same warp: one allocation for the pair
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tmem_slot),
+                 "r"(kPairTmemCols)
                  : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
-  // codebooks of this group: [R][256][8] x 8 copies (one-stage and fast-mode
-  // tables converted to the weight type, exactly as the GEMV stages them)
+  // codebooks of this CTA's group, 8 copies per entry; lanes write the copies
+  // of one entry side by side (whole 128-byte rows, no bank conflicts)
   {
     const uint16_t* books = p.codebooks + (size_t)g * R * p.entries * 8;
     const float* scales = p.stage_scales ? p.stage_scales + (size_t)g * R : nullptr;
-    for (int i = threadIdx.x; i < R * p.entries; i += kThreads) {
-      const int st = i / p.entries, e = i - st * p.entries;
-      uint4 v = *reinterpret_cast<const uint4*>(books + (size_t)i * 8);
+    for (int i = threadIdx.x; i < R * p.entries * kCbCopies; i += kThreads) {
+      const int c = i % kCbCopies, se = i / kCbCopies;
+      const int st = se / p.entries, e = se - st * p.entries;
+      uint4 v = *reinterpret_cast<const uint4*>(books + (size_t)se * 8);
       v.x = staged_word<R, NM, F16>(v.x, scales, st);
       v.y = staged_word<R, NM, F16>(v.y, scales, st);
       v.z = staged_word<R, NM, F16>(v.z, scales, st);
       v.w = staged_word<R, NM, F16>(v.w, scales, st);
-#pragma unroll
-      for (int c = 0; c < kCbCopies; ++c)
-        *reinterpret_cast<uint4*>(cb + ((st * 256 + e) * kCbCopies + c) * 16) = v;
+      *reinterpret_cast<uint4*>(cb + ((st * 256 + e) * kCbCopies + c) * 16) = v;
     }
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // both CTAs' barriers and TMEM exist before any remote arrive or pair MMA
   tc_fence_after();
   const uint32_t tmem = *tmem_slot_ptr;
+  const uint32_t lead_full_w = mapa_shared(full_w, 0), lead_full_x = mapa_shared(full_x, 0);
 
   if (warp == 0) {
-    // ---------------- TMA producer -------------------------------------
+    // ---------------- TMA producer (both CTAs) ---------------------------
     if (lane == 0) {
       int issued = 0;
       for (int kb = 0; kb < kblocks; ++kb) {
-        const int s = kb % kStages;
-        if (kb >= kStages && !mbar_wait(empty + 8 * s, ((kb / kStages) - 1) & 1)) {
+        const int s = kb % S;
+        if (kb >= S && !mbar_wait_cluster(empty + 8 * s, ((kb / S) - 1) & 1)) {
           abort_flag = 1;
           break;
         }
         if (abort_flag) break;
-        mbar_expect_tx(full_a + 8 * s, boxes * (kTmaRows * 128));
-        for (int h = 0; h < boxes; ++h)
-          tma_load_2d(a_sm + s * kABytes + h * (kTmaRows * 128), &xmap, kb * kBK, m0 + h * kTmaRows, full_a + 8 * s);
+        if (rank == 0) mbar_expect_tx(full_x + 8 * s, 2 * nacc * (kHalf * 128));
+        for (int a = 0; a < nacc; ++a)
+          tma_load_2d_pair(x_sm + s * kXBytes + a * (kHalf * 128), &xmap, kb * kBK, m0 + a * kAccN + (int)rank * kHalf,
+                           lead_full_x + 8 * s);
         ++issued;
       }
-      // never leave a copy in flight: wait (bounded) for the last load of every stage
-      for (int kb = issued - kStages < 0 ? 0 : issued - kStages; kb < issued; ++kb)
-        if (!mbar_wait(full_a + 8 * (kb % kStages), (kb / kStages) & 1)) abort_flag = 1;
+      // the leader sees both CTAs' loads land: never leave one in flight
+      if (rank == 0)
+        for (int kb = issued - S < 0 ? 0 : issued - S; kb < issued; ++kb)
+          if (!mbar_wait(full_x + 8 * (kb % S), (kb / S) & 1)) abort_flag = 1;
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------------------------------
+  } else if (warp == 1 && rank == 1) {
+    // ---------------- peer: forward its decoded stages to the leader -------
+    // The decoders arrive on their own CTA's barrier (a CTA-scope release);
+    // this thread, with no loads of its own in flight, turns each completed
+    // phase into one cluster-scope arrive on the leader's barrier.  (Decoders
+    // arriving remotely themselves made every release wait for their id
+    // prefetches from HBM: twice the decode time per stage.)
     if (lane == 0) {
       for (int kb = 0; kb < kblocks; ++kb) {
-        const int s = kb % kStages;
-        const uint32_t par = (kb / kStages) & 1;
-        if (!mbar_wait(full_a + 8 * s, par) || !mbar_wait(full_b + 8 * s, par)) {
+        const int s = kb % S;
+        if (!mbar_wait(full_w + 8 * s, (kb / S) & 1)) {
+          abort_flag = 1;
+          break;
+        }
+        mbar_arrive_cluster(lead_full_w + 8 * s);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- pair MMA issuer (leader) ---------------------------
+    if (lane == 0) {
+      for (int kb = 0; kb < kblocks; ++kb) {
+        const int s = kb % S;
+        const uint32_t par = (kb / S) & 1;
+        if (!mbar_wait_cluster(full_x + 8 * s, par) || !mbar_wait_cluster(full_w + 8 * s, par)) {
           abort_flag = 1;
           break;
         }
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < kBK / 16; ++ks) {
-          const uint64_t bd = smem_desc_sw128(b_sm + s * kBBytes + ks * 32);
-#pragma unroll
-          for (int mt = 0; mt < kBM / kUM; ++mt) {
-            if (mt >= mtiles) break;
-            const uint64_t ad = smem_desc_sw128(a_sm + s * kABytes + mt * (kUM * 128) + ks * 32);
-            umma_16bit<F16>(tmem + (uint32_t)(mt * kBN), ad, bd, (kb > 0 || ks > 0) ? 1u : 0u);
+          const uint64_t ad = smem_desc_sw128(w_sm + s * kWBytes + ks * 32);
+          for (int a = 0; a < nacc; ++a) {
+            const uint64_t bd = smem_desc_sw128(x_sm + s * kXBytes + a * (kHalf * 128) + ks * 32);
+            umma_pair<F16>(tmem + (uint32_t)(a * kAccN), ad, bd, (kb > 0 || ks > 0) ? 1u : 0u);
           }
         }
-        umma_commit(empty + 8 * s);
+        umma_commit_pair(empty + 8 * s);
       }
-      umma_commit(acc_full);  // fires once every MMA issued above has completed
+      umma_commit_pair(acc_full);  // both CTAs: every pair MMA issued above has completed
     }
   } else {
-    // ---------------- decoders, then epilogue -----------------------------
-    const int t = threadIdx.x - 64;  // row t & 127 of the tile, blocks part * kPartBlocks.. of each stage
-    const int row = t & (kBN - 1), part = t >> 7;
+    // ---------------- decoders (both CTAs), then epilogue -----------------
+    const int t = threadIdx.x - 64;
+    const int row = t & (kRows - 1), part = t >> 7;
     const int n = n0 + row;
     const bool row_ok = n < g_row1;
     const uint32_t rho2 = row_ok ? T::rho2(p.row_scale[n]) : 0u;
@@ -358,13 +455,9 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_kernel(const __grid_cons
     const int rr = local % 16;
     const long long tile_bytes = (long long)p.chunks * R * 256;
     const uint8_t* idrow = p.packed + tile * tile_bytes + rr * 16 + part * kPartBlocks;
-    const uint32_t bsm_row0 = b_sm + (row >> 3) * 1024 + (row & 7) * 128;
+    const uint32_t wsm_row0 = w_sm + (row >> 3) * 1024 + (row & 7) * 128;
     const uint32_t cb_lane = cb_sm + (uint32_t)(lane & 7) * 16;
     const int nsw = row & 7;
-    // stage kb covers blocks 8kb..8kb+7 = bytes 8*(kb&1) of chunk kb/2; this
-    // thread's blocks are kPartBlocks bytes per part further in.  The ids
-    // stream from HBM once (evict-first loads), kIdAhead stages ahead.
-    static_assert(kPartBlocks == 2 || kPartBlocks == 4, "ids are loaded as 2 or 4 bytes");
     constexpr int kIdAhead = 4;
     auto load_ids = [&](int kb, uint32_t (&dst)[R]) {
 #pragma unroll
@@ -375,92 +468,65 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_kernel(const __grid_cons
                                             : (uint32_t)__ldcs(reinterpret_cast<const unsigned short*>(a));
       }
     };
-    uint32_t idq[kIdAhead + 1][R];  // idq[0]: this stage; idq[j]: stage kb + j
+    uint32_t idq[kIdAhead + 1][R];
 #pragma unroll
     for (int j = 0; j < kIdAhead; ++j) load_ids(j, idq[j]);
     for (int kb = 0; kb < kblocks; ++kb) {
-      const int s = kb % kStages;
+      const int s = kb % S;
       load_ids(kb + kIdAhead, idq[kIdAhead]);
-      if (kb >= kStages && !mbar_wait(empty + 8 * s, ((kb / kStages) - 1) & 1)) {
+      if (kb >= S && !mbar_wait_cluster(empty + 8 * s, ((kb / S) - 1) & 1)) {
         abort_flag = 1;
         break;
       }
       if (abort_flag) break;
       const int k_left = row_ok ? p.K - kb * kBK : 0;
-      decode_stage_part<R, NUM>(bsm_row0 + s * kBBytes, nsw, idq[0], part * kPartBlocks, cb_lane, rho2, k_left);
+      decode_stage_part<R, NUM>(wsm_row0 + s * kWBytes, nsw, idq[0], part * kPartBlocks, cb_lane, rho2, k_left);
       fence_proxy_async();
       __syncwarp();
-      if (lane == 0) mbar_arrive(full_b + 8 * s);
+      if (lane == 0) mbar_arrive(full_w + 8 * s);
 #pragma unroll
       for (int j = 0; j < kIdAhead; ++j)
 #pragma unroll
         for (int st = 0; st < R; ++st) idq[j][st] = idq[j + 1][st];
     }
-    // epilogue: TMEM lanes 32*(warp%4) .. +31 are this warp's tokens
-    const bool ok = !abort_flag && mbar_wait(acc_full, 0);
+    // epilogue: TMEM lane 32 * (warp % 4) + lane is output row n0 + that lane;
+    // column c is token m0 + c; the four warps of a lane quarter split the columns
+    const bool ok = !abort_flag && mbar_wait_cluster(acc_full, 0);
     if (!ok) abort_flag = 1;
     tc_fence_after();
     if (ok) {
-      const int quarter = warp & 3;
-      const bool vec_ok = (p.ldy % 8) == 0 && ((uintptr_t)p.y & 15) == 0;
-      // kDecodeWarps / 4 warps share a lane quarter and split the four accumulators
-      constexpr int kAccPerWarp = 16 / kDecodeWarps;
-      for (int mi = 0; mi < kAccPerWarp; ++mi) {
-      const int mt = kAccPerWarp * ((warp - 2) >> 2) + mi;
-      if (mt >= mtiles) continue;  // this accumulator holds no tokens (warp-uniform)
-      const int m = m0 + mt * kUM + quarter * 32 + lane;
-      for (int c0 = 0; c0 < kBN; c0 += 16) {
+      const int quarter = warp & 3, share = (warp - 2) >> 2;
+      const int erow = quarter * 32 + lane;
+      const int en = n0 + erow;
+      const bool eok = en < g_row1;
+      const float bias = (eok && p.bias) ? __bfloat162float(__ushort_as_bfloat16(p.bias[en])) : 0.f;
+      const int cols = nacc * kAccN / 4;  // per warp
+      for (int c0 = share * cols; c0 < (share + 1) * cols; c0 += 16) {
         uint32_t v[16];
-        tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(mt * kBN + c0), v);
-        if (m >= p.M) continue;
-        const int col0 = n0 + c0;
-        float f[16];
+        tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, v);
+        if (!eok) continue;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          f[j] = __uint_as_float(v[j]);
-          if (p.bias && col0 + j < g_row1) f[j] += __bfloat162float(__ushort_as_bfloat16(p.bias[col0 + j]));
+          const int m = m0 + c0 + j;
+          if (m >= p.M) break;
+          const float f = __uint_as_float(v[j]) + bias;
+          const long long idx = (long long)m * p.ldy + en;
+          if (p.y_dtype == WAL_F32) static_cast<float*>(p.y)[idx] = f;
+          else if (p.y_dtype == WAL_F16) static_cast<uint16_t*>(p.y)[idx] = __half_as_ushort(__float2half_rn(f));
+          else static_cast<uint16_t*>(p.y)[idx] = __bfloat16_as_ushort(__float2bfloat16_rn(f));
         }
-        const bool full = col0 + 16 <= g_row1 && vec_ok;
-        if (p.y_dtype == WAL_F32) {
-          float* yr = static_cast<float*>(p.y) + (long long)m * p.ldy + col0;
-          if (full) {
-#pragma unroll
-            for (int j = 0; j < 16; j += 4) *reinterpret_cast<float4*>(yr + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
-          } else {
-            for (int j = 0; j < 16; ++j)
-              if (col0 + j < g_row1) yr[j] = f[j];
-          }
-        } else {  // 16-bit output: bf16 or fp16, one rounding of the fp32 sum
-          const bool yf16 = p.y_dtype == WAL_F16;
-          uint16_t* yr = static_cast<uint16_t*>(p.y) + (long long)m * p.ldy + col0;
-          if (full) {
-            uint32_t w[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              w[j] = yf16 ? WT<true>::cvt2(f[2 * j], f[2 * j + 1]) : WT<false>::cvt2(f[2 * j], f[2 * j + 1]);
-            *reinterpret_cast<uint4*>(yr) = make_uint4(w[0], w[1], w[2], w[3]);
-            *reinterpret_cast<uint4*>(yr + 8) = make_uint4(w[4], w[5], w[6], w[7]);
-          } else {
-            for (int j = 0; j < 16; ++j)
-              if (col0 + j < g_row1)
-                yr[j] = yf16 ? __half_as_ushort(__float2half_rn(f[j])) : __bfloat16_as_ushort(__float2bfloat16_rn(f[j]));
-          }
-        }
-      }
       }
     }
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // neither CTA frees TMEM or exits while the pair still works on it
   if (abort_flag && threadIdx.x == 0 && p.status) atomicExch(p.status, 1);
   if (warp == 0) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPairTmemCols) : "memory");
   }
 }
 
-int smem_bytes(int R) {
-  return 1024 + kStages * (kABytes + kBBytes) + R * kCbCopyBytes * kCbCopies + 8 * (3 * kStages + 1) + 16;
-}
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -485,11 +551,23 @@ using namespace wal;
 using namespace wal::gemm;
 
 template <int R, int NUM>
-static int launch_gemm(const CUtensorMap& map, const GemmParams& p, dim3 grid, int smem, cudaStream_t s) {
-  if (cudaFuncSetAttribute(rvq_gemm_kernel<R, NUM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-      cudaSuccess)
+static int launch_gemm_pair(const CUtensorMap& map, const GemmParams& p, dim3 grid, int smem, cudaStream_t s) {
+  auto kern = rvq_gemm_pair_kernel<R, NUM>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return WAL_ERR_CUDA;
-  rvq_gemm_kernel<R, NUM><<<grid, kThreads, smem, s>>>(map, p);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;  // the CTA pair: neighbouring 128-row tiles
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, map, p) != cudaSuccess) return WAL_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? WAL_OK : WAL_ERR_CUDA;
 }
 
@@ -528,14 +606,14 @@ extern "C" int wal_rvq_gemm_typed(const wal_rvq_layer* layer, const void* x, int
   p.entries = g.num_entries;
   p.y_dtype = y_dtype;
   p.num_groups = g.num_groups;
-  // group boundaries; an N tile (kBN rows) must not straddle two groups
+  // group boundaries; a CTA's 128 weight rows must not straddle two groups
   long long t = 0, rows = 0;
   p.group_tile_start[0] = 0;
   p.group_row_start[0] = 0;
   for (int i = 0; i < g.num_groups; ++i) {
     const long long n = g.num_groups == 1 ? g.out_features : (layer->group_rows ? layer->group_rows[i] : -1);
     if (n <= 0) return WAL_ERR_INVALID_ARGUMENT;
-    if (i + 1 < g.num_groups && (rows + n) % kBN != 0) return WAL_ERR_UNSUPPORTED;
+    if (i + 1 < g.num_groups && (rows + n) % pair::kRows != 0) return WAL_ERR_UNSUPPORTED;
     rows += n;
     t += (n + 15) / 16;
     p.group_tile_start[i + 1] = (int)t;
@@ -548,26 +626,29 @@ extern "C" int wal_rvq_gemm_typed(const wal_rvq_layer* layer, const void* x, int
   CUtensorMap map;
   const cuuint64_t dims[2] = {(cuuint64_t)g.in_features, (cuuint64_t)M};
   const cuuint64_t strides[1] = {(cuuint64_t)ldx * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kTmaRows};  // 64 x 256: two loads per stage
+  const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)pair::kHalf};  // 64 x 128: one box per accumulator half
   const cuuint32_t estr[2] = {1, 1};
   if (enc(&map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x),
           dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return WAL_ERR_CUDA;
   const int R = g.num_stages;
-  const int smem = smem_bytes(R);
-  const dim3 grid((unsigned)((M + kBM - 1) / kBM), (unsigned)((g.out_features + kBN - 1) / kBN));
+  const int smem = pair::smem_bytes(R);
+  // CTA pairs along the weight rows: an odd tile count gets one padding CTA
+  const long long row_tiles = (g.out_features + pair::kRows - 1) / pair::kRows;
+  if (M > (int64_t)65535 * pair::kTok) return WAL_ERR_SHAPE;  // token tiles along grid y
+  const dim3 grid((unsigned)((row_tiles + 1) / 2 * 2), (unsigned)((M + pair::kTok - 1) / pair::kTok));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int nm = fast ? kFast : kExact;
   switch (R * 100 + nm * 10 + (f16 ? 1 : 0)) {
-    case 100 + kExact * 10: return launch_gemm<1, num_mode(kExact, false)>(map, p, grid, smem, s);
-    case 100 + kExact * 10 + 1: return launch_gemm<1, num_mode(kExact, true)>(map, p, grid, smem, s);
-    case 100 + kFast * 10: return launch_gemm<1, num_mode(kFast, false)>(map, p, grid, smem, s);
-    case 100 + kFast * 10 + 1: return launch_gemm<1, num_mode(kFast, true)>(map, p, grid, smem, s);
-    case 200 + kExact * 10: return launch_gemm<2, num_mode(kExact, false)>(map, p, grid, smem, s);
-    case 200 + kExact * 10 + 1: return launch_gemm<2, num_mode(kExact, true)>(map, p, grid, smem, s);
-    case 200 + kFast * 10: return launch_gemm<2, num_mode(kFast, false)>(map, p, grid, smem, s);
-    case 200 + kFast * 10 + 1: return launch_gemm<2, num_mode(kFast, true)>(map, p, grid, smem, s);
+    case 100 + kExact * 10: return launch_gemm_pair<1, num_mode(kExact, false)>(map, p, grid, smem, s);
+    case 100 + kExact * 10 + 1: return launch_gemm_pair<1, num_mode(kExact, true)>(map, p, grid, smem, s);
+    case 100 + kFast * 10: return launch_gemm_pair<1, num_mode(kFast, false)>(map, p, grid, smem, s);
+    case 100 + kFast * 10 + 1: return launch_gemm_pair<1, num_mode(kFast, true)>(map, p, grid, smem, s);
+    case 200 + kExact * 10: return launch_gemm_pair<2, num_mode(kExact, false)>(map, p, grid, smem, s);
+    case 200 + kExact * 10 + 1: return launch_gemm_pair<2, num_mode(kExact, true)>(map, p, grid, smem, s);
+    case 200 + kFast * 10: return launch_gemm_pair<2, num_mode(kFast, false)>(map, p, grid, smem, s);
+    case 200 + kFast * 10 + 1: return launch_gemm_pair<2, num_mode(kFast, true)>(map, p, grid, smem, s);
     default: return WAL_ERR_UNSUPPORTED;
   }
 }
