@@ -330,9 +330,12 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_pair_kernel(const __grid
 
   const uint32_t rank = cluster_ctarank();  // 0: leader
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // the pair runs along x (a kernel with pair MMAs needs an even cluster width)
-  const int n0 = blockIdx.x * kRows;  // this CTA's weight rows (the grid may hold one padding CTA)
-  const int m0 = blockIdx.y * kTok;
+  // grid x = (pair rank, token tile), y = pair of 128-row tiles: the pair runs
+  // along x (a kernel with pair MMAs needs an even cluster width), and the
+  // token tiles of one pair of row tiles run side by side, so the weight ids
+  // stream from HBM once and the other tiles find them in L2
+  const int n0 = (2 * (int)blockIdx.y + (int)rank) * kRows;  // this CTA's weight rows (maybe a padding CTA)
+  const int m0 = (int)(blockIdx.x >> 1) * kTok;
   const int nacc = p.M - m0 > kAccN ? 2 : 1;  // accumulators holding tokens (the same in both CTAs)
   const int kblocks = (p.K + kBK - 1) / kBK;
 
@@ -636,8 +639,8 @@ extern "C" int wal_rvq_gemm_typed(const wal_rvq_layer* layer, const void* x, int
   const int smem = pair::smem_bytes(R);
   // CTA pairs along the weight rows: an odd tile count gets one padding CTA
   const long long row_tiles = (g.out_features + pair::kRows - 1) / pair::kRows;
-  if (M > (int64_t)65535 * pair::kTok) return WAL_ERR_SHAPE;  // token tiles along grid y
-  const dim3 grid((unsigned)((row_tiles + 1) / 2 * 2), (unsigned)((M + pair::kTok - 1) / pair::kTok));
+  if ((row_tiles + 1) / 2 > 65535) return WAL_ERR_SHAPE;  // pairs of row tiles along grid y
+  const dim3 grid((unsigned)(2 * ((M + pair::kTok - 1) / pair::kTok)), (unsigned)((row_tiles + 1) / 2));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int nm = fast ? kFast : kExact;
   switch (R * 100 + nm * 10 + (f16 ? 1 : 0)) {
