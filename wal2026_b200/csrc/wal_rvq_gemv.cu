@@ -822,10 +822,11 @@ using namespace wal;
 
 // Warps per tile for a CTA with tpc tiles: rounds of 16/wpt tiles, each round
 // ceil(chunks/wpt) chunks, plus a small reduction cost per round growing with
-// wpt.  Splits within 5% of the cheapest are ranked by the warps the first
-// round keeps busy (8B gate/up, 13 tiles per CTA: 2 warps per tile, 16 warps
-// busy, 31.7 us against 33.2 us for one warp per tile, 13 warps busy).
-static int best_wpt(long long tpc, int chunks, int wmax) {
+// wpt.  For one n-tile of tokens, splits within 5% of the cheapest are ranked
+// by the warps the first round keeps busy (8B gate/up at M = 1, 13 tiles per
+// CTA: 2 warps per tile, 16 warps busy, 31.7 us against 33.2 us for one warp
+// per tile, 13 warps busy; at M = 32 the same choice cost 61.3 against 54.9 us).
+static int best_wpt(long long tpc, int chunks, int wmax, bool rank_busy) {
   double cost[5];
   long long busy[5];
   int n = 0;
@@ -840,7 +841,7 @@ static int best_wpt(long long tpc, int chunks, int wmax) {
   }
   int pick = -1;
   for (int i = 0; i < n; ++i)
-    if (cost[i] <= best * 1.05 + 1e-9 &&
+    if (cost[i] <= (rank_busy ? best * 1.05 : best) + 1e-9 &&
         (pick < 0 || busy[i] > busy[pick] || (busy[i] == busy[pick] && cost[i] < cost[pick])))
       pick = i;
   return 1 << pick;
@@ -858,7 +859,7 @@ static int run_gemv(GemvParams p, int num_ctas, cudaStream_t stream) {
     int wmax = 16;
     while (wmax > 1 && C::smem(p.entries, p.M, kpad, wmax) > 227 * 1024) wmax >>= 1;
     if (p.wpt > wmax) {
-      p.wpt = p.auto_tpc > 0 ? best_wpt(p.auto_tpc, p.chunks, wmax) : wmax;
+      p.wpt = p.auto_tpc > 0 ? best_wpt(p.auto_tpc, p.chunks, wmax, p.M <= 8) : wmax;
       p.wpt_shift = log2_pow2(p.wpt);
       smem = C::smem(p.entries, p.M, kpad, p.wpt);
     }
@@ -1106,7 +1107,7 @@ static int gemv_common(const wal_rvq_layer* layer, const void* xv, int x_dtype, 
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const long long grid = layer->num_tiles < sms ? layer->num_tiles : sms;
     const long long tpc = (layer->num_tiles + grid - 1) / grid;  // tiles per CTA (max)
-    wpt = best_wpt(tpc, p.chunks, 16);
+    wpt = best_wpt(tpc, p.chunks, 16, M <= 8);
     p.auto_tpc = (int)tpc;
   }
   p.wpt = wpt;
