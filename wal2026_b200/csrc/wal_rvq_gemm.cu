@@ -1,7 +1,7 @@
 // Prefill path (M >= 128 tokens): fused Block-RVQ decode -> shared memory ->
 // tcgen05.mma on pairs of SMs (cta_group::2, fp32 accumulators in TMEM).
 //
-// Two CTAs of a cluster compute a 256 (output rows) x 512 (tokens) tile of y
+// Two CTAs of a cluster compute a 256 (output rows) x 512, 384 or 256 (tokens) tile of y
 // over all of K in stages of 64 columns.  Each CTA decodes its own 128 weight
 // rows exactly (the same arithmetic as the decode GEMV: fp32 stage sum, two
 // roundings in the weight type) into a 128-byte-swizzled K-major buffer and
@@ -62,6 +62,7 @@ struct GemmParams {
   int num_groups;
   int group_tile_start[65];
   int group_row_start[65];
+  int tok;  // tokens per pair tile: 512, 384 or 256 (two accumulators of tok / 2)
 };
 
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -183,20 +184,21 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
       : "memory");
 }
 
-// Pair MMA: D[256 x 256] (+)= A[256 x 16] B[256 x 16]^T, A rows 0-127 and B
-// rows 0-127 from the leader's shared memory, rows 128-255 from the peer's,
-// D rows 0-127 in the leader's TMEM and 128-255 in the peer's (same columns).
+// Pair MMA: D[256 x N] (+)= A[256 x 16] B[N x 16]^T, A rows 0-127 and B rows
+// 0..N/2-1 from the leader's shared memory, the rest from the peer's, D rows
+// 0-127 in the leader's TMEM and 128-255 in the peer's (same columns).
 template <bool F16>
-__host__ __device__ constexpr uint32_t idesc_pair() {
-  return (1u << 4) | (F16 ? 0u : (1u << 7) | (1u << 10)) | ((uint32_t)(256 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+__host__ __device__ constexpr uint32_t idesc_pair(int n) {
+  return (1u << 4) | (F16 ? 0u : (1u << 7) | (1u << 10)) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
 }
 
 template <bool F16>
-__device__ __forceinline__ void umma_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+__device__ __forceinline__ void umma_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n}\n"
-      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc_pair<F16>()), "r"(accumulate), "r"(0u)
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u)
       : "memory");
 }
 
@@ -291,9 +293,8 @@ __device__ __forceinline__ void decode_stage_part(uint32_t bsm_row, int nsw, con
 //               row segments per warp store).
 namespace pair {
 constexpr int kRows = 128;                  // weight rows per CTA
-constexpr int kTok = 512;                   // tokens per pair tile: two accumulators
-constexpr int kAccN = 256;                  // tokens per accumulator (MMA N)
-constexpr int kHalf = 128;                  // tokens of one accumulator held by one CTA
+constexpr int kAccN = 256;                  // TMEM columns per accumulator (MMA N at most)
+constexpr int kHalf = 128;                  // tokens of one accumulator held by one CTA (at most)
 constexpr int kStages = 3;
 constexpr int kXBytes = 2 * kHalf * kBK * 2;  // 32 KB: this CTA's halves of both accumulators
 constexpr int kWBytes = kRows * kBK * 2;      // 16 KB: decoded weights
@@ -335,8 +336,9 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_pair_kernel(const __grid
   // token tiles of one pair of row tiles run side by side, so the weight ids
   // stream from HBM once and the other tiles find them in L2
   const int n0 = (2 * (int)blockIdx.y + (int)rank) * kRows;  // this CTA's weight rows (maybe a padding CTA)
-  const int m0 = (int)(blockIdx.x >> 1) * kTok;
-  const int nacc = p.M - m0 > kAccN ? 2 : 1;  // accumulators holding tokens (the same in both CTAs)
+  const int tok = p.tok, accn = tok / 2, half = tok / 4;  // tile tokens, MMA N, tokens per CTA and accumulator
+  const int m0 = (int)(blockIdx.x >> 1) * tok;
+  const int nacc = p.M - m0 > accn ? 2 : 1;  // accumulators holding tokens (the same in both CTAs)
   const int kblocks = (p.K + kBK - 1) / kBK;
 
   int g = 0;
@@ -395,9 +397,9 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_pair_kernel(const __grid
           break;
         }
         if (abort_flag) break;
-        if (rank == 0) mbar_expect_tx(full_x + 8 * s, 2 * nacc * (kHalf * 128));
+        if (rank == 0) mbar_expect_tx(full_x + 8 * s, 2 * nacc * (half * 128));
         for (int a = 0; a < nacc; ++a)
-          tma_load_2d_pair(x_sm + s * kXBytes + a * (kHalf * 128), &xmap, kb * kBK, m0 + a * kAccN + (int)rank * kHalf,
+          tma_load_2d_pair(x_sm + s * kXBytes + a * (kHalf * 128), &xmap, kb * kBK, m0 + a * accn + (int)rank * half,
                            lead_full_x + 8 * s);
         ++issued;
       }
@@ -426,6 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_pair_kernel(const __grid
   } else if (warp == 1) {
     // ---------------- pair MMA issuer (leader) ---------------------------
     if (lane == 0) {
+      const uint32_t idesc = idesc_pair<F16>(accn);
       for (int kb = 0; kb < kblocks; ++kb) {
         const int s = kb % S;
         const uint32_t par = (kb / S) & 1;
@@ -439,7 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_pair_kernel(const __grid
           const uint64_t ad = smem_desc_sw128(w_sm + s * kWBytes + ks * 32);
           for (int a = 0; a < nacc; ++a) {
             const uint64_t bd = smem_desc_sw128(x_sm + s * kXBytes + a * (kHalf * 128) + ks * 32);
-            umma_pair<F16>(tmem + (uint32_t)(a * kAccN), ad, bd, (kb > 0 || ks > 0) ? 1u : 0u);
+            umma_pair<F16>(tmem + (uint32_t)(a * kAccN), ad, bd, idesc, (kb > 0 || ks > 0) ? 1u : 0u);
           }
         }
         umma_commit_pair(empty + 8 * s);
@@ -493,7 +496,8 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_pair_kernel(const __grid
         for (int st = 0; st < R; ++st) idq[j][st] = idq[j + 1][st];
     }
     // epilogue: TMEM lane 32 * (warp % 4) + lane is output row n0 + that lane;
-    // column c is token m0 + c; the four warps of a lane quarter split the columns
+    // column a * 256 + c of accumulator a is token m0 + a * accn + c; the four
+    // warps of a lane quarter split each accumulator's columns
     const bool ok = !abort_flag && mbar_wait_cluster(acc_full, 0);
     if (!ok) abort_flag = 1;
     tc_fence_after();
@@ -503,14 +507,15 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_pair_kernel(const __grid
       const int en = n0 + erow;
       const bool eok = en < g_row1;
       const float bias = (eok && p.bias) ? __bfloat162float(__ushort_as_bfloat16(p.bias[en])) : 0.f;
-      const int cols = nacc * kAccN / 4;  // per warp
-      for (int c0 = share * cols; c0 < (share + 1) * cols; c0 += 16) {
+      const int cols = accn / 4;  // per warp and accumulator: 64, 48 or 32
+      for (int c = 0; c < nacc * cols; c += 16) {
+        const int a = c / cols, c0 = share * cols + (c - a * cols);  // accumulator, its column
         uint32_t v[16];
-        tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, v);
+        tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * kAccN + c0), v);
         if (!eok) continue;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          const int m = m0 + c0 + j;
+          const int m = m0 + a * accn + c0 + j;
           if (m >= p.M) break;
           const float f = __uint_as_float(v[j]) + bias;
           const long long idx = (long long)m * p.ldy + en;
@@ -629,7 +634,22 @@ extern "C" int wal_rvq_gemm_typed(const wal_rvq_layer* layer, const void* x, int
   CUtensorMap map;
   const cuuint64_t dims[2] = {(cuuint64_t)g.in_features, (cuuint64_t)M};
   const cuuint64_t strides[1] = {(cuuint64_t)ldx * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)pair::kHalf};  // 64 x 128: one box per accumulator half
+  // Token tile per pair: 512, 384 or 256 (MMA N = 256, 192 or 128).  A stage
+  // takes about 1400 cycles whatever the tile (the shared-memory port: weight
+  // operand reads, both SMs reading each CTA's activation half, the fills and
+  // the decode), so the rule is the fewest waves of pairs on the GPU's pair
+  // slots, then the smallest tile (8B q/k/v at 2048 tokens: 144 pairs of 384 in
+  // two waves, 125 us, against 96 pairs of 512 in two waves, 136 us; o at 512
+  // tokens: 59 us with 256 against 61 us with 512).
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long slots = sms / 2, row_pairs = ((g.out_features + pair::kRows - 1) / pair::kRows + 1) / 2;
+  auto waves = [&](long long tok) { return (row_pairs * ((M + tok - 1) / tok) + slots - 1) / slots; };
+  p.tok = 512;
+  for (int tok : {384, 256})
+    if (waves(tok) <= waves(p.tok)) p.tok = tok;
+  const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)(p.tok / 4)};  // one box per accumulator half
   const cuuint32_t estr[2] = {1, 1};
   if (enc(&map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x),
           dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -640,7 +660,7 @@ extern "C" int wal_rvq_gemm_typed(const wal_rvq_layer* layer, const void* x, int
   // CTA pairs along the weight rows: an odd tile count gets one padding CTA
   const long long row_tiles = (g.out_features + pair::kRows - 1) / pair::kRows;
   if ((row_tiles + 1) / 2 > 65535) return WAL_ERR_SHAPE;  // pairs of row tiles along grid y
-  const dim3 grid((unsigned)(2 * ((M + pair::kTok - 1) / pair::kTok)), (unsigned)((row_tiles + 1) / 2));
+  const dim3 grid((unsigned)(2 * ((M + p.tok - 1) / p.tok)), (unsigned)((row_tiles + 1) / 2));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int nm = fast ? kFast : kExact;
   switch (R * 100 + nm * 10 + (f16 ? 1 : 0)) {
