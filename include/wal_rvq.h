@@ -425,7 +425,10 @@ WAL_API int wal_silu_mul(const uint16_t* gu, int64_t ld_gu, int64_t M, int64_t I
  * front and every call leaves them at zero, so one workspace serves a whole
  * decode loop whose n grows; calls sharing one workspace must not overlap in
  * time.  Split-K over positions with an exact (log-sum-exp) merge in split
- * order: deterministic.  The merge keeps 8 * G bytes per split in shared
+ * order: deterministic.  Few (sequence, kv head) pairs get the fewest splits
+ * of at most 128 positions, each staged in one round; many pairs get fewer,
+ * longer splits (about 2.6 CTAs per SM) that stream through two 64-position
+ * stage buffers.  The merge keeps 8 * G bytes per split in shared
  * memory: a call whose splits (about n / 128 at large n) do not fit in 227 KB
  * returns WAL_ERR_SHAPE (hd = 128, G = 8: n <= 366,592 positions).  No
  * reference counterpart (the reference runs Hugging Face attention).
@@ -438,8 +441,8 @@ WAL_API int wal_decode_attention(const uint16_t* q, int64_t ld_q, const uint16_t
 
 /*
  * wal_decode_attention with an explicit split count (0 = library default):
- * num_splits splits of at most 128 and at least 32 positions each
- * (ceil(n / 128) <= num_splits <= ceil(n / 32), else WAL_ERR_SHAPE); the
+ * num_splits splits of at least 32 positions each (num_splits <= ceil(n /
+ * 32), else WAL_ERR_SHAPE; splits longer than 128 positions stream); the
  * workspace must hold that many splits' partials (WAL_ERR_BUFFER_TOO_SMALL
  * otherwise).  For tuning and tests.
  */
@@ -458,7 +461,7 @@ WAL_API int wal_decode_attention_ex(const uint16_t* q, int64_t ld_q, const uint1
  * compiled into this library, which every GPU that loads the library keeps
  * until the process exits.  Limit: B * hkv <= 4096 and the call's split
  * partials and statistics (B * hkv * nsplit * G * (hd + 2) * 4 bytes) within
- * 4 MiB - 16 KiB (Llama-3-8B heads at 2048 positions fit up to batch 15);
+ * 4 MiB - 16 KiB (Llama-3-8B heads at 2048 positions fit up to batch 55);
  * larger calls return WAL_ERR_BUFFER_TOO_SMALL and launch nothing.  Each call clears the merge counters it uses with an
  * asynchronous memset on the stream before its kernel.  The first call on a
  * device looks up the array's device address (cudaGetSymbolAddress, that

@@ -56,14 +56,14 @@ def test_static_scratch_rejects_shapes_beyond_its_size():
     q, kc, vc = _inputs(33, 128, 128, 64, 8, 4)
     out = torch.empty(33, 128 * 64, device=DEV, dtype=torch.bfloat16)
     assert _static(q, kc, vc, 8, out) == _abi.WAL_ERR_BUFFER_TOO_SMALL
-    # 32 sequences x 8 kv heads x 16 splits x 4 heads x 128 fp32 partials = 8 MiB > 4 MiB
-    q, kc, vc = _inputs(32, 32, 8, 128, 2048, 5)
-    out = torch.empty(32, 32 * 128, device=DEV, dtype=torch.bfloat16)
-    assert _static(q, kc, vc, 2048, out) == _abi.WAL_ERR_BUFFER_TOO_SMALL
-    # the same cache read at 4 sequences fits (1 MiB of partials) and still matches
-    want = torch.empty(4, 32 * 128, device=DEV, dtype=torch.bfloat16)
-    decode_attention(q[:4], kc[:4], vc[:4], 2048, want, decode_attention_workspace(4, 32, 8, 128, 2048, DEV))
+    # 128 sequences x 8 kv heads x 1 split x 8 heads x 128 fp32 partials = 4 MiB, above 4 MiB - 16 KiB
+    q, kc, vc = _inputs(128, 64, 8, 128, 64, 5)
+    out = torch.empty(128, 64 * 128, device=DEV, dtype=torch.bfloat16)
+    assert _static(q, kc, vc, 64, out) == _abi.WAL_ERR_BUFFER_TOO_SMALL
+    # the same cache read at 4 sequences fits and still matches
+    want = torch.empty(4, 64 * 128, device=DEV, dtype=torch.bfloat16)
+    decode_attention(q[:4], kc[:4], vc[:4], 64, want, decode_attention_workspace(4, 64, 8, 128, 64, DEV))
     got = torch.empty_like(want)
-    assert _static(q[:4], kc[:4], vc[:4], 2048, got) == _abi.WAL_OK
+    assert _static(q[:4], kc[:4], vc[:4], 64, got) == _abi.WAL_OK
     torch.cuda.synchronize()
     assert torch.equal(got, want)

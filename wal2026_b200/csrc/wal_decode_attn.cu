@@ -70,6 +70,61 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&m)[4]) {
                : "r"(addr));
 }
 
+// Merge of a (sequence, kv head)'s splits by its last CTA: split weights
+// exp2(m_s - M), the normalising sum, then the weighted sum of the split
+// outputs in split order (deterministic), written as the bf16 output row.
+// scratch: shared memory for 2 * nsplit * G floats.
+template <int HD, int G>
+__device__ __forceinline__ void merge_splits(const AttnParams& p, int bh, int b, int kvh, float* scratch) {
+  constexpr int NW = kThreads / 32;
+  __shared__ float inv_l[8];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int ns = p.nsplit;
+  float* wgt = scratch;           // [nsplit][G] exp2(m_s - M)
+  float* lsm = wgt + ns * G;      // [nsplit][G] split sums
+  const float2* st = p.stats + (long long)bh * ns * G;
+  for (int i = tid; i < ns * G; i += kThreads) {
+    const float2 v = __ldcg(st + i);
+    wgt[i] = v.x;
+    lsm[i] = v.y;
+  }
+  __syncthreads();
+  for (int g = warp; g < G; g += NW) {
+    float m = -INFINITY;
+    for (int s2 = lane; s2 < ns; s2 += 32) m = fmaxf(m, wgt[s2 * G + g]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float l = 0.f;
+    for (int s2 = lane; s2 < ns; s2 += 32) {
+      const float w = exp2f(wgt[s2 * G + g] - m);
+      wgt[s2 * G + g] = w;
+      l = fmaf(w, lsm[s2 * G + g], l);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    if (lane == 0) inv_l[g] = 1.f / l;
+  }
+  __syncthreads();
+  const float4* src = reinterpret_cast<const float4*>(p.part + (long long)bh * ns * G * HD);
+  uint16_t* orow = p.out + (long long)b * p.ld_out + (long long)kvh * G * HD;
+  for (int i = tid; i < G * HD / 4; i += kThreads) {
+    const int g = i / (HD / 4);
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+    for (int s2 = 0; s2 < ns; ++s2) {
+      const float w = wgt[s2 * G + g];
+      const float4 c = __ldcg(src + (long long)s2 * (G * HD / 4) + i);
+      a.x = fmaf(w, c.x, a.x); a.y = fmaf(w, c.y, a.y); a.z = fmaf(w, c.z, a.z); a.w = fmaf(w, c.w, a.w);
+    }
+    const float inv = inv_l[g];
+    const uint32_t lo = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(a.x * inv)) |
+                        ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(a.y * inv)) << 16);
+    const uint32_t hi = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(a.z * inv)) |
+                        ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(a.w * inv)) << 16);
+    *reinterpret_cast<uint2*>(orow + i * 4) = make_uint2(lo, hi);
+  }
+}
+
 // Tensor-core decode attention for one (sequence, kv head, split): the G query
 // heads are the rows of m16n8k16 tiles (rows >= G are zero), positions the
 // columns of the score tiles and the k dimension of the P.V tiles.  K and V
@@ -237,50 +292,191 @@ __global__ void __launch_bounds__(kThreads) decode_attn_kernel(const __grid_cons
   __syncthreads();
   if (!last) return;
   __threadfence();
-  const int ns = p.nsplit;
-  float* wgt = po + NW * G * HD;  // [nsplit][G] exp2(m_s - M)
-  float* lsm = wgt + ns * G;      // [nsplit][G] split sums
-  const float2* st = p.stats + (long long)bh * ns * G;
-  for (int i = tid; i < ns * G; i += kThreads) {
-    const float2 v = __ldcg(st + i);
-    wgt[i] = v.x;
-    lsm[i] = v.y;
-  }
-  __syncthreads();
-  for (int g = warp; g < G; g += NW) {
-    float m = -INFINITY;
-    for (int s2 = lane; s2 < ns; s2 += 32) m = fmaxf(m, wgt[s2 * G + g]);
+  merge_splits<HD, G>(p, bh, b, kvh, po + NW * G * HD);
+}
+
+// Streaming variant: the split's positions pass through the CTA in stages of
+// 64 (16 per warp), double-buffered, so the copy of stage c + 1 overlaps the
+// scores and P.V of stage c and a CTA can cover a long split; each warp keeps
+// its own running (max, sum, un-normalised output) per head across the stages
+// (exp2 rescaling when its max grows), and the four warps are combined once at
+// the end into the split's slot, in the format the merge reads.
+constexpr int kStage = 64;
+
+template <int HD, int G>
+__global__ void __launch_bounds__(kThreads) decode_attn_stream_kernel(const __grid_constant__ AttnParams p) {
+  constexpr int KT = HD / 16;
+  constexpr int NT = HD / 8;
+  constexpr int P16 = HD / 8;
+  constexpr int PSH = HD == 128 ? 4 : 3;
+  constexpr int NW = kThreads / 32;
+  constexpr int RB = HD * 2;
+  constexpr int BUF = 2 * kStage * RB;  // one stage: K rows, then V rows
+  static_assert(NW * 16 == kStage, "16 positions per warp and stage");
+  extern __shared__ __align__(128) uint8_t sm[];
+  __shared__ float wst[NW][8][2];  // per warp and head: running max, sum
+  __shared__ float stat[2][8];
+  __shared__ int last;
+  const int bh = blockIdx.x, split = blockIdx.y;
+  const int b = bh / p.hkv, kvh = bh - b * p.hkv;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r = lane >> 2, qd = lane & 3;
+  const int t0 = split * p.chunk;
+  const int len = min(p.n - t0, p.chunk);  // >= 1: the plan leaves no empty split
+  const int nst = (len + kStage - 1) / kStage;
+  const uint32_t sm_s = (uint32_t)__cvta_generic_to_shared(sm);
+  const uint16_t* kb = p.k + (((long long)b * p.hkv + kvh) * p.cache_len + t0) * HD;
+  const uint16_t* vb = p.v + (((long long)b * p.hkv + kvh) * p.cache_len + t0) * HD;
+
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+  // stage c -> buffer c & 1: K rows then V rows (rows >= len zero-filled),
+  // 16-byte piece j of row t at piece j ^ (t & 7)
+  auto issue = [&](int c) {
+    const uint32_t base = sm_s + (uint32_t)((c & 1) * BUF);
+    const int tb = c * kStage;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float l = 0.f;
-    for (int s2 = lane; s2 < ns; s2 += 32) {
-      const float w = exp2f(wgt[s2 * G + g] - m);
-      wgt[s2 * G + g] = w;
-      l = fmaf(w, lsm[s2 * G + g], l);
+    for (int kv = 0; kv < 2; ++kv) {
+      const uint16_t* src = kv == 0 ? kb : vb;
+      const uint32_t dst = base + (uint32_t)(kv * kStage * RB);
+      for (int i = tid; i < kStage * P16; i += kThreads) {
+        const int t = i >> PSH, j = i & (P16 - 1);
+        const bool in = tb + t < len;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst + (uint32_t)(t * RB + ((j ^ (t & 7)) << 4))),
+                     "l"(in ? src + (long long)(tb + t) * HD + j * 8 : src), "r"(in ? 16u : 0u));
+      }
     }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+  };
+  issue(0);
+  if (nst > 1) issue(1);
+  uint32_t qa[KT][2];
+  const uint16_t* qrow = p.q + (long long)b * p.ld_q + (long long)(kvh * G + (r < G ? r : 0)) * HD;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    if (lane == 0) stat[1][g] = 1.f / l;
+  for (int kt = 0; kt < KT; ++kt) {
+    qa[kt][0] = r < G ? *reinterpret_cast<const uint32_t*>(qrow + kt * 16 + 2 * qd) : 0u;
+    qa[kt][1] = r < G ? *reinterpret_cast<const uint32_t*>(qrow + kt * 16 + 8 + 2 * qd) : 0u;
+  }
+  float mw = -INFINITY, lw = 0.f;  // this warp's running max and sum for head r
+  float o[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+  const int wp0 = warp * 16;
+  for (int c = 0; c < nst; ++c) {
+    if (c + 1 < nst) asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+    else asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    __syncthreads();  // stage c landed for every thread's copies
+    const uint32_t ks = sm_s + (uint32_t)((c & 1) * BUF), vs = ks + (uint32_t)(kStage * RB);
+    float s[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+      const int row = wp0 + nt * 8 + (lane & 7);
+#pragma unroll
+      for (int kt = 0; kt < KT; kt += 2) {
+        uint32_t m[4];
+        const int j = 2 * kt + (lane >> 3);
+        ldsm_x4(ks + row * RB + ((j ^ (row & 7)) << 4), m);
+        mma16816(s[nt], qa[kt][0], qa[kt][1], m[0], m[1]);
+        mma16816(s[nt], qa[kt + 1][0], qa[kt + 1][1], m[2], m[3]);
+      }
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int t = c * kStage + wp0 + nt * 8 + 2 * qd + e;
+        s[nt][e] = t < len ? s[nt][e] * p.qscale : -INFINITY;
+        mx = fmaxf(mx, s[nt][e]);
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float mn = fmaxf(mw, mx);
+    const bool none = mn == -INFINITY;  // nothing valid seen by this warp yet
+    const float alpha = none ? 1.f : exp2f(mw - mn);
+    float ls = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        s[nt][e] = none ? 0.f : exp2f(s[nt][e] - mn);  // masked positions: exp2(-inf) = 0
+        ls += s[nt][e];
+      }
+    ls += __shfl_xor_sync(0xffffffffu, ls, 1);
+    ls += __shfl_xor_sync(0xffffffffu, ls, 2);
+    lw = fmaf(lw, alpha, ls);
+    mw = mn;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      o[nt][0] *= alpha;
+      o[nt][1] *= alpha;
+    }
+    // P.V: the warp's 16 positions are one k-tile; P re-packed as bf16 A fragments
+    const uint32_t a0 = pack_bf16x2(s[0][0], s[0][1]);
+    const uint32_t a2 = pack_bf16x2(s[1][0], s[1][1]);
+    const int row = wp0 + ((lane >> 3) & 1) * 8 + (lane & 7);
+#pragma unroll
+    for (int np = 0; np < NT / 2; ++np) {
+      uint32_t m[4];
+      const int j = 2 * np + (lane >> 4);
+      ldsm_x4_t(vs + row * RB + ((j ^ (row & 7)) << 4), m);
+      mma16816(o[2 * np], a0, a2, m[0], m[1]);
+      mma16816(o[2 * np + 1], a0, a2, m[2], m[3]);
+    }
+    __syncthreads();  // every warp is done with buffer c & 1
+    if (c + 2 < nst) issue(c + 2);
+  }
+  // combine the warps: M = max of their maxima, each scaled by exp2(m_w - M)
+  if (qd == 0 && r < G) {
+    wst[warp][r][0] = mw;
+    wst[warp][r][1] = lw;
   }
   __syncthreads();
-  const float4* src = reinterpret_cast<const float4*>(p.part + (long long)bh * ns * G * HD);
-  uint16_t* orow = p.out + (long long)b * p.ld_out + (long long)kvh * G * HD;
+  if (tid < G) {
+    float M = wst[0][tid][0];
+#pragma unroll
+    for (int w = 1; w < NW; ++w) M = fmaxf(M, wst[w][tid][0]);
+    float L = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w)
+      if (wst[w][tid][0] != -INFINITY) L = fmaf(exp2f(wst[w][tid][0] - M), wst[w][tid][1], L);
+    stat[0][tid] = M;
+    stat[1][tid] = L;
+  }
+  __syncthreads();
+  float* po = reinterpret_cast<float*>(sm);  // [NW][G][HD]: the stage buffers are free now
+  if (r < G) {
+    const float wsc = mw == -INFINITY ? 0.f : exp2f(mw - stat[0][r]);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+      *reinterpret_cast<float2*>(po + (warp * G + r) * HD + nt * 8 + 2 * qd) = make_float2(o[nt][0] * wsc, o[nt][1] * wsc);
+  }
+  __syncthreads();
+  const long long slot = (long long)bh * p.nsplit + split;
+  float4* dst = reinterpret_cast<float4*>(p.part + slot * G * HD);
   for (int i = tid; i < G * HD / 4; i += kThreads) {
-    const int g = i / (HD / 4);
-    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-    for (int s2 = 0; s2 < ns; ++s2) {
-      const float w = wgt[s2 * G + g];
-      const float4 c = __ldcg(src + (long long)s2 * (G * HD / 4) + i);
-      a.x = fmaf(w, c.x, a.x); a.y = fmaf(w, c.y, a.y); a.z = fmaf(w, c.z, a.z); a.w = fmaf(w, c.w, a.w);
+    float4 acc = reinterpret_cast<const float4*>(po)[i];
+#pragma unroll
+    for (int w = 1; w < NW; ++w) {
+      const float4 cc = reinterpret_cast<const float4*>(po + w * G * HD)[i];
+      acc.x += cc.x; acc.y += cc.y; acc.z += cc.z; acc.w += cc.w;
     }
-    const float inv = stat[1][g];
-    const uint32_t lo = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(a.x * inv)) |
-                        ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(a.y * inv)) << 16);
-    const uint32_t hi = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(a.z * inv)) |
-                        ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(a.w * inv)) << 16);
-    *reinterpret_cast<uint2*>(orow + i * 4) = make_uint2(lo, hi);
+    dst[i] = acc;
   }
+  if (tid < G) p.stats[slot * G + tid] = make_float2(stat[0][tid], stat[1][tid]);
+  // the last split of this (b, kv head) to finish merges
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned prev = atomicAdd(p.counter + bh, 1u);
+    last = prev == (unsigned)(p.nsplit - 1);
+    if (last) p.counter[bh] = 0u;  // ready for the next call
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  merge_splits<HD, G>(p, bh, b, kvh, po + NW * G * HD);
 }
 
 // Split count before rounding the chunk to a multiple of 4: the fewest splits
@@ -300,6 +496,20 @@ long long split_bound(long long B, int hkv, long long n) {
 
 void plan(long long B, int hkv, long long n, int* nsplit, int* chunk) {
   long long s = split_bound(B, hkv, n);
+  // Many (sequence, kv head) pairs: fewer, longer splits that stream through
+  // two stage buffers, about 2.6 CTAs per SM, and past one wave of 3 CTAs per
+  // SM not just above a wave boundary.  Measured on B200 (us, this split count
+  // against the fewest 128-position splits): 8B heads at 2048 positions, batch
+  // 4 / 8 / 32: 11.1 / 15.9 / 51.3 against 11.7 / 16.4 / 56.5; 70B heads at
+  // 4096 positions, batch 16 / 64: 49.9 / 181 against 68.1 / 235.
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long bh = B * hkv, want = (long long)sms * 13 / 5, slots = 3LL * sms;
+  if (bh * s > want) {
+    const long long s0 = s;
+    s = (want + bh - 1) / bh;
+    while (s < s0 && bh * s > slots && (bh * s) % slots < slots * 2 / 5) ++s;
+  }
   long long c = ((n + s - 1) / s + 3) & ~3LL;  // multiple of 4 keeps the shared-memory regions 16-byte aligned
   s = (n + c - 1) / c;
   *nsplit = (int)s;
@@ -339,7 +549,9 @@ constexpr size_t kMaxSmem = 227u * 1024u;  // opt-in dynamic shared memory per C
 
 template <int HD, int G>
 int launch(const AttnParams& p, long long B, void* stream) {
-  auto kern = decode_attn_kernel<HD, G>;
+  // splits of at most 128 positions: one CTA stages all of its K and V at
+  // once; longer splits stream through two stage buffers
+  auto kern = p.chunk <= kMaxChunk ? decode_attn_kernel<HD, G> : decode_attn_stream_kernel<HD, G>;
   const int smem = (int)smem_bytes(HD, G, p.nsplit);
   if (smem > 48 * 1024 && cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
     return WAL_ERR_CUDA;
@@ -437,9 +649,9 @@ int wal_decode_attention_ex(const uint16_t* q, int64_t ld_q, const uint16_t* k_c
   if ((uintptr_t)workspace & 255) return WAL_ERR_ALIGNMENT;
   const int G = hq / hkv;
   if (num_splits < 0) return WAL_ERR_INVALID_ARGUMENT;
-  if (num_splits > 0) {  // explicit split: at most kMaxChunk and at least 32 positions per split
+  if (num_splits > 0) {  // explicit split: at least 32 positions per split
     long long sp = num_splits;
-    if (sp < (n + kMaxChunk - 1) / kMaxChunk || sp > (n + 31) / 32) return WAL_ERR_SHAPE;
+    if (sp > (n + 31) / 32) return WAL_ERR_SHAPE;
     long long c = ((n + sp - 1) / sp + 3) & ~3LL;
     p.nsplit = (int)((n + c - 1) / c);
     p.chunk = (int)c;
