@@ -208,7 +208,14 @@ def check(status: int, where: str) -> None:
     raise WalValueError(status, where)
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_handle(device: torch.device | None = None) -> int:
+    """The cudaStream_t of torch's current stream on ``device`` (default: the current device)."""
+    if _raw_stream is not None:  # a fraction of a microsecond instead of ~3 us through the Stream object
+        idx = torch.cuda.current_device() if device is None or device.index is None else device.index
+        return int(_raw_stream(idx))
     return int(torch.cuda.current_stream(device).cuda_stream)
 
 

@@ -30,7 +30,9 @@
 #include "wal_rvq_decode.cuh"
 
 #include <cstdio>
+#include <mutex>
 #include <type_traits>
+#include <vector>
 
 namespace wal {
 
@@ -786,17 +788,75 @@ void assign_ctas(GemvParams& p, int ctas) {
   p.cta_start[G] = ctas;
 }
 
+// Launch facts looked up once instead of on every call: per device its SM
+// count; per (device, kernel) the shared-memory attributes, set again only
+// for a larger size; per (device, kernel, threads, shared memory) the
+// resident CTAs per SM.  These runtime queries took several microseconds per
+// call, as long as a small layer's decode GEMV runs on the GPU.
+struct KernelAttr {
+  int dev;
+  const void* fn;
+  int smem;
+};
+struct KernelOcc {
+  int dev;
+  const void* fn;
+  int threads, smem, per_sm;
+};
+constexpr int kMaxDevs = 64;
+std::mutex g_launch_mu;
+int g_sms[kMaxDevs];
+std::vector<KernelAttr> g_attr;
+std::vector<KernelOcc> g_occ;
+
+int sm_count(int dev, int* sms) {
+  if (dev < 0 || dev >= kMaxDevs) return WAL_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_launch_mu);
+  if (g_sms[dev] == 0 && cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    g_sms[dev] = 0;
+    return WAL_ERR_CUDA;
+  }
+  *sms = g_sms[dev];
+  return WAL_OK;
+}
+
+template <typename Kern>
+int launch_facts(Kern kern, int threads, int smem, int* sms, int* per_sm) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return WAL_ERR_CUDA;
+  int st = sm_count(dev, sms);
+  if (st != WAL_OK) return st;
+  const void* fn = reinterpret_cast<const void*>(kern);
+  std::lock_guard<std::mutex> lk(g_launch_mu);
+  KernelAttr* attr = nullptr;
+  for (auto& a : g_attr)
+    if (a.dev == dev && a.fn == fn) attr = &a;
+  if (!attr || attr->smem < smem) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return WAL_ERR_CUDA;
+    if (attr) {
+      attr->smem = smem;
+    } else {
+      cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+      g_attr.push_back({dev, fn, smem});
+    }
+  }
+  for (const auto& o : g_occ)
+    if (o.dev == dev && o.fn == fn && o.threads == threads && o.smem == smem) {
+      *per_sm = o.per_sm;
+      return WAL_OK;
+    }
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, kern, threads, smem) != cudaSuccess) return WAL_ERR_CUDA;
+  g_occ.push_back({dev, fn, threads, smem, *per_sm});
+  return WAL_OK;
+}
+
 template <typename Kern>
 int persistent_grid(Kern kern, int threads, int smem, int num_ctas, GemvParams& p, int* grid_out,
                     int* capacity_out = nullptr, bool pair_tiles = false) {
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-    return WAL_ERR_CUDA;
-  cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
-  int dev = 0, sms = 0, per_sm = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return WAL_ERR_CUDA;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return WAL_ERR_CUDA;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess)
-    return WAL_ERR_CUDA;
+  int sms = 0, per_sm = 0;
+  const int st = launch_facts(kern, threads, smem, &sms, &per_sm);
+  if (st != WAL_OK) return st;
   if (per_sm < 1) return WAL_ERR_UNSUPPORTED;
   const long long capacity = (long long)sms * per_sm;
   long long grid = num_ctas > 0 ? num_ctas : capacity;
@@ -1103,8 +1163,7 @@ static int gemv_common(const wal_rvq_layer* layer, const void* xv, int x_dtype, 
   p.auto_tpc = 0;
   if (wpt == 0) {
     int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaGetDevice(&dev) != cudaSuccess || sm_count(dev, &sms) != WAL_OK) return WAL_ERR_CUDA;
     const long long grid = layer->num_tiles < sms ? layer->num_tiles : sms;
     const long long tpc = (layer->num_tiles + grid - 1) / grid;  // tiles per CTA (max)
     wpt = best_wpt(tpc, p.chunks, 16, M <= 8);

@@ -478,11 +478,18 @@ class PackedGroupedBlockRVQLinear(nn.Module):
                                                 y.stride(0), _abi.DTYPE_CODE[y.dtype], _abi.stream_handle(x2.device))
             _abi.check(st, "wal_rvq_gemv_corrected")
             return
-        with torch.cuda.device(x2.device):
-            st = lib.wal_rvq_gemv_typed(ctypes.byref(layer), x2.data_ptr(), _abi.DTYPE_CODE[x2.dtype], x2.shape[0],
-                                        x2.stride(0), y.data_ptr(), y.stride(0), _abi.DTYPE_CODE[y.dtype],
-                                        warps_per_tile, num_ctas, _abi.stream_handle(x2.device))
-        _abi.check(st, "wal_rvq_gemv")
+        # decode-sized calls are short (a few us on the GPU), so the host path
+        # avoids a device switch when the input's device is already current
+        dev = x2.device
+        args = (ctypes.byref(layer), x2.data_ptr(), _abi.DTYPE_CODE[x2.dtype], x2.shape[0], x2.stride(0),
+                y.data_ptr(), y.stride(0), _abi.DTYPE_CODE[y.dtype], warps_per_tile, num_ctas)
+        if dev.index == torch.cuda.current_device():
+            st = lib.wal_rvq_gemv_typed(*args, _abi.stream_handle(dev))
+        else:
+            with torch.cuda.device(dev):
+                st = lib.wal_rvq_gemv_typed(*args, _abi.stream_handle(dev))
+        if st:
+            _abi.check(st, "wal_rvq_gemv")
 
     def reconstruct_weight(self, out_dtype: torch.dtype = torch.bfloat16) -> Tensor:
         """The weight in ``out_dtype`` (bf16, fp16 or fp32), bit-identical to the reference's
