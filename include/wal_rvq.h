@@ -167,14 +167,16 @@ WAL_API int wal_rvq_gemv_typed(const wal_rvq_layer* layer, const void* x, int x_
 
 /*
  * Prefill GEMM (large M): y[M, N] = x[M, K] @ w^T (+ bias) on the tcgen05
- * tensor cores.  Weight tiles are decoded exactly (same arithmetic as the
- * GEMV) into shared memory per 64-column stage; x tiles arrive by TMA.
+ * tensor cores, two SMs per tile (a cluster of 2 CTAs issuing cta_group::2
+ * MMAs).  Weight tiles are decoded exactly (same arithmetic as the GEMV) into
+ * shared memory per 64-column stage; x tiles arrive by TMA (no multicast).
  * Supports d = 8, R in {1, 2}, <= 256 entries; row groups must start at a
  * multiple of 128 rows.  x: bf16, ldx % 8 == 0, 16-byte aligned base.
  * y_dtype: WAL_BF16 or WAL_F32.  status: optional device int, set to 1 if a
  * pipeline wait timed out (the CTA then stops and frees its resources), NULL
  * to skip.  Returns WAL_ERR_UNSUPPORTED for other configurations (callers use
- * wal_rvq_gemv).  Replaces reference src/runtime.py:1501-1507 for M >= 256.
+ * wal_rvq_gemv).  Replaces reference src/runtime.py:1501-1507 for large M (the
+ * module uses it from 128 tokens).
  */
 WAL_API int wal_rvq_gemm(const wal_rvq_layer* layer, const uint16_t* x, int64_t M, int64_t ldx,
                  void* y, int64_t ldy, int y_dtype, int* status, void* stream);
