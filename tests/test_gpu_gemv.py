@@ -246,6 +246,35 @@ def test_prefill_falls_back_for_uncovered_formats():
     assert_close(mod(x).float().cpu().numpy(), ref, tol=8e-3)
 
 
+@pytest.mark.parametrize("dtype,cols", [(torch.float32, 1004), (torch.bfloat16, 1004), (torch.bfloat16, 1008),
+                                        (torch.float16, 1016)],
+                         ids=["f32-vector", "bf16-scalar-stride", "bf16-ragged-piece", "f16-ragged-piece"])
+def test_prefill_gemm_output_layouts(dtype, cols):
+    # 1004 output rows into y rows of `cols` elements: 16-byte stores of whole
+    # pieces when y and its stride allow them (the last piece of a row only
+    # partly inside the layer), scalar stores when the stride is not a
+    # multiple of 16 bytes; the columns past the layer stay untouched
+    N, K, M = 1004, 256, 300
+    enc = single_group(synthetic.rvq_encoding(N, K, d=8, R=2, seed=11))
+    b = synthetic.bias_vector(N, seed=5)
+    mod = PackedGroupedBlockRVQLinear(enc, b).cuda()
+    x = synthetic.activations(M, K, seed=9)
+    ref = orc.forward_f32(bits_of(x), orc.groups_from_encoding(enc), K, bits_of(b))
+    full = torch.full((M, cols), 7.0, device="cuda", dtype=dtype)
+    y = full[:, :N]
+    status = torch.zeros(1, device="cuda", dtype=torch.int32)
+    assert mod.gemm_into(x.cuda(), y, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    if dtype == torch.float32:
+        assert_close(y.cpu().numpy(), ref)
+    elif dtype == torch.bfloat16:
+        assert_bf16_within_ulp(bits_of(y), orc.f32_to_bf16_bits(ref))
+    else:
+        assert_close(y.float().cpu().numpy(), ref, tol=2e-3)
+    assert bool((full[:, N:] == 7.0).all())
+
+
 def _sampled_groups(enc, rows: np.ndarray) -> list[dict]:
     """Oracle group dicts holding only the given (sorted, global) output rows of each group."""
     out = []

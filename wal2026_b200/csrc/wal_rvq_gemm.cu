@@ -63,6 +63,7 @@ struct GemmParams {
   int group_tile_start[65];
   int group_row_start[65];
   int tok;  // tokens per pair tile: 512, 384 or 256 (two accumulators of tok / 2)
+  int vec_out;  // y and its row stride allow 16-byte stores
 };
 
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -501,16 +502,64 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_pair_kernel(const __grid
     // epilogue: TMEM lane 32 * (warp % 4) + lane is output row n0 + that lane;
     // column a * 256 + c of accumulator a is token m0 + a * accn + c; the four
     // warps of a lane quarter split each accumulator's columns
-    const bool ok = !abort_flag && mbar_wait_cluster(acc_full, 0);
+    bool ok = !abort_flag && mbar_wait_cluster(acc_full, 0);
+    ok = __all_sync(0xffffffffu, ok);  // TMEM loads are warp-wide
     if (!ok) abort_flag = 1;
     tc_fence_after();
-    if (ok) {
-      const int quarter = warp & 3, share = (warp - 2) >> 2;
-      const int erow = quarter * 32 + lane;
-      const int en = n0 + erow;
-      const bool eok = en < g_row1;
-      const float bias = (eok && p.bias) ? __bfloat162float(__ushort_as_bfloat16(p.bias[en])) : 0.f;
-      const int cols = accn / 4;  // per warp and accumulator: 64, 48 or 32
+    const int quarter = warp & 3, share = (warp - 2) >> 2;
+    const int erow = quarter * 32 + lane;
+    const int en = n0 + erow;
+    const bool eok = en < g_row1;
+    const float bias = (eok && p.bias) ? __bfloat162float(__ushort_as_bfloat16(p.bias[en])) : 0.f;
+    const int cols = accn / 4;  // per warp and accumulator: 64, 48 or 32
+    if (p.vec_out) {
+      // The four warps of one column share (one per lane quarter, 128 rows)
+      // pass each 16-token block through shared memory (the stage ring is
+      // idle once the accumulators are complete) and store whole 16-byte
+      // pieces of the output rows: a warp store writes two tokens' 256 or 512
+      // contiguous bytes instead of 64 or 128 bytes of one token.  Two staging
+      // buffers per share, so one named barrier per block orders both the
+      // writes before the reads and the reads before the next reuse.
+      const int esz = p.y_dtype == WAL_F32 ? 4 : 2;
+      const int chunks = 8 * esz;  // 16-byte pieces per token row of 128 outputs
+      uint8_t* stage = gbase + (x_sm - base) + share * 16384;
+      for (int c = 0, b = 0; c < nacc * cols; c += 16, b ^= 1) {
+        const int a = c / cols, c0 = share * cols + (c - a * cols);  // accumulator, its column
+        uint32_t v[16];
+        if (ok) tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * kAccN + c0), v);
+        uint8_t* buf = stage + b * 8192;
+        if (esz == 4) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) reinterpret_cast<float*>(buf)[j * 128 + erow] = __uint_as_float(v[j]) + bias;
+        } else {
+          const bool fp16 = p.y_dtype == WAL_F16;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float f = __uint_as_float(v[j]) + bias;
+            reinterpret_cast<uint16_t*>(buf)[j * 128 + erow] =
+                fp16 ? __half_as_ushort(__float2half_rn(f)) : __bfloat16_as_ushort(__float2bfloat16_rn(f));
+          }
+        }
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + share) : "memory");
+        if (ok) {
+          const int t0 = m0 + a * accn + c0;  // token of row 0 of this block
+          for (int k = erow; k < 16 * chunks; k += 128) {
+            const int j = k / chunks, r0 = (k - j * chunks) * (16 / esz);
+            const int m = t0 + j;
+            if (m >= p.M) continue;
+            const uint4 w = *reinterpret_cast<const uint4*>(buf + (size_t)k * 16);
+            uint8_t* dst = static_cast<uint8_t*>(p.y) + ((long long)m * p.ldy + n0 + r0) * esz;
+            if (n0 + r0 + 16 / esz <= g_row1) {
+              *reinterpret_cast<uint4*>(dst) = w;
+            } else {  // the last rows of the layer
+              const uint8_t* src = reinterpret_cast<const uint8_t*>(&w);
+              for (int e = 0; e < 16 / esz && n0 + r0 + e < g_row1; ++e)
+                for (int q = 0; q < esz; ++q) dst[e * esz + q] = src[e * esz + q];
+            }
+          }
+        }
+      }
+    } else if (ok) {
       for (int c = 0; c < nacc * cols; c += 16) {
         const int a = c / cols, c0 = share * cols + (c - a * cols);  // accumulator, its column
         uint32_t v[16];
@@ -616,6 +665,10 @@ extern "C" int wal_rvq_gemm_typed(const wal_rvq_layer* layer, const void* x, int
   p.chunks = (int)((blocks + 15) / 16);
   p.entries = g.num_entries;
   p.y_dtype = y_dtype;
+  {
+    const long long esz = y_dtype == WAL_F32 ? 4 : 2;
+    p.vec_out = ((uintptr_t)y % 16 == 0 && (ldy * esz) % 16 == 0) ? 1 : 0;
+  }
   p.num_groups = g.num_groups;
   // group boundaries; a CTA's 128 weight rows must not straddle two groups
   long long t = 0, rows = 0;
