@@ -293,8 +293,10 @@ __device__ __forceinline__ void decode_stage_part(uint32_t bsm_row, int nsw, con
 //   warps 2-17  (both CTAs) decoders, as in the single-CTA kernel, arriving on
 //               their CTA's full_w[stage] (the peer's warp 1 forwards each
 //               completed stage to the leader's); then the epilogue: each thread
-//               owns one output row and stores its tokens (64- or 128-byte
-//               row segments per warp store).
+//               reads one output row's tokens from TMEM, the four warps of a
+//               column share pass 16-token blocks through the idle stage ring
+//               and store 16-byte pieces of the output rows (scalar stores
+//               when y or its stride is not 16-byte aligned).
 namespace pair {
 constexpr int kRows = 128;                  // weight rows per CTA
 constexpr int kAccN = 256;                  // TMEM columns per accumulator (MMA N at most)
