@@ -369,22 +369,6 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_pair_kernel(const __grid
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
-  // codebooks of this CTA's group, 8 copies per entry; lanes write the copies
-  // of one entry side by side (whole 128-byte rows, no bank conflicts)
-  {
-    const uint16_t* books = p.codebooks + (size_t)g * R * p.entries * 8;
-    const float* scales = p.stage_scales ? p.stage_scales + (size_t)g * R : nullptr;
-    for (int i = threadIdx.x; i < R * p.entries * kCbCopies; i += kThreads) {
-      const int c = i % kCbCopies, se = i / kCbCopies;
-      const int st = se / p.entries, e = se - st * p.entries;
-      uint4 v = *reinterpret_cast<const uint4*>(books + (size_t)se * 8);
-      v.x = staged_word<R, NM, F16>(v.x, scales, st);
-      v.y = staged_word<R, NM, F16>(v.y, scales, st);
-      v.z = staged_word<R, NM, F16>(v.z, scales, st);
-      v.w = staged_word<R, NM, F16>(v.w, scales, st);
-      *reinterpret_cast<uint4*>(cb + ((st * 256 + e) * kCbCopies + c) * 16) = v;
-    }
-  }
   tc_fence_before();
   __syncthreads();
   cluster_sync();  // both CTAs' barriers and TMEM exist before any remote arrive or pair MMA
@@ -483,6 +467,38 @@ __global__ void __launch_bounds__(kThreads, 1) rvq_gemm_pair_kernel(const __grid
     uint32_t idq[kIdAhead + 1][R];
 #pragma unroll
     for (int j = 0; j < kIdAhead; ++j) load_ids(j, idq[j]);
+    // codebooks of this CTA's group, 8 copies per entry, staged by the decoder
+    // warps while the first activation boxes are in flight (the producer
+    // starts right after the cluster barrier); every load of a thread goes
+    // out before its first store (one L2 round trip, not one per entry), and
+    // lanes write the copies of one entry side by side (whole 128-byte rows,
+    // no bank conflicts)
+    {
+      const uint16_t* books = p.codebooks + (size_t)g * R * p.entries * 8;
+      const float* scales = p.stage_scales ? p.stage_scales + (size_t)g * R : nullptr;
+      constexpr int kItems = R * 256 * kCbCopies / (kDecodeWarps * 32);
+      const int total = R * p.entries * kCbCopies;
+      uint4 v[kItems];
+#pragma unroll
+      for (int q = 0; q < kItems; ++q) {
+        const int i = t + q * kDecodeWarps * 32;
+        if (i < total) v[q] = *reinterpret_cast<const uint4*>(books + (size_t)(i / kCbCopies) * 8);
+      }
+#pragma unroll
+      for (int q = 0; q < kItems; ++q) {
+        const int i = t + q * kDecodeWarps * 32;
+        if (i >= total) break;
+        const int c = i % kCbCopies, se = i / kCbCopies;
+        const int st = se / p.entries, e = se - st * p.entries;
+        v[q].x = staged_word<R, NM, F16>(v[q].x, scales, st);
+        v[q].y = staged_word<R, NM, F16>(v[q].y, scales, st);
+        v[q].z = staged_word<R, NM, F16>(v[q].z, scales, st);
+        v[q].w = staged_word<R, NM, F16>(v[q].w, scales, st);
+        *reinterpret_cast<uint4*>(cb + ((st * 256 + e) * kCbCopies + c) * 16) = v[q];
+      }
+      // the decoder warps only (no bounded wait precedes it, so all arrive)
+      asm volatile("bar.sync 5, %0;" ::"r"(kDecodeWarps * 32) : "memory");
+    }
     for (int kb = 0; kb < kblocks; ++kb) {
       const int s = kb % S;
       load_ids(kb + kIdAhead, idq[kIdAhead]);
