@@ -172,7 +172,10 @@ WAL_API int wal_rvq_gemv_typed(const wal_rvq_layer* layer, const void* x, int x_
  * shared memory per 64-column stage; x tiles arrive by TMA (no multicast).
  * Supports d = 8, R in {1, 2}, <= 256 entries; row groups must start at a
  * multiple of 128 rows.  x: bf16, ldx % 8 == 0, 16-byte aligned base.
- * y_dtype: WAL_BF16 or WAL_F32.  status: optional device int, set to 1 if a
+ * y_dtype: WAL_BF16 or WAL_F32; y takes 16-byte stores of whole output
+ * pieces when its base and its row stride (ldy elements) are multiples of 16
+ * bytes, scalar stores otherwise (any ldy >= N works; the elements of a row
+ * past N are not written).  status: optional device int, set to 1 if a
  * pipeline wait timed out (the CTA then stops and frees its resources), NULL
  * to skip.  Returns WAL_ERR_UNSUPPORTED for other configurations (callers use
  * wal_rvq_gemv).  Replaces reference src/runtime.py:1501-1507 for large M (the
